@@ -1,0 +1,404 @@
+#!/usr/bin/env python
+"""Benchmark of the int4 MatMulNBits path on B200 (one JSON line on rank 0).
+
+Workload ("decode GEMV sweep"): M in {1, 2, 4, 8} tokens x the four fused
+projection shapes (K, N) = qkvz|ab (2048, 8224), attn qkv (2048, 3072), gate|up (2048, 12288),
+down (6144, 2048). One step = the 16 matmuls of the sweep. Weights are synthetic with the
+configs' distribution (seeded), replicated on every GPU (data-parallel, no collective: each rank
+runs the same per-GPU work, weak scaling). Each call uses the next of 8 distinct device copies of
+its weight, 272 MB in total, so weights stream from HBM, not from the 126 MB L2.
+
+Metric: algorithmic bytes / second, bytes = N*K/2 (int4) + N*K/16 (fp16 scales) + 2*M*K + 2*M*N
+(the weight bytes of gemmbench/bench.js:53 plus activations in and out). ``value`` is the
+device-timed aggregate with inputs resident; ``e2e`` is the same sweep through the C ABI's
+host-buffer entry point (pinned host x -> device -> matmul -> pinned host y, every call).
+
+``--impl reference`` times the reference's CPU path (fp32 dequantise-then-matmul, the fake-quant
+route of convert/export_engine.py:88-103, restated in ``oracle/``) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "strands-decider-web_b200")
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+SHAPES = [("qkvz_ab", 2048, 8224), ("attn_qkv", 2048, 3072), ("gate_up", 2048, 12288), ("down", 6144, 2048)]
+MS = [1, 2, 4, 8]
+COPIES = 8
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def load_pkg():
+    name = "strands_decider_web_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def alg_bytes(M, K, N):
+    return N * K // 2 + N * K // 16 + 2 * M * K + 2 * M * N
+
+
+def sweep_bytes():
+    return sum(alg_bytes(M, K, N) for M in MS for _, K, N in SHAPES)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the GEMV kernel from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "gemv_decode_sweep.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 20 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.lines = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3:
+                time.sleep(0.01)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU side: the reference's fp32 path (oracle), used for cpu_baseline and --impl reference
+# ------------------------------------------------------------------------------------------------
+def cpu_setup():
+    import numpy as np
+    import torch
+    from oracle import s4ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    deqs, xs = {}, {}
+    for name, K, N in SHAPES:
+        packed, scales = s4ref.config_weights(rng, K, N)
+        deqs[name] = torch.from_numpy(s4ref.dequant(packed, scales))   # dequantised once (fake-quant)
+    for M in MS:
+        for name, K, N in SHAPES:
+            xs[(M, name)] = torch.from_numpy(s4ref.config_x(rng, M, K).astype(np.float32))
+    return deqs, xs
+
+
+def cpu_sweep_once(deqs, xs):
+    import torch
+    with torch.inference_mode():
+        for M in MS:
+            for name, K, N in SHAPES:
+                (xs[(M, name)] @ deqs[name].T).to(torch.float16)
+
+
+def cpu_time(deqs, xs, seconds: float):
+    cpu_sweep_once(deqs, xs)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_sweep_once(deqs, xs)
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            return n, dt
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    deqs, xs = cpu_setup()
+    for _ in range(args.warmup):
+        cpu_sweep_once(deqs, xs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_sweep_once(deqs, xs)
+    dt = time.perf_counter() - t0
+    gbs = sweep_bytes() * args.steps / dt / 1e9
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": "int4 GEMM GB/s (decode sweep M=1..8, algorithmic bytes)", "value": gbs,
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode_gemv_sweep_config2", "M": MS, "shapes_KN": [[K, N] for _, K, N in SHAPES]},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} full sweeps (16 matmuls each), torch fp32 on dequantised weights"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
+# GPU side
+# ------------------------------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from oracle import s4ref  # input generator only (same seeded synthetic data as the tests)
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    pkg = load_pkg()
+    ctx = pkg.Context(local_rank)
+    stream = torch.cuda.current_stream(dev)
+
+    rng = np.random.default_rng(0)
+    Ws = {}
+    for name, K, N in SHAPES:
+        packed, scales = s4ref.config_weights(rng, K, N)
+        Ws[name] = [ctx.upload(packed, scales, N, K) for _ in range(COPIES)]
+    xs, ys = {}, {}
+    for M in MS:
+        for name, K, N in SHAPES:
+            xs[(M, name)] = torch.from_numpy(s4ref.config_x(rng, M, K)).to(dev)
+            ys[(M, name)] = torch.empty((M, N), dtype=torch.float16, device=dev)
+    counter = [0]
+
+    def step():
+        for mi, M in enumerate(MS):
+            for name, K, N in SHAPES:
+                W = Ws[name][(counter[0] * len(MS) + mi) % COPIES]
+                ctx.matmul(xs[(M, name)], W, M, ys[(M, name)], stream)
+        counter[0] += 1
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ctx.launch_count
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    launches = ctx.launch_count - launches0
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    errs = ctx.check_errors()
+    if errs:
+        raise RuntimeError(f"device error word 0x{errs:x} after the timed region")
+    total_bytes = sweep_bytes() * args.steps * world
+    value = total_bytes / (ms / 1e3) / 1e9
+
+    # ---- e2e: the same sweep through the host-buffer C-ABI entry point ------------------------------
+    hx, hy = {}, {}
+    for M in MS:
+        for name, K, N in SHAPES:
+            hx[(M, name)] = xs[(M, name)].cpu().pin_memory()
+            hy[(M, name)] = torch.empty((M, N), dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        for mi, M in enumerate(MS):
+            for name, K, N in SHAPES:
+                W = Ws[name][(counter[0] * len(MS) + mi) % COPIES]
+                ctx.matmul_host_async(hx[(M, name)], W, hy[(M, name)], M, stream)
+        counter[0] += 1
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e3.record(stream)
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    e2e_value = total_bytes / (ms_e2e / 1e3) / 1e9
+    h2d = sum(2 * M * K for M in MS for _, K, _ in SHAPES)
+    d2h = sum(2 * M * N for M in MS for _, _, N in SHAPES)
+
+    # ---- parity spot check of the timed configuration (outside the timed region) ---------------------
+    rng2 = np.random.default_rng(0)
+    packed, scales = s4ref.config_weights(rng2, SHAPES[0][1], SHAPES[0][2])
+    ok_all = True
+    worst = 0.0
+    for M in MS:
+        y = ys[(M, SHAPES[0][0])]
+        ctx.matmul(xs[(M, SHAPES[0][0])], Ws[SHAPES[0][0]][0], M, y, stream)
+        torch.cuda.synchronize(dev)
+        _, ref = s4ref.matmul(xs[(M, SHAPES[0][0])].cpu().numpy(), packed, scales)
+        ok, mr, _ = s4ref.check(y.cpu().numpy(), ref)
+        ok_all &= ok
+        worst = max(worst, mr)
+
+    # ---- per-(shape, M) breakdown on this rank (device time, 8 rotating copies) -------------------------
+    per = {}
+    if rank == 0 and not args.quick:
+        for name, K, N in SHAPES:
+            for M in MS:
+                reps = 64
+                for r in range(8):
+                    ctx.matmul(xs[(M, name)], Ws[name][r % COPIES], M, ys[(M, name)], stream)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for r in range(reps):
+                    ctx.matmul(xs[(M, name)], Ws[name][r % COPIES], M, ys[(M, name)], stream)
+                b.record(stream)
+                torch.cuda.synchronize(dev)
+                us = a.elapsed_time(b) * 1e3 / reps
+                gbs = alg_bytes(M, K, N) / (us * 1e-6) / 1e9
+                per[f"{name}/M{M}"] = {"us": round(us, 3), "GBps": round(gbs, 1)}
+
+    # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------------------------------
+    hbm, bf16, peak_kind = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        deqs, cxs = cpu_setup()
+        n, dt = cpu_time(deqs, cxs, args.cpu_seconds)
+        cpu = {"value": sweep_bytes() * n / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"{n} full sweeps (16 matmuls each) in {dt:.1f} s, torch fp32 on weights dequantised once "
+                         f"(fake-quant route, export_engine.py:88-103)"}
+
+    if rank == 0:
+        per_launch_bytes = sweep_bytes() / len(MS) / len(SHAPES)
+        gemv_launches_per_step = len(MS) * len(SHAPES)
+        per_rank_ms = ms / args.steps
+        avg_launch_us = per_rank_ms * 1e3 / gemv_launches_per_step
+        achieved = per_launch_bytes / (avg_launch_us * 1e-6) / 1e9
+        line = {
+            "metric": "int4 GEMM GB/s (decode sweep M=1..8, algorithmic bytes)",
+            "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "decode_gemv_sweep_config2", "M": MS,
+                       "shapes_KN": [[K, N] for _, K, N in SHAPES], "weight_copies": COPIES,
+                       "l2": "inputs larger than L2: 8 rotating weight copies (272 MB) per step sequence",
+                       "parallelism": f"dp{world} (weights replicated, no collective)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": profile_traffic(), "peak_kind": peak_kind,
+                         "kernel": "gemv_streamk_kernel", "launch_us_avg": avg_launch_us},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "s4_matmul_host_async (pinned host x -> device -> matmul -> pinned host y)"},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+            "parity": {"ok": bool(ok_all), "max_rel": worst, "tol": s4ref.TOL_MAX_REL},
+            "per_call": per,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--quick", action="store_true", help="skip the per-call breakdown")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # timing rules: at least 3 untimed warm-up steps
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world == 1 and args.gpus > 1:
+        print(f"--gpus {args.gpus} needs torchrun with {args.gpus} processes", file=sys.stderr)
+        return 2
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

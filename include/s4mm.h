@@ -1,0 +1,131 @@
+/*
+ * s4mm — B200 (sm_100a) int4 MatMulNBits linear path, C ABI.
+ *
+ * Weight format (what the reference's engine uploads, convert/export_engine.py:3-4,17-26):
+ *   packed  uint8  [N][K/32][16]   element 2i of a 32-block in the low nibble of byte i,
+ *                                  element 2i+1 in the high nibble, value q means q-8;
+ *   scales  fp16   [N][K/32]       one per block, any sign.
+ * Matmul:  y[M][N] (fp16) = x[M][K] (fp16) @ ((q-8)*scale)^T, fp32 accumulation.
+ *
+ * Every call returns an int status (S4_OK == 0). On failure s4_last_error() gives a message
+ * for the calling thread. No call throws, none aborts the process.
+ *
+ * Threading: a context is bound to one device; it is thread-compatible, not thread-safe
+ * (one host thread drives it at a time), like the reference's single inference worker
+ * (web/public/js/worker.js:249-252). Work is asynchronous on the stream passed in unless a
+ * function says it is synchronous.
+ */
+#ifndef S4MM_H
+#define S4MM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define S4_API __attribute__((visibility("default")))
+#else
+#define S4_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define S4_OK 0
+#define S4_ERR_INVALID 1      /* bad argument: null pointer, size, alignment */
+#define S4_ERR_CUDA 2         /* a CUDA runtime call failed */
+#define S4_ERR_NOMEM 3        /* device or pinned memory allocation failed */
+#define S4_ERR_DEVICE 4       /* a kernel reported an error (bounded wait expired) */
+#define S4_ERR_UNSUPPORTED 5  /* no sm_100 device, or shape outside what a kernel handles */
+
+/* Kernel families of the dispatcher (s4_force / s4_plan). */
+#define S4_FAMILY_AUTO 0
+#define S4_FAMILY_GEMV 1      /* decode GEMV, M <= 32: stream-K over the weight bytes */
+#define S4_FAMILY_TC 2        /* tcgen05 GEMM, weights dequantised to fp16 in shared memory */
+
+typedef struct s4_ctx s4_ctx;
+typedef struct s4_weight s4_weight;
+
+/* Library version, (major << 16) | minor. */
+S4_API int s4_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+S4_API const char* s4_last_error(void);
+
+/* Open a context on CUDA device `device`. Replaces the device side of Engine.create
+ * (web/public/engine/engine.js:63-87): the context owns the split-K scratch the reference
+ * allocates per activation pool (engine.js:190-199) and the dispatch table. */
+S4_API int s4_init(int device, s4_ctx** out);
+S4_API int s4_destroy(s4_ctx* ctx);
+
+/* Upload one fused projection's int4 weight from HOST memory and repack it on the device into
+ * the B200 tiled layout. Synchronous: the weight is usable on any stream when it returns.
+ * Replaces the Gemm constructor's upload (web/public/gemmbench/kernels.js:84-87) and the
+ * engine's shard writes (engine.js:76-84). N >= 1 (any N; padded internally), K % 32 == 0.
+ * flags: 0 (reserved). */
+S4_API int s4_weight_upload(s4_ctx* ctx, const uint8_t* packed, const uint16_t* scales, int N, int K,
+                     uint32_t flags, s4_weight** out);
+
+/* Same, from DEVICE pointers already holding the MatMulNBits bytes (a shard range resolved like
+ * the engine's w(name), engine.js:175-180). Synchronous. */
+S4_API int s4_weight_upload_device(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, int N,
+                            int K, uint32_t flags, s4_weight** out);
+
+S4_API int s4_weight_free(s4_weight* w);
+
+/* Shape and device footprint of an uploaded weight. */
+S4_API int s4_weight_info(const s4_weight* w, int* N, int* K, size_t* device_bytes);
+
+/* Copy the repacked device layout back to host buffers (diagnostics and round-trip tests).
+ * wq_bytes / ws_bytes must be at least what s4_weight_layout_bytes reports. Synchronous. */
+S4_API int s4_weight_layout_bytes(const s4_weight* w, size_t* wq_bytes, size_t* ws_bytes);
+S4_API int s4_weight_download_layout(const s4_weight* w, void* wq_host, size_t wq_bytes, void* ws_host,
+                              size_t ws_bytes);
+
+/* y[M][N] = x[M][K] @ W^T on DEVICE pointers, asynchronous on `stream` (a cudaStream_t, NULL =
+ * legacy default stream). x and y are fp16 row-major with row strides K and N, 16-byte aligned.
+ * Allocates nothing. Replaces plan().matmul(A, wname, Y) (engine.js:236-246) including the
+ * split-K REDUCE step (kernels.js:269-282, engine.js:244). M == 0 is a no-op. */
+S4_API int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, void* stream);
+
+/* The standalone Gemm object's setA + encode + readY on HOST buffers (kernels.js:90-103):
+ * copies x to the device, runs s4_matmul, copies y back. Synchronous. Uses context-owned
+ * staging buffers that grow on demand. */
+S4_API int s4_matmul_host(s4_ctx* ctx, const s4_weight* w, const uint16_t* x, int M, uint16_t* y);
+
+/* Asynchronous form of s4_matmul_host on `stream`: host->device copy of x, matmul, device->host
+ * copy of y, nothing waited for (the encode() + mapAsync half of Gemm, kernels.js:98-103).
+ * x and y should be pinned host memory; they must stay valid until the stream reaches this
+ * work. Calls on one context share its staging buffers, so keep them on one stream. */
+S4_API int s4_matmul_host_async(s4_ctx* ctx, const s4_weight* w, const uint16_t* x, int M, uint16_t* y,
+                                void* stream);
+
+/* mid[M][I] = silu(big[:, :I]) * big[:, I:2I], fp16 in/out, fp32 math, DEVICE pointers,
+ * asynchronous. Replaces SILU_MUL (web/public/engine/wgsl.js:81-90). */
+S4_API int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, void* stream);
+
+/* Dispatcher. s4_plan reports the (family, tile, split) s4_matmul will use for M on an
+ * (N, K) weight; replaces matmulKernel(M) (engine.js:17-33). s4_force pins a choice for every
+ * later call (family 0 = back to the table), like matmulKernel's `force` (engine.js:23);
+ * tile/split 0 mean "kernel default". s4_set_table loads a measured M-bucket table:
+ * JSON {"buckets": [{"max_m": int, "family": "gemv"|"tc", "tile": int, "split": int}, ...]}. */
+S4_API int s4_plan(s4_ctx* ctx, int M, int N, int K, int* family, int* tile, int* split);
+S4_API int s4_force(s4_ctx* ctx, int family, int tile, int split);
+S4_API int s4_set_table(s4_ctx* ctx, const char* json);
+
+/* Device-side error word written by kernels whose bounded waits expired; 0 = clean.
+ * Reading it synchronises the context's device. s4_clear_errors resets it and the split-K
+ * arrival counters. */
+S4_API int s4_check_errors(s4_ctx* ctx, uint32_t* flags);
+S4_API int s4_clear_errors(s4_ctx* ctx);
+
+/* Number of kernels this context has launched since s4_init (host-side count). */
+S4_API int s4_launch_count(s4_ctx* ctx, uint64_t* count);
+
+/* Number of SMs and the device ordinal of the context. */
+S4_API int s4_device_info(s4_ctx* ctx, int* device, int* sm_count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* S4MM_H */

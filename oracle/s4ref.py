@@ -1,0 +1,253 @@
+"""numpy restatement of the reference's int4 MatMulNBits path (TEST INFRASTRUCTURE ONLY).
+
+Every function cites the reference file:line it restates. Conventions of the format
+(convert/export_engine.py:3-4, web/public/gemmbench/kernels.js:1-3):
+
+* weights ``W[N, K]`` are quantised in blocks of 32 consecutive K values of one output row;
+* ``packed[N][K/32][16]`` bytes: element ``2i`` of a block in the low nibble of byte ``i``,
+  element ``2i+1`` in the high nibble; nibble value ``q`` means ``q - 8`` (zero point 8);
+* ``scales[N][K/32]`` fp16, one per block, any sign (``quant`` produces negative ones);
+* ``Y[M, N] = X[M, K] @ dequant(W).T`` computed in fp32 and rounded once to fp16.
+
+The product never imports this module; tests compare the CUDA path against it.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+BLOCK = 32
+
+
+# --------------------------------------------------------------------------------------------
+# quantiser / packer  (convert/export_engine.py:17-26)
+# --------------------------------------------------------------------------------------------
+def quant(W: np.ndarray):
+    """Symmetric round-to-nearest int4 quantiser, restating ``quant`` (export_engine.py:17-26).
+
+    Per block of 32: the element of largest magnitude (first one on ties, as torch.argmax) is
+    divided by -8 to give the scale (so that element maps to nibble 0); a zero scale becomes 1;
+    the scale is rounded to fp16 and that rounded value is used for ``q = clamp(round(w/s)+8)``
+    (round half to even, as torch.round). Returns ``(packed u8 [N,K/32,16], scales f16 [N,K/32],
+    deq f32 [N,K])``.
+    """
+    W = np.asarray(W, dtype=np.float32)
+    N, K = W.shape
+    assert K % BLOCK == 0
+    b = W.reshape(N, K // BLOCK, BLOCK)
+    idx = np.abs(b).argmax(-1)[..., None]                                   # :20
+    scale = np.take_along_axis(b, idx, -1) / np.float32(-8.0)               # :21
+    scale = np.where(scale == 0, np.float32(1.0), scale)                    # :22
+    scale = scale.astype(np.float16).astype(np.float32)                     # :22
+    q = np.clip(np.round(b / scale) + 8, 0, 15).astype(np.uint8)            # :23
+    packed = pack_nibbles(q)                                                # :24
+    deq = ((q.astype(np.float32) - 8) * scale).reshape(N, K)                # :25
+    return packed, scale[..., 0].astype(np.float16), deq
+
+
+def pack_nibbles(q: np.ndarray) -> np.ndarray:
+    """``q[N,B,32]`` nibble values -> ``packed[N,B,16]`` (export_engine.py:24, make_gemm.py:9)."""
+    q = np.asarray(q, dtype=np.uint8)
+    return np.ascontiguousarray(q[..., 0::2] | (q[..., 1::2] << 4)).astype(np.uint8)
+
+
+def unpack_nibbles(packed: np.ndarray) -> np.ndarray:
+    """Inverse of :func:`pack_nibbles`: element ``e`` of a block is nibble ``e % 2`` of byte
+    ``e // 2`` (kernels.js:2-3, ``decodeBlock`` kernels.js:23-38)."""
+    p = np.asarray(packed, dtype=np.uint8)
+    q = np.empty(p.shape[:-1] + (p.shape[-1] * 2,), dtype=np.uint8)
+    q[..., 0::2] = p & 15
+    q[..., 1::2] = p >> 4
+    return q
+
+
+def dequant(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """fp32 ``(q - 8) * scale`` (export_engine.py:25; the per-element formula of kernels.js:35
+    and of the CPU checks in gemmbench/bench.js:49 and portable.js:62)."""
+    q = unpack_nibbles(packed).astype(np.float32) - 8.0
+    s = np.asarray(scales).astype(np.float32)[..., None]
+    N, B, _ = q.shape
+    return (q * s).reshape(N, B * BLOCK)
+
+
+def matmul(x: np.ndarray, packed: np.ndarray, scales: np.ndarray, deq: np.ndarray | None = None):
+    """The reference CPU path: fp32 dequantise-then-matmul, one fp16 rounding at the end.
+
+    Restates the fake-quant fp32 route (export_engine.py:88-103: dequantised weights copied into
+    an fp32 model, so each projection is ``x.float() @ deq.T``) and the fp32 dot of the GEMM
+    benches (bench.js:49). Returns ``(y f16 [M,N], y32 f32 [M,N])``.
+    """
+    if deq is None:
+        deq = dequant(packed, scales)
+    y32 = np.asarray(x, dtype=np.float16).astype(np.float32) @ deq.T
+    return y32.astype(np.float16), y32
+
+
+def cpu_check_columns(x16: np.ndarray, packed: np.ndarray, scales: np.ndarray, cols, rows=None):
+    """Element-wise fp32 dot products on a few output columns, restating the spot check of
+    gemmbench/bench.js:47-52 (all rows, columns {0, 1, N/2, N-1}) and portable.js:59-66
+    (rows {0, M/2, M-1}). Returns a dict ``{(m, n): fp32 value}``."""
+    M = x16.shape[0]
+    rows = range(M) if rows is None else rows
+    xf = x16.astype(np.float32)
+    out = {}
+    for n in cols:
+        w = dequant(packed[n:n + 1], scales[n:n + 1])[0]
+        for m in rows:
+            out[(m, n)] = float(np.dot(xf[m].astype(np.float64), w.astype(np.float64)))
+    return out
+
+
+# --------------------------------------------------------------------------------------------
+# metrics  (chain.js:12, bench.js:50-51)
+# --------------------------------------------------------------------------------------------
+def max_rel(y, ref) -> float:
+    """max |y - ref| / max |ref| over all elements (chain.js:12, bench.js:50-51)."""
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    mag = np.abs(ref).max()
+    return float(np.abs(y - ref).max() / mag) if mag > 0 else float(np.abs(y - ref).max())
+
+
+def min_row_cosine(y, ref) -> float:
+    """Smallest per-row cosine similarity between ``y`` and ``ref`` (rows = tokens)."""
+    y = np.asarray(y, dtype=np.float64).reshape(ref.shape[0], -1)
+    r = np.asarray(ref, dtype=np.float64).reshape(ref.shape[0], -1)
+    num = (y * r).sum(1)
+    den = np.sqrt((y * y).sum(1) * (r * r).sum(1))
+    cos = np.where(den > 0, num / np.where(den > 0, den, 1), 1.0)
+    return float(cos.min())
+
+
+TOL_MAX_REL = 2e-3       # max relative error
+TOL_MIN_COSINE = 0.99999  # per-row cosine
+
+
+def check(y, ref, tol=TOL_MAX_REL, cos=TOL_MIN_COSINE):
+    """(ok, max_rel, min_row_cosine) under the north-star tolerance."""
+    mr = max_rel(y, ref)
+    mc = min_row_cosine(y, ref)
+    return (mr <= tol and mc >= cos), mr, mc
+
+
+# --------------------------------------------------------------------------------------------
+# synthetic inputs  (convert/make_gemm.py:4-10, convert/make_chain.py:22-29)
+# --------------------------------------------------------------------------------------------
+MAKE_GEMM_SHAPES = [(2048, 6144), (2048, 2048), (6144, 2048), (2048, 12288)]   # make_gemm.py:5
+
+
+def make_gemm_weights(rng, K: int, N: int):
+    """One shape of the GEMM bench generator (make_gemm.py:7-10): uniform nibbles, signed scales
+    N(0,1)*0.02 in fp16. Draw order matters: nibbles first, then scales."""
+    blocks = K // BLOCK
+    q = rng.integers(0, 16, size=(N, blocks, 32), dtype=np.uint8)
+    packed = pack_nibbles(q)
+    scales = (rng.standard_normal((N, blocks)) * 0.02).astype(np.float16)
+    return packed, scales
+
+
+def make_chain_weights(rng, K: int, N: int):
+    """One layer of the chain generator (make_chain.py:27-29): scales N(0,1)/(sqrt(K)*4.6)."""
+    q = rng.integers(0, 16, size=(N, K // BLOCK, 32), dtype=np.uint8)
+    packed = pack_nibbles(q)
+    scales = (rng.standard_normal((N, K // BLOCK)) * (1.0 / (np.sqrt(K) * 4.6))).astype(np.float16)
+    return packed, scales
+
+
+def config_weights(rng, K: int, N: int):
+    """Weights of the BASELINE configs: nibbles uniform (q-8 uniform in [-8,7]), fp16 scales
+    |N(0, 0.02)| / 7. Nibbles are drawn before scales, as in make_gemm.py:8-10."""
+    q = rng.integers(0, 16, size=(N, K // BLOCK, 32), dtype=np.uint8)
+    packed = pack_nibbles(q)
+    scales = (np.abs(rng.standard_normal((N, K // BLOCK)) * 0.02) / 7.0).astype(np.float16)
+    return packed, scales
+
+
+def config_x(rng, M: int, K: int):
+    """Activations of the BASELINE configs: fp16 N(0, 1)."""
+    return rng.standard_normal((M, K)).astype(np.float16)
+
+
+def sha256(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+# --------------------------------------------------------------------------------------------
+# SiLU * mul  (web/public/engine/wgsl.js:81-90)
+# --------------------------------------------------------------------------------------------
+def silu_mul(big: np.ndarray, I: int) -> np.ndarray:
+    """``mid[t, j] = silu(g) * u`` with ``big[t] = [g (I) | u (I)]``; f32 math, f16 out
+    (wgsl.js:81-90)."""
+    b = np.asarray(big, dtype=np.float16).astype(np.float32)
+    g, u = b[:, :I], b[:, I:2 * I]
+    return (g / (1.0 + np.exp(-g)) * u).astype(np.float16)
+
+
+# --------------------------------------------------------------------------------------------
+# device layout (the layout the upload kernel writes; checked bit-exactly against the GPU)
+# --------------------------------------------------------------------------------------------
+NB_ROWS = 128   # output rows (N) per n-block
+KT_COLS = 64    # K per k-tile (two quant blocks)
+
+
+def tiled_dims(N: int, K: int):
+    nblk = (N + NB_ROWS - 1) // NB_ROWS
+    kt = (K + KT_COLS - 1) // KT_COLS
+    return nblk, kt
+
+
+def _shuffle_word(w: np.ndarray) -> np.ndarray:
+    """MatMulNBits u32 (nibble i = k_i, i=0..7) -> device u32: k0,k2,k4,k6 in nibbles 0-3 and
+    k1,k3,k5,k7 in nibbles 4-7, so the magic-number fp16 conversion yields the pairs
+    (k0,k1), (k2,k3), (k4,k5), (k6,k7)."""
+    w = w.astype(np.uint32)
+    out = np.zeros_like(w)
+    for i in range(8):
+        nib = (w >> np.uint32(4 * i)) & np.uint32(15)
+        pos = (i // 2) if i % 2 == 0 else 4 + i // 2
+        out |= nib << np.uint32(4 * pos)
+    return out
+
+
+def repack_device(packed: np.ndarray, scales: np.ndarray, N: int, K: int):
+    """The B200 layout of one weight (what ``s4_weight_upload`` writes on the device).
+
+    ``wq`` u32 ``[NBLK][KT][8 sub][32 lanes][4 words]``: sub-tile ``sub`` holds rows
+    ``r0 = nb*128 + sub*16``; lane ``L = 4g + t`` word ``j = 2*blk + h`` holds the 8 values of row
+    ``r0 + g + 8h`` at ``k = kt*64 + blk*32 + 8t .. +8``, shuffled by :func:`_shuffle_word`.
+    ``ws`` f16 ``[NBLK][KT][8 sub][8 g][4]`` = scales of (row g, blk0), (row g+8, blk0),
+    (row g, blk1), (row g+8, blk1). Rows >= N and K >= K are padded with nibble 8 and scale 0.
+    """
+    nblk, kt = tiled_dims(N, K)
+    Np, Kp = nblk * NB_ROWS, kt * KT_COLS
+    B = K // BLOCK
+    q = np.full((Np, Kp // 2), 0x88, dtype=np.uint8)
+    q[:N, :K // 2] = packed.reshape(N, B * 16)
+    sc = np.zeros((Np, Kp // BLOCK), dtype=np.float16)
+    sc[:N, :B] = scales
+    words = q.view("<u4").reshape(Np, Kp // 8)           # word c of row r covers k 8c..8c+7
+    words = _shuffle_word(words)
+    # [nb, sub, h, g, kt, blk, t]
+    w7 = words.reshape(nblk, 8, 2, 8, kt, 2, 4)
+    wq = w7.transpose(0, 4, 1, 3, 6, 5, 2).reshape(nblk, kt, 8, 32, 4)   # lane = (g, t); word = (blk, h)
+    s6 = sc.reshape(nblk, 8, 2, 8, kt, 2)                 # [nb, sub, h, g, kt, blk]
+    ws = s6.transpose(0, 4, 1, 3, 5, 2).reshape(nblk, kt, 8, 8, 4)
+    return np.ascontiguousarray(wq.astype(np.uint32)), np.ascontiguousarray(ws)
+
+
+def unrepack_device(wq: np.ndarray, ws: np.ndarray, N: int, K: int):
+    """Inverse of :func:`repack_device` (used by the round-trip tests)."""
+    nblk, kt = tiled_dims(N, K)
+    Np, Kp = nblk * NB_ROWS, kt * KT_COLS
+    w7 = wq.reshape(nblk, kt, 8, 8, 4, 2, 2).transpose(0, 2, 6, 3, 1, 5, 4)  # -> nb, sub, h, g, kt, blk, t
+    words = w7.reshape(Np, Kp // 8).astype(np.uint32)
+    orig = np.zeros_like(words)
+    for i in range(8):
+        pos = (i // 2) if i % 2 == 0 else 4 + i // 2
+        orig |= ((words >> np.uint32(4 * pos)) & np.uint32(15)) << np.uint32(4 * i)
+    q = orig.astype("<u4").view(np.uint8).reshape(Np, Kp // 2)
+    packed = q[:N, :K // 2].reshape(N, K // BLOCK, 16)
+    s6 = ws.reshape(nblk, kt, 8, 8, 2, 2).transpose(0, 2, 5, 3, 1, 4)     # -> nb, sub, h, g, kt, blk
+    sc = s6.reshape(Np, Kp // BLOCK)[:N, :K // BLOCK]
+    return np.ascontiguousarray(packed), np.ascontiguousarray(sc)

@@ -1,0 +1,580 @@
+// C ABI of libs4mm.so: context, weight handles, dispatcher, launches. Declarations and the
+// reference interfaces each entry point replaces are in include/s4mm.h.
+#include <climits>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/s4mm.h"
+#include "common.cuh"
+
+namespace s4 {
+cudaError_t launch_repack(const uint8_t* packed, const __half* scales, uint32_t* wq, __half* ws, int N, int K,
+                          int nblk, int ktiles, int sm_count, cudaStream_t stream);
+cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
+                        uint32_t* tickets, uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0,
+                        int groups, int grid, cudaStream_t stream, bool pdl);
+size_t gemv_partials_bytes(int max_grid);
+cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
+bool tc_available();
+cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, uint32_t* err, int M,
+                           int N, int K, int nblk, int ktiles, int tile_n, int sm_count, cudaStream_t stream);
+}  // namespace s4
+
+namespace {
+
+constexpr int kMaxTickets = 1 << 16;  // n-blocks per weight: N <= 8,388,608
+constexpr int kGemvMaxM = 32;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(S4_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+struct Bucket {
+  int max_m;
+  int family;
+  int tile;
+  int split;
+};
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+struct s4_ctx {
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;  // used by the synchronous host-pointer calls
+  float* partials = nullptr;      // GEMV split-K partials
+  uint32_t* tickets = nullptr;    // GEMV n-block arrival counters (self-resetting)
+  uint32_t* err = nullptr;        // device error word
+  void* dx = nullptr;             // staging for s4_matmul_host
+  void* dy = nullptr;
+  size_t dx_cap = 0, dy_cap = 0;
+  std::vector<Bucket> table;
+  Bucket forced{0, S4_FAMILY_AUTO, 0, 0};
+  uint64_t launches = 0;
+  int gemv_grid = 0;  // CTAs of a GEMV launch (default: one per SM)
+};
+
+struct s4_weight {
+  s4_ctx* ctx = nullptr;
+  int N = 0, K = 0, nblk = 0, ktiles = 0;
+  uint8_t* wq = nullptr;
+  uint8_t* ws = nullptr;
+  size_t wq_bytes = 0, ws_bytes = 0;
+};
+
+namespace {
+
+std::vector<Bucket> default_table() {
+  // M-bucket table (replaces engine.js:17-33). GEMV up to 32 tokens; tcgen05 GEMM above when the
+  // kernel is built in, else repeated GEMV launches of 32 tokens.
+  std::vector<Bucket> t;
+  t.push_back({kGemvMaxM, S4_FAMILY_GEMV, 0, 0});
+  t.push_back({INT_MAX, s4::tc_available() ? S4_FAMILY_TC : S4_FAMILY_GEMV, 0, 0});
+  return t;
+}
+
+Bucket choose(const s4_ctx* ctx, int M) {
+  if (ctx->forced.family != S4_FAMILY_AUTO) return ctx->forced;
+  for (const Bucket& b : ctx->table)
+    if (M <= b.max_m) return b;
+  return ctx->table.empty() ? Bucket{INT_MAX, S4_FAMILY_GEMV, 0, 0} : ctx->table.back();
+}
+
+// ---- a minimal JSON reader for the dispatch table ---------------------------------------------------
+struct Json {
+  const char* p;
+  const char* end;
+  void ws() {
+    while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
+  }
+  bool lit(char c) {
+    ws();
+    if (p < end && *p == c) {
+      ++p;
+      return true;
+    }
+    return false;
+  }
+  bool str(std::string& out) {
+    ws();
+    if (p >= end || *p != '"') return false;
+    ++p;
+    out.clear();
+    while (p < end && *p != '"') {
+      if (*p == '\\' && p + 1 < end) ++p;
+      out.push_back(*p++);
+    }
+    if (p >= end) return false;
+    ++p;
+    return true;
+  }
+  bool num(long long& v) {
+    ws();
+    char* e = nullptr;
+    v = strtoll(p, &e, 10);
+    if (e == p) return false;
+    p = e;
+    return true;
+  }
+  bool skip_value() {
+    ws();
+    if (p >= end) return false;
+    if (*p == '"') {
+      std::string s;
+      return str(s);
+    }
+    if (*p == '{' || *p == '[') {
+      const char open = *p, close = (*p == '{') ? '}' : ']';
+      int depth = 0;
+      bool in_str = false;
+      for (; p < end; ++p) {
+        if (in_str) {
+          if (*p == '\\') ++p;
+          else if (*p == '"') in_str = false;
+          continue;
+        }
+        if (*p == '"') in_str = true;
+        else if (*p == open) ++depth;
+        else if (*p == close && --depth == 0) {
+          ++p;
+          return true;
+        }
+      }
+      return false;
+    }
+    while (p < end && *p != ',' && *p != '}' && *p != ']') ++p;
+    return true;
+  }
+};
+
+int parse_family(const std::string& s) {
+  if (s == "gemv") return S4_FAMILY_GEMV;
+  if (s == "tc") return S4_FAMILY_TC;
+  return -1;
+}
+
+bool parse_table(const char* text, std::vector<Bucket>& out, std::string& why) {
+  Json j{text, text + strlen(text)};
+  if (!j.lit('{')) return why = "expected '{'", false;
+  bool found = false;
+  while (true) {
+    std::string key;
+    if (j.lit('}')) break;
+    if (!j.str(key) || !j.lit(':')) return why = "expected a key", false;
+    if (key == "buckets") {
+      found = true;
+      if (!j.lit('[')) return why = "\"buckets\" must be an array", false;
+      while (!j.lit(']')) {
+        if (!j.lit('{')) return why = "bucket must be an object", false;
+        Bucket b{INT_MAX, -1, 0, 0};
+        while (!j.lit('}')) {
+          std::string k;
+          if (!j.str(k) || !j.lit(':')) return why = "bad bucket key", false;
+          if (k == "family") {
+            std::string f;
+            if (!j.str(f) || (b.family = parse_family(f)) < 0) return why = "family must be \"gemv\" or \"tc\"", false;
+          } else if (k == "max_m" || k == "tile" || k == "split") {
+            long long v;
+            if (!j.num(v) || v < 0 || v > INT_MAX) return why = "bad number in bucket", false;
+            (k == "max_m" ? b.max_m : k == "tile" ? b.tile : b.split) = (int)v;
+          } else if (!j.skip_value()) {
+            return why = "bad value", false;
+          }
+          j.lit(',');
+        }
+        if (b.family < 0) return why = "bucket without family", false;
+        if (b.family == S4_FAMILY_TC && !s4::tc_available()) return why = "tc family is not built", false;
+        if (!out.empty() && b.max_m <= out.back().max_m) return why = "max_m must increase", false;
+        out.push_back(b);
+        j.lit(',');
+      }
+    } else if (!j.skip_value()) {
+      return why = "bad value", false;
+    }
+    j.lit(',');
+  }
+  if (!found || out.empty()) return why = "no buckets", false;
+  out.back().max_m = INT_MAX;  // the last bucket covers every larger M
+  return true;
+}
+
+int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, int N, int K, s4_weight** out) {
+  s4_weight* w = new (std::nothrow) s4_weight();
+  if (!w) return fail(S4_ERR_NOMEM, "out of host memory");
+  w->ctx = ctx;
+  w->N = N;
+  w->K = K;
+  w->nblk = (N + s4::kRowsPerBlock - 1) / s4::kRowsPerBlock;
+  w->ktiles = (K + s4::kKPerTile - 1) / s4::kKPerTile;
+  w->wq_bytes = (size_t)w->nblk * w->ktiles * s4::kChunkWBytes;
+  w->ws_bytes = (size_t)w->nblk * w->ktiles * s4::kChunkSBytes;
+  cudaError_t e = cudaMalloc(&w->wq, w->wq_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&w->ws, w->ws_bytes);
+  if (e != cudaSuccess) {
+    cudaFree(w->wq);
+    delete w;
+    return fail(S4_ERR_NOMEM, "weight allocation of %zu bytes failed: %s", w->wq_bytes + w->ws_bytes,
+                cudaGetErrorString(e));
+  }
+  e = s4::launch_repack(static_cast<const uint8_t*>(packed_dev), static_cast<const __half*>(scales_dev),
+                        reinterpret_cast<uint32_t*>(w->wq), reinterpret_cast<__half*>(w->ws), N, K, w->nblk,
+                        w->ktiles, ctx->sm_count, ctx->stream);
+  if (e == cudaSuccess) {
+    ++ctx->launches;
+    e = cudaStreamSynchronize(ctx->stream);
+  }
+  if (e != cudaSuccess) {
+    cudaFree(w->wq);
+    cudaFree(w->ws);
+    delete w;
+    return cuda_fail(e, "repack");
+  }
+  *out = w;
+  return S4_OK;
+}
+
+int check_shape(int N, int K) {
+  if (N < 1) return fail(S4_ERR_INVALID, "N must be >= 1 (got %d)", N);
+  if (K < 32 || K % 32 != 0) return fail(S4_ERR_INVALID, "K must be a positive multiple of 32 (got %d)", K);
+  const long long nblk = (N + 127) / 128;
+  if (nblk > kMaxTickets) return fail(S4_ERR_INVALID, "N=%d exceeds the supported %d rows", N, kMaxTickets * 128);
+  return S4_OK;
+}
+
+int grow(void** buf, size_t* cap, size_t need) {
+  if (need <= *cap) return S4_OK;
+  cudaFree(*buf);
+  *buf = nullptr;
+  *cap = 0;
+  cudaError_t e = cudaMalloc(buf, need);
+  if (e != cudaSuccess) return fail(S4_ERR_NOMEM, "staging allocation of %zu bytes failed", need);
+  *cap = need;
+  return S4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int s4_version(void) { return (1 << 16) | 0; }
+
+const char* s4_last_error(void) { return g_last_error.c_str(); }
+
+int s4_init(int device, s4_ctx** out) {
+  if (!out) return fail(S4_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0)
+    return fail(S4_ERR_UNSUPPORTED, "no CUDA device: %s", e != cudaSuccess ? cudaGetErrorString(e) : "count is 0");
+  if (device < 0 || device >= count) return fail(S4_ERR_INVALID, "device %d out of range [0, %d)", device, count);
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return fail(S4_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device, prop.major,
+                prop.minor);
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(S4_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  s4_ctx* ctx = new (std::nothrow) s4_ctx();
+  if (!ctx) return fail(S4_ERR_NOMEM, "out of host memory");
+  ctx->device = device;
+  ctx->sm_count = prop.multiProcessorCount;
+  ctx->gemv_grid = prop.multiProcessorCount;
+  ctx->table = default_table();
+  e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->partials, s4::gemv_partials_bytes(ctx->gemv_grid));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->tickets, kMaxTickets * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->err, sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemsetAsync(ctx->tickets, 0, kMaxTickets * sizeof(uint32_t), ctx->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ctx->err, 0, sizeof(uint32_t), ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    int rc = cuda_fail(e, "context allocation");
+    s4_destroy(ctx);
+    return rc;
+  }
+  *out = ctx;
+  return S4_OK;
+}
+
+int s4_destroy(s4_ctx* ctx) {
+  if (!ctx) return S4_OK;
+  DeviceGuard guard(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  cudaFree(ctx->partials);
+  cudaFree(ctx->tickets);
+  cudaFree(ctx->err);
+  cudaFree(ctx->dx);
+  cudaFree(ctx->dy);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return S4_OK;
+}
+
+int s4_weight_upload(s4_ctx* ctx, const uint8_t* packed, const uint16_t* scales, int N, int K, uint32_t flags,
+                     s4_weight** out) {
+  if (!ctx || !packed || !scales || !out) return fail(S4_ERR_INVALID, "NULL argument");
+  if (flags != 0) return fail(S4_ERR_INVALID, "unknown flags 0x%x", flags);
+  int rc = check_shape(N, K);
+  if (rc) return rc;
+  DeviceGuard guard(ctx->device);
+  const size_t pbytes = (size_t)N * (K / 32) * 16, sbytes = (size_t)N * (K / 32) * 2;
+  void *dp = nullptr, *ds = nullptr;
+  cudaError_t e = cudaMalloc(&dp, pbytes);
+  if (e == cudaSuccess) e = cudaMalloc(&ds, sbytes);
+  if (e != cudaSuccess) {
+    cudaFree(dp);
+    return fail(S4_ERR_NOMEM, "upload staging of %zu bytes failed", pbytes + sbytes);
+  }
+  e = cudaMemcpyAsync(dp, packed, pbytes, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(ds, scales, sbytes, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(dp);
+    cudaFree(ds);
+    return cuda_fail(e, "upload copy");
+  }
+  rc = upload_common(ctx, dp, ds, N, K, out);
+  cudaFree(dp);
+  cudaFree(ds);
+  return rc;
+}
+
+int s4_weight_upload_device(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, int N, int K,
+                            uint32_t flags, s4_weight** out) {
+  if (!ctx || !packed_dev || !scales_dev || !out) return fail(S4_ERR_INVALID, "NULL argument");
+  if (flags != 0) return fail(S4_ERR_INVALID, "unknown flags 0x%x", flags);
+  if ((reinterpret_cast<uintptr_t>(packed_dev) & 3) || (reinterpret_cast<uintptr_t>(scales_dev) & 1))
+    return fail(S4_ERR_INVALID, "packed must be 4-byte and scales 2-byte aligned");
+  int rc = check_shape(N, K);
+  if (rc) return rc;
+  DeviceGuard guard(ctx->device);
+  return upload_common(ctx, packed_dev, scales_dev, N, K, out);
+}
+
+int s4_weight_free(s4_weight* w) {
+  if (!w) return S4_OK;
+  DeviceGuard guard(w->ctx->device);
+  cudaFree(w->wq);
+  cudaFree(w->ws);
+  delete w;
+  return S4_OK;
+}
+
+int s4_weight_info(const s4_weight* w, int* N, int* K, size_t* device_bytes) {
+  if (!w) return fail(S4_ERR_INVALID, "NULL weight");
+  if (N) *N = w->N;
+  if (K) *K = w->K;
+  if (device_bytes) *device_bytes = w->wq_bytes + w->ws_bytes;
+  return S4_OK;
+}
+
+int s4_weight_layout_bytes(const s4_weight* w, size_t* wq_bytes, size_t* ws_bytes) {
+  if (!w) return fail(S4_ERR_INVALID, "NULL weight");
+  if (wq_bytes) *wq_bytes = w->wq_bytes;
+  if (ws_bytes) *ws_bytes = w->ws_bytes;
+  return S4_OK;
+}
+
+int s4_weight_download_layout(const s4_weight* w, void* wq_host, size_t wq_bytes, void* ws_host, size_t ws_bytes) {
+  if (!w || !wq_host || !ws_host) return fail(S4_ERR_INVALID, "NULL argument");
+  if (wq_bytes < w->wq_bytes || ws_bytes < w->ws_bytes) return fail(S4_ERR_INVALID, "host buffers too small");
+  DeviceGuard guard(w->ctx->device);
+  cudaError_t e = cudaMemcpy(wq_host, w->wq, w->wq_bytes, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(ws_host, w->ws, w->ws_bytes, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "layout download");
+  return S4_OK;
+}
+
+int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, void* stream) {
+  if (!ctx || !w) return fail(S4_ERR_INVALID, "NULL context or weight");
+  if (w->ctx != ctx) return fail(S4_ERR_INVALID, "weight belongs to another context");
+  if (M < 0) return fail(S4_ERR_INVALID, "M must be >= 0 (got %d)", M);
+  if (M == 0) return S4_OK;
+  if (!x || !y) return fail(S4_ERR_INVALID, "NULL x or y");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+    return fail(S4_ERR_INVALID, "x and y must be 16-byte aligned");
+  DeviceGuard guard(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Bucket b = choose(ctx, M);
+  cudaError_t e = cudaSuccess;
+  if (b.family == S4_FAMILY_TC) {
+    e = s4::launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->err, M, w->N,
+                           w->K, w->nblk, w->ktiles, b.tile, ctx->sm_count, st);
+    if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
+    ++ctx->launches;
+    return S4_OK;
+  }
+  const int grid = b.split > 0 ? b.split : ctx->gemv_grid;
+  if (grid > ctx->gemv_grid) return fail(S4_ERR_INVALID, "GEMV split %d exceeds the scratch for %d CTAs", grid, ctx->gemv_grid);
+  for (int tok0 = 0; tok0 < M; tok0 += kGemvMaxM) {
+    const int rem = M - tok0;
+    const int groups = rem >= kGemvMaxM ? kGemvMaxM / 8 : (rem + 7) / 8;
+    e = s4::launch_gemv(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->partials,
+                        ctx->tickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tok0, groups, grid, st, true);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+    ++ctx->launches;
+  }
+  return S4_OK;
+}
+
+int s4_matmul_host(s4_ctx* ctx, const s4_weight* w, const uint16_t* x, int M, uint16_t* y) {
+  if (!ctx || !w) return fail(S4_ERR_INVALID, "NULL context or weight");
+  if (M < 0) return fail(S4_ERR_INVALID, "M must be >= 0 (got %d)", M);
+  if (M == 0) return S4_OK;
+  if (!x || !y) return fail(S4_ERR_INVALID, "NULL x or y");
+  DeviceGuard guard(ctx->device);
+  const size_t xb = (size_t)M * w->K * 2, yb = (size_t)M * w->N * 2;
+  if (xb > ctx->dx_cap || yb > ctx->dy_cap) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "staging resize");
+  }
+  int rc = grow(&ctx->dx, &ctx->dx_cap, xb);
+  if (!rc) rc = grow(&ctx->dy, &ctx->dy_cap, yb);
+  if (rc) return rc;
+  cudaError_t e = cudaMemcpyAsync(ctx->dx, x, xb, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "x upload");
+  rc = s4_matmul(ctx, w, ctx->dx, M, ctx->dy, ctx->stream);
+  if (rc) return rc;
+  e = cudaMemcpyAsync(y, ctx->dy, yb, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "y download");
+  return S4_OK;
+}
+
+int s4_matmul_host_async(s4_ctx* ctx, const s4_weight* w, const uint16_t* x, int M, uint16_t* y, void* stream) {
+  if (!ctx || !w) return fail(S4_ERR_INVALID, "NULL context or weight");
+  if (M < 0) return fail(S4_ERR_INVALID, "M must be >= 0 (got %d)", M);
+  if (M == 0) return S4_OK;
+  if (!x || !y) return fail(S4_ERR_INVALID, "NULL x or y");
+  DeviceGuard guard(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t xb = (size_t)M * w->K * 2, yb = (size_t)M * w->N * 2;
+  if (xb > ctx->dx_cap || yb > ctx->dy_cap) {
+    // growing frees the old staging buffers: wait for work that may still use them
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "staging resize");
+  }
+  int rc = grow(&ctx->dx, &ctx->dx_cap, xb);
+  if (!rc) rc = grow(&ctx->dy, &ctx->dy_cap, yb);
+  if (rc) return rc;
+  cudaError_t e = cudaMemcpyAsync(ctx->dx, x, xb, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "x upload");
+  rc = s4_matmul(ctx, w, ctx->dx, M, ctx->dy, stream);
+  if (rc) return rc;
+  e = cudaMemcpyAsync(y, ctx->dy, yb, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return cuda_fail(e, "y download");
+  return S4_OK;
+}
+
+int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, void* stream) {
+  if (!ctx) return fail(S4_ERR_INVALID, "NULL context");
+  if (M < 0 || I < 1) return fail(S4_ERR_INVALID, "bad shape M=%d I=%d", M, I);
+  if (M == 0) return S4_OK;
+  if (!big || !mid) return fail(S4_ERR_INVALID, "NULL big or mid");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = s4::launch_silu_mul(static_cast<const __half*>(big), static_cast<__half*>(mid), M, I, ctx->sm_count,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
+  ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_plan(s4_ctx* ctx, int M, int N, int K, int* family, int* tile, int* split) {
+  if (!ctx) return fail(S4_ERR_INVALID, "NULL context");
+  (void)N;
+  (void)K;
+  const Bucket b = choose(ctx, M < 1 ? 1 : M);
+  if (family) *family = b.family;
+  if (tile) *tile = b.tile;
+  if (split) *split = b.split > 0 ? b.split : (b.family == S4_FAMILY_GEMV ? ctx->gemv_grid : 0);
+  return S4_OK;
+}
+
+int s4_force(s4_ctx* ctx, int family, int tile, int split) {
+  if (!ctx) return fail(S4_ERR_INVALID, "NULL context");
+  if (family != S4_FAMILY_AUTO && family != S4_FAMILY_GEMV && family != S4_FAMILY_TC)
+    return fail(S4_ERR_INVALID, "unknown family %d", family);
+  if (family == S4_FAMILY_TC && !s4::tc_available()) return fail(S4_ERR_UNSUPPORTED, "tc family is not built");
+  if (tile < 0 || split < 0) return fail(S4_ERR_INVALID, "tile and split must be >= 0");
+  if (family == S4_FAMILY_GEMV && split > ctx->gemv_grid)
+    return fail(S4_ERR_INVALID, "GEMV split %d exceeds %d", split, ctx->gemv_grid);
+  ctx->forced = Bucket{INT_MAX, family, tile, split};
+  return S4_OK;
+}
+
+int s4_set_table(s4_ctx* ctx, const char* json) {
+  if (!ctx || !json) return fail(S4_ERR_INVALID, "NULL argument");
+  std::vector<Bucket> t;
+  std::string why;
+  if (!parse_table(json, t, why)) return fail(S4_ERR_INVALID, "dispatch table: %s", why.c_str());
+  for (const Bucket& b : t)
+    if (b.family == S4_FAMILY_GEMV && b.split > ctx->gemv_grid)
+      return fail(S4_ERR_INVALID, "GEMV split %d exceeds %d", b.split, ctx->gemv_grid);
+  ctx->table = t;
+  return S4_OK;
+}
+
+int s4_check_errors(s4_ctx* ctx, uint32_t* flags) {
+  if (!ctx || !flags) return fail(S4_ERR_INVALID, "NULL argument");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(flags, ctx->err, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "error word read");
+  return S4_OK;
+}
+
+int s4_clear_errors(s4_ctx* ctx) {
+  if (!ctx) return fail(S4_ERR_INVALID, "NULL context");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(ctx->tickets, 0, kMaxTickets * sizeof(uint32_t));
+  if (e != cudaSuccess) return cuda_fail(e, "error reset");
+  return S4_OK;
+}
+
+int s4_launch_count(s4_ctx* ctx, uint64_t* count) {
+  if (!ctx || !count) return fail(S4_ERR_INVALID, "NULL argument");
+  *count = ctx->launches;
+  return S4_OK;
+}
+
+int s4_device_info(s4_ctx* ctx, int* device, int* sm_count) {
+  if (!ctx) return fail(S4_ERR_INVALID, "NULL context");
+  if (device) *device = ctx->device;
+  if (sm_count) *sm_count = ctx->sm_count;
+  return S4_OK;
+}
+
+}  // extern "C"

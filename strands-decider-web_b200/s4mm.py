@@ -1,0 +1,294 @@
+"""Python host side of the int4 MatMulNBits path: ctypes bindings over ``libs4mm.so``.
+
+The classes mirror the reference's JavaScript call surface so that code written against it maps
+one to one:
+
+* :class:`Gemm` is the standalone ``Gemm`` object of web/public/gemmbench/kernels.js:83-104
+  (``constructor(device, {K, N, B, Sc})`` uploads, ``setA(M, A16)``, ``encode()``, ``readY()``).
+* :meth:`Context.matmul` is the engine's ``matmul(A, wname, Y)`` closure
+  (web/public/engine/engine.js:236-246) on device tensors, with the weight resolved beforehand
+  (:meth:`Context.upload`, the engine's shard upload + ``w(name)``, engine.js:63-87,175-180).
+* :meth:`Context.silu_mul` is the ``SILU_MUL`` step between gate|up and down (wgsl.js:81-90).
+
+Errors: every C call returns a status; a non-zero one raises :class:`S4Error` with
+``s4_last_error()``, as the reference throws ``Error`` (engine.js:177, 228). There is no CPU
+fallback: if the library or a B200 is missing, construction raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libs4mm.so")
+
+FAMILY_AUTO, FAMILY_GEMV, FAMILY_TC = 0, 1, 2
+FAMILY_NAMES = {FAMILY_AUTO: "auto", FAMILY_GEMV: "gemv", FAMILY_TC: "tc"}
+ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_DEVICE, ERR_UNSUPPORTED = 1, 2, 3, 4, 5
+
+# Every symbol include/s4mm.h declares, with its ctypes signature.
+_P = C.c_void_p
+_SIGS = {
+    "s4_version": (C.c_int, []),
+    "s4_last_error": (C.c_char_p, []),
+    "s4_init": (C.c_int, [C.c_int, C.POINTER(_P)]),
+    "s4_destroy": (C.c_int, [_P]),
+    "s4_weight_upload": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.c_uint32, C.POINTER(_P)]),
+    "s4_weight_upload_device": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.c_uint32, C.POINTER(_P)]),
+    "s4_weight_free": (C.c_int, [_P]),
+    "s4_weight_info": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_size_t)]),
+    "s4_weight_layout_bytes": (C.c_int, [_P, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+    "s4_weight_download_layout": (C.c_int, [_P, _P, C.c_size_t, _P, C.c_size_t]),
+    "s4_matmul": (C.c_int, [_P, _P, _P, C.c_int, _P, _P]),
+    "s4_matmul_host": (C.c_int, [_P, _P, _P, C.c_int, _P]),
+    "s4_matmul_host_async": (C.c_int, [_P, _P, _P, C.c_int, _P, _P]),
+    "s4_silu_mul": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
+    "s4_plan": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                          C.POINTER(C.c_int)]),
+    "s4_force": (C.c_int, [_P, C.c_int, C.c_int, C.c_int]),
+    "s4_set_table": (C.c_int, [_P, C.c_char_p]),
+    "s4_check_errors": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "s4_clear_errors": (C.c_int, [_P]),
+    "s4_launch_count": (C.c_int, [_P, C.POINTER(C.c_uint64)]),
+    "s4_device_info": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+}
+
+
+class S4Error(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"s4mm error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load_library(path: str = LIB_PATH):
+    """Load ``libs4mm.so`` and bind every declared entry point. Raises if it is missing."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise S4Error(ERR_UNSUPPORTED, f"{path} is not built (run __graft_entry__.build())")
+        lib = C.CDLL(path)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise S4Error(rc, _lib.s4_last_error().decode(errors="replace"))
+
+
+def _ptr(a) -> int:
+    """Device or host address of a torch tensor or numpy array."""
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    raise TypeError(f"expected a torch tensor or numpy array, got {type(a)}")
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        try:
+            import torch
+            return torch.cuda.current_stream().cuda_stream
+        except Exception:
+            return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+class Weight:
+    """An uploaded, device-repacked int4 weight (the engine's resolved ``.q``/``.s`` pair)."""
+
+    def __init__(self, ctx: "Context", handle: int, N: int, K: int):
+        self.ctx, self.handle, self.N, self.K = ctx, handle, N, K
+
+    @property
+    def device_bytes(self) -> int:
+        n, k, b = C.c_int(), C.c_int(), C.c_size_t()
+        _check(_lib.s4_weight_info(self.handle, C.byref(n), C.byref(k), C.byref(b)))
+        return b.value
+
+    def layout(self):
+        """Download the device layout: ``(wq uint32, ws float16)`` flat arrays."""
+        qb, sb = C.c_size_t(), C.c_size_t()
+        _check(_lib.s4_weight_layout_bytes(self.handle, C.byref(qb), C.byref(sb)))
+        wq = np.empty(qb.value // 4, np.uint32)
+        ws = np.empty(sb.value // 2, np.float16)
+        _check(_lib.s4_weight_download_layout(self.handle, wq.ctypes.data, qb.value, ws.ctypes.data, sb.value))
+        return wq, ws
+
+    def free(self):
+        if self.handle:
+            _check(_lib.s4_weight_free(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            if self.handle and _lib is not None and self.ctx.handle:
+                _lib.s4_weight_free(self.handle)
+        except Exception:
+            pass
+
+
+class Context:
+    """One library context on one CUDA device (the device side of ``Engine.create``)."""
+
+    def __init__(self, device: int = 0):
+        load_library()
+        h = _P()
+        _check(_lib.s4_init(int(device), C.byref(h)))
+        self.handle = h.value
+        self.device = int(device)
+        self._weights = []
+
+    # -- weights ---------------------------------------------------------------------------------
+    def upload(self, packed, scales, N: int, K: int) -> Weight:
+        """Upload MatMulNBits bytes (``packed`` uint8 [N][K/32][16], ``scales`` fp16 [N][K/32]).
+
+        Host numpy arrays go through ``s4_weight_upload``; CUDA tensors through
+        ``s4_weight_upload_device``. Synchronous."""
+        h = _P()
+        if hasattr(packed, "is_cuda") and packed.is_cuda:
+            _check(_lib.s4_weight_upload_device(self.handle, packed.data_ptr(), scales.data_ptr(), N, K, 0,
+                                                C.byref(h)))
+        else:
+            p = np.ascontiguousarray(np.asarray(packed, dtype=np.uint8))
+            s = np.ascontiguousarray(np.asarray(scales, dtype=np.float16))
+            if p.size != N * (K // 32) * 16 or s.size != N * (K // 32):
+                raise S4Error(ERR_INVALID, f"packed/scales sizes do not match N={N} K={K}")
+            _check(_lib.s4_weight_upload(self.handle, p.ctypes.data, s.ctypes.data, N, K, 0, C.byref(h)))
+        return Weight(self, h.value, N, K)
+
+    # -- compute ---------------------------------------------------------------------------------
+    def matmul(self, x, W: Weight, M: int | None = None, y=None, stream=None):
+        """``y[M][N] = x[M][K] @ W^T`` on CUDA fp16 tensors (the engine's matmul(A, wname, Y))."""
+        import torch
+        if M is None:
+            M = x.shape[0]
+        if y is None:
+            y = torch.empty((M, W.N), dtype=torch.float16, device=x.device)
+        _check(_lib.s4_matmul(self.handle, W.handle, x.data_ptr(), int(M), y.data_ptr(), _stream_handle(stream)))
+        return y
+
+    def matmul_host(self, x: np.ndarray, W: Weight, y: np.ndarray | None = None) -> np.ndarray:
+        """Synchronous host-buffer matmul (``Gemm.setA`` + ``encode`` + ``readY``); fp16 arrays
+        or their uint16 bit patterns."""
+        x = np.ascontiguousarray(x)
+        M = x.shape[0]
+        if y is None:
+            y = np.empty((M, W.N), dtype=np.float16)
+        _check(_lib.s4_matmul_host(self.handle, W.handle, x.ctypes.data, int(M), y.ctypes.data))
+        return y
+
+    def matmul_host_ptr(self, x_ptr: int, M: int, W: Weight, y_ptr: int):
+        _check(_lib.s4_matmul_host(self.handle, W.handle, x_ptr, int(M), y_ptr))
+
+    def matmul_host_async(self, x, W: Weight, y, M: int | None = None, stream=None):
+        """Enqueue host->device copy, matmul and device->host copy on ``stream`` (pinned host
+        tensors or arrays ``x`` [M][K] and ``y`` [M][N], fp16); returns without waiting."""
+        if M is None:
+            M = x.shape[0]
+        _check(_lib.s4_matmul_host_async(self.handle, W.handle, _ptr(x), int(M), _ptr(y), _stream_handle(stream)))
+
+    def silu_mul(self, big, I: int, mid=None, stream=None):
+        """``mid = silu(big[:, :I]) * big[:, I:2I]`` on CUDA fp16 tensors."""
+        import torch
+        M = big.shape[0]
+        if mid is None:
+            mid = torch.empty((M, I), dtype=torch.float16, device=big.device)
+        _check(_lib.s4_silu_mul(self.handle, big.data_ptr(), int(M), int(I), mid.data_ptr(), _stream_handle(stream)))
+        return mid
+
+    # -- dispatcher ------------------------------------------------------------------------------
+    def plan(self, M: int, N: int = 0, K: int = 0):
+        f, t, s = C.c_int(), C.c_int(), C.c_int()
+        _check(_lib.s4_plan(self.handle, int(M), int(N), int(K), C.byref(f), C.byref(t), C.byref(s)))
+        return FAMILY_NAMES[f.value], t.value, s.value
+
+    def force(self, family=FAMILY_AUTO, tile: int = 0, split: int = 0):
+        if isinstance(family, str):
+            family = {v: k for k, v in FAMILY_NAMES.items()}[family]
+        _check(_lib.s4_force(self.handle, int(family), int(tile), int(split)))
+
+    def set_table(self, table):
+        import json
+        text = table if isinstance(table, str) else json.dumps(table)
+        _check(_lib.s4_set_table(self.handle, text.encode()))
+
+    # -- diagnostics -----------------------------------------------------------------------------
+    def check_errors(self) -> int:
+        f = C.c_uint32()
+        _check(_lib.s4_check_errors(self.handle, C.byref(f)))
+        return f.value
+
+    def clear_errors(self):
+        _check(_lib.s4_clear_errors(self.handle))
+
+    @property
+    def launch_count(self) -> int:
+        c = C.c_uint64()
+        _check(_lib.s4_launch_count(self.handle, C.byref(c)))
+        return c.value
+
+    @property
+    def sm_count(self) -> int:
+        d, s = C.c_int(), C.c_int()
+        _check(_lib.s4_device_info(self.handle, C.byref(d), C.byref(s)))
+        return s.value
+
+    def close(self):
+        if self.handle:
+            _check(_lib.s4_destroy(self.handle))
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
+class Gemm:
+    """The reference's standalone GEMM object (web/public/gemmbench/kernels.js:83-104).
+
+    ``Gemm(ctx, K=, N=, B=packed bytes, Sc=fp16 scale bits)`` uploads; ``setA(M, A16)`` stages
+    fp16 activations (uint16 bit patterns, as ``Uint16Array``); ``encode()`` runs the matmul on
+    the device; ``readY()`` returns the fp16 output bits (uint16, ``[M*N]``)."""
+
+    def __init__(self, ctx: Context, K: int, N: int, B, Sc):
+        import torch
+        self.ctx, self.K, self.N = ctx, int(K), int(N)
+        B = np.frombuffer(np.ascontiguousarray(B).tobytes(), np.uint8)
+        Sc = np.frombuffer(np.ascontiguousarray(Sc).tobytes(), np.uint16).view(np.float16)
+        self.W = ctx.upload(B, Sc, self.N, self.K)
+        self._dev = torch.device("cuda", ctx.device)
+        self.M = 0
+
+    def setA(self, M: int, A16):
+        import torch
+        a = np.ascontiguousarray(np.asarray(A16).view(np.uint16)).reshape(M, self.K)
+        self.M = int(M)
+        self.A = torch.from_numpy(a.view(np.int16)).to(self._dev).view(torch.float16)
+        self.Y = torch.empty((self.M, self.N), dtype=torch.float16, device=self._dev)
+
+    def encode(self, stream=None):
+        self.ctx.matmul(self.A, self.W, self.M, self.Y, stream)
+
+    def readY(self) -> np.ndarray:
+        import torch
+        torch.cuda.synchronize(self._dev)
+        return self.Y.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)

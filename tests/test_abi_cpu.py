@@ -1,0 +1,65 @@
+"""C-ABI checks that need no GPU: the library loads, exports every declared entry point, and
+rejects bad arguments with a status and a message instead of crashing."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "s4mm.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^S4_API\s+[\w\s\*]+?\b(s4_\w+)\(", text, flags=re.M)))
+
+
+def test_header_declares_the_boundary():
+    syms = declared_symbols()
+    for must in ("s4_init", "s4_destroy", "s4_weight_upload", "s4_matmul", "s4_matmul_host", "s4_silu_mul",
+                 "s4_plan", "s4_force", "s4_set_table", "s4_last_error"):
+        assert must in syms
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.load_library()
+    raw = C.CDLL(pkg.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(raw, name), name
+    assert set(declared_symbols()) == set(pkg.s4mm._SIGS), "ctypes bindings out of sync with the header"
+    assert lib.s4_version() >> 16 == 1
+
+
+def test_errors_without_work(pkg):
+    lib = pkg.load_library()
+    h = C.c_void_p()
+    # NULL out-pointer -> invalid argument, with a message
+    assert lib.s4_init(0, None) == pkg.s4mm.ERR_INVALID
+    assert b"NULL" in lib.s4_last_error()
+    # null context / weight handles
+    assert lib.s4_matmul(None, None, None, 1, None, None) == pkg.s4mm.ERR_INVALID
+    assert lib.s4_weight_upload(None, None, None, 16, 64, 0, C.byref(h)) == pkg.s4mm.ERR_INVALID
+    assert lib.s4_set_table(None, b"{}") == pkg.s4mm.ERR_INVALID
+    assert lib.s4_weight_free(None) == 0
+    assert lib.s4_destroy(None) == 0
+
+
+def test_init_without_gpu_fails_cleanly(pkg):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(pkg.S4Error) as e:
+        pkg.Context(0)
+    assert e.value.code in (pkg.s4mm.ERR_UNSUPPORTED, pkg.s4mm.ERR_CUDA)
+
+
+def test_missing_library_is_loud(pkg, tmp_path):
+    saved = pkg.s4mm._lib
+    pkg.s4mm._lib = None
+    try:
+        with pytest.raises(pkg.S4Error):
+            pkg.s4mm.load_library(str(tmp_path / "missing.so"))
+    finally:
+        pkg.s4mm._lib = saved

@@ -1,0 +1,149 @@
+"""The CPU oracle against the reference's own outputs (golden fixtures) and its own invariants."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import s4ref
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _cases(fname):
+    z = np.load(os.path.join(GOLDEN, fname))
+    names = sorted({k.split("/")[0] for k in z.files})
+    return z, names
+
+
+QZ, QNAMES = _cases("quant_cases.npz")
+MZ, MNAMES = _cases("matmul_cases.npz")
+
+
+@pytest.mark.parametrize("name", QNAMES)
+def test_quant_matches_reference_bit_exact(name):
+    packed, scales, deq = s4ref.quant(QZ[f"{name}/W"])
+    assert packed.dtype == np.uint8 and scales.dtype == np.float16
+    np.testing.assert_array_equal(packed, QZ[f"{name}/packed"])
+    np.testing.assert_array_equal(scales.view(np.uint16), QZ[f"{name}/scales"].view(np.uint16))
+    np.testing.assert_array_equal(deq.view(np.uint32), QZ[f"{name}/deq"].view(np.uint32))
+
+
+def test_quant_edge_rules():
+    W = QZ["edges_8x64/W"]
+    packed, scales, _ = s4ref.quant(W)
+    assert scales[0, 0] == 1.0                        # zero block -> scale 1
+    assert scales[1, 1] < 0 and scales[2, 1] > 0      # sign follows -max/8
+    q = s4ref.unpack_nibbles(packed)
+    # the element of largest magnitude always maps to nibble 0
+    for r in range(1, 8):
+        for b in range(2):
+            blk = W[r, 32 * b:32 * b + 32]
+            if np.abs(blk).max() > 0:
+                assert q[r, b, np.abs(blk).argmax()] == 0
+
+
+@pytest.mark.parametrize("name", QNAMES)
+def test_dequant_of_packed_equals_reference_deq(name):
+    deq = s4ref.dequant(QZ[f"{name}/packed"], QZ[f"{name}/scales"])
+    np.testing.assert_array_equal(deq, QZ[f"{name}/deq"])
+
+
+@pytest.mark.parametrize("name", MNAMES)
+def test_matmul_matches_reference_fake_quant(name):
+    x = MZ[f"{name}/x"]
+    y16, y32 = s4ref.matmul(x, MZ[f"{name}/packed"], MZ[f"{name}/scales"])
+    ref = MZ[f"{name}/y32"]
+    # same fp32 math, different summation order: fp32-level agreement
+    assert s4ref.max_rel(y32, ref) < 1e-5
+    ok, mr, mc = s4ref.check(y16, ref)
+    assert ok, (mr, mc)
+
+
+@pytest.mark.parametrize("name", MNAMES)
+def test_cpu_check_columns_formula(name):
+    x = MZ[f"{name}/x"]
+    packed, scales = MZ[f"{name}/packed"], MZ[f"{name}/scales"]
+    N = packed.shape[0]
+    cols = sorted({0, 1, N >> 1, N - 1})
+    pts = s4ref.cpu_check_columns(x, packed, scales, cols)
+    ref = MZ[f"{name}/y32"]
+    for (m, n), v in pts.items():
+        assert abs(v - ref[m, n]) <= 1e-5 * max(1.0, np.abs(ref).max())
+
+
+def test_generators_match_reference_recipe_hashes():
+    gens = json.load(open(os.path.join(GOLDEN, "generators.json")))
+    rng = np.random.default_rng(0)
+    for g in gens["make_gemm"]:
+        packed, scales = s4ref.make_gemm_weights(rng, g["K"], g["N"])
+        assert s4ref.sha256(packed) == g["packed_sha256"]
+        assert s4ref.sha256(scales) == g["scales_sha256"]
+    rng = np.random.default_rng(0)
+    for g in gens["make_chain"][:4]:
+        packed, scales = s4ref.make_chain_weights(rng, g["K"], g["N"])
+        assert s4ref.sha256(packed) == g["packed_sha256"]
+        assert s4ref.sha256(scales) == g["scales_sha256"]
+
+
+def test_pack_unpack_round_trip():
+    rng = np.random.default_rng(5)
+    q = rng.integers(0, 16, size=(7, 3, 32), dtype=np.uint8)
+    np.testing.assert_array_equal(s4ref.unpack_nibbles(s4ref.pack_nibbles(q)), q)
+
+
+@pytest.mark.parametrize("N,K", [(128, 64), (8224, 2048), (16, 96), (130, 32), (2048, 6144), (1, 32)])
+def test_device_layout_round_trip(N, K):
+    rng = np.random.default_rng(N * 7 + K)
+    packed, scales = s4ref.config_weights(rng, K, N)
+    wq, ws = s4ref.repack_device(packed, scales, N, K)
+    nblk, kt = s4ref.tiled_dims(N, K)
+    assert wq.shape == (nblk, kt, 8, 32, 4) and ws.shape == (nblk, kt, 8, 8, 4)
+    p2, s2 = s4ref.unrepack_device(wq, ws, N, K)
+    np.testing.assert_array_equal(p2, packed)
+    np.testing.assert_array_equal(s2.view(np.uint16), scales.view(np.uint16))
+
+
+def test_device_layout_fragment_semantics():
+    """Decode the device layout the way the GEMV kernel's fragments do and compare with the
+    row-major dequantised matrix: lane (g,t) word (blk,h) = row g+8h, k = 8t..8t+7 of block blk."""
+    N, K = 256, 128
+    rng = np.random.default_rng(3)
+    packed, scales = s4ref.config_weights(rng, K, N)
+    wq, ws = s4ref.repack_device(packed, scales, N, K)
+    deq = s4ref.dequant(packed, scales)
+    nblk, kt = s4ref.tiled_dims(N, K)
+    for nb in range(nblk):
+        for t_ in range(kt):
+            for sub in range(8):
+                for lane in range(32):
+                    g, t = lane >> 2, lane & 3
+                    for j in range(4):
+                        blk, h = j >> 1, j & 1
+                        w = int(wq[nb, t_, sub, lane, j])
+                        lo = [(w >> (4 * i)) & 15 for i in range(4)]
+                        hi = [(w >> (16 + 4 * i)) & 15 for i in range(4)]
+                        vals = [v for pair in zip(lo, hi) for v in pair]     # k0..k7 in order
+                        r = nb * 128 + sub * 16 + g + 8 * h
+                        k0 = t_ * 64 + blk * 32 + 8 * t
+                        s = np.float32(ws[nb, t_, sub, g, blk * 2 + h])
+                        got = (np.array(vals, np.float32) - 8) * s
+                        np.testing.assert_array_equal(got, deq[r, k0:k0 + 8])
+
+
+def test_silu_mul_formula():
+    rng = np.random.default_rng(2)
+    big = rng.standard_normal((3, 8)).astype(np.float16)
+    mid = s4ref.silu_mul(big, 4)
+    g = big[:, :4].astype(np.float64)
+    u = big[:, 4:].astype(np.float64)
+    np.testing.assert_allclose(mid.astype(np.float64), g / (1 + np.exp(-g)) * u, rtol=2e-3, atol=1e-4)
+
+
+def test_metrics():
+    ref = np.array([[1.0, -2.0], [0.5, 4.0]], np.float32)
+    assert s4ref.max_rel(ref, ref) == 0.0
+    assert abs(s4ref.max_rel(ref + np.float32(0.004), ref) - 0.001) < 1e-7
+    assert s4ref.min_row_cosine(ref, ref) > 0.999999
+    ok, _, _ = s4ref.check(ref * 1.01, ref)
+    assert not ok
