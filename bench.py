@@ -235,11 +235,35 @@ def run_ours(args, rank, world, local_rank):
             ys[(M, name)] = torch.empty((M, N), dtype=torch.float16, device=dev)
     counter = [0]
 
-    def step():
+    def sweep(rot: int, st):
+        # one step: the 16 matmuls, each on the next copy of its weight
         for mi, M in enumerate(MS):
             for name, K, N in SHAPES:
-                W = Ws[name][(counter[0] * len(MS) + mi) % COPIES]
-                ctx.matmul(xs[(M, name)], W, M, ys[(M, name)], stream)
+                W = Ws[name][(rot * len(MS) + mi) % COPIES]
+                ctx.matmul(xs[(M, name)], W, M, ys[(M, name)], st)
+
+    # The engine replays a cached step list (engine.js:313-343); here each step is a CUDA graph
+    # (one per weight rotation) so the host does not pace the GPU.
+    graphs = []
+    cap_stream = torch.cuda.Stream(dev)
+    cap_stream.wait_stream(stream)
+    with torch.cuda.stream(cap_stream):
+        for rot in range(COPIES):
+            sweep(rot, cap_stream)          # eager warm-up of this rotation
+        cap_stream.synchronize()
+        launches_per_step = None
+        for rot in range(COPIES):
+            g = torch.cuda.CUDAGraph()
+            n0 = ctx.launch_count
+            with torch.cuda.graph(g, stream=cap_stream):
+                sweep(rot, cap_stream)
+            launches_per_step = ctx.launch_count - n0
+            graphs.append(g)
+    stream.wait_stream(cap_stream)
+    torch.cuda.synchronize(dev)
+
+    def step():
+        graphs[counter[0] % COPIES].replay()
         counter[0] += 1
 
     def barrier():
@@ -258,7 +282,6 @@ def run_ours(args, rank, world, local_rank):
         step()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = ctx.launch_count
     with ClockSampler(local_rank) as clocks:
         barrier()
         e0.record(stream)
@@ -266,7 +289,7 @@ def run_ours(args, rank, world, local_rank):
             step()
         e1.record(stream)
         barrier()
-    launches = ctx.launch_count - launches0
+    launches = launches_per_step * args.steps   # kernels inside the replayed graphs
     ms = max_over_ranks(e0.elapsed_time(e1))
     errs = ctx.check_errors()
     if errs:
@@ -282,6 +305,7 @@ def run_ours(args, rank, world, local_rank):
             hy[(M, name)] = torch.empty((M, N), dtype=torch.float16).pin_memory()
 
     def e2e_step():
+        # every call through the public host-buffer entry point, no graph
         for mi, M in enumerate(MS):
             for name, K, N in SHAPES:
                 W = Ws[name][(counter[0] * len(MS) + mi) % COPIES]
@@ -319,20 +343,27 @@ def run_ours(args, rank, world, local_rank):
     # ---- per-(shape, M) breakdown on this rank (device time, 8 rotating copies) -------------------------
     per = {}
     if rank == 0 and not args.quick:
+        # each (shape, M) alone: a graph of 64 back-to-back calls over the 8 rotating copies
         for name, K, N in SHAPES:
             for M in MS:
                 reps = 64
-                for r in range(8):
-                    ctx.matmul(xs[(M, name)], Ws[name][r % COPIES], M, ys[(M, name)], stream)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(cap_stream):
+                    with torch.cuda.graph(g, stream=cap_stream):
+                        for r in range(reps):
+                            ctx.matmul(xs[(M, name)], Ws[name][r % COPIES], M, ys[(M, name)], cap_stream)
+                torch.cuda.synchronize(dev)
+                for _ in range(3):
+                    g.replay()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                for r in range(reps):
-                    ctx.matmul(xs[(M, name)], Ws[name][r % COPIES], M, ys[(M, name)], stream)
+                for _ in range(5):
+                    g.replay()
                 b.record(stream)
                 torch.cuda.synchronize(dev)
-                us = a.elapsed_time(b) * 1e3 / reps
+                us = a.elapsed_time(b) * 1e3 / (5 * reps)
                 gbs = alg_bytes(M, K, N) / (us * 1e-6) / 1e9
-                per[f"{name}/M{M}"] = {"us": round(us, 3), "GBps": round(gbs, 1)}
+                per[f"{name}/M{M}"] = {"us": round(us, 3), "GBps": round(gbs, 1), "frac": round(gbs / peaks()[0], 3)}
 
     # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------------------------------
     hbm, bf16, peak_kind = peaks()
@@ -371,6 +402,7 @@ def run_ours(args, rank, world, local_rank):
             "per_call": per,
         }
         print(json.dumps(line), flush=True)
+    del graphs
     ctx.close()
     if world > 1:
         dist.barrier()

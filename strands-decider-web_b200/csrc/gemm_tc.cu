@@ -1,10 +1,488 @@
-// tcgen05 GEMM family (placeholder until the kernel lands).
+// tcgen05 GEMM family (M > 32): y[M][N] = x[M][K] @ W^T with int4 block-32 weights dequantised to
+// fp16 in shared memory and fed to the 5th-generation tensor cores, fp32 accumulation in TMEM.
+//
+// Replaces kernelV4 (+ REDUCE) of web/public/gemmbench/kernels.js:269-353 and the portable
+// kernelV6 (kernels.js:438-479) that the engine picks for M > 8 (engine.js:17-33). Unlike V4 it
+// accumulates in fp32 end to end, split-K partials included.
+//
+// Shape of one MMA (swap-AB): A = 128 weight rows (output columns n) x 16 K, fp16, K-major in
+// shared memory with the 128-byte swizzle; B = tn tokens x 16 K of the activations, loaded by TMA
+// with the same swizzle; D = 128 x tn fp32 in TMEM (lane = n, column = token).
+//
+// Work: units (token block tb, n-block nb, k-tile kt) of 64 K, kt fastest; CTA b of G takes units
+// [b*U/G, (b+1)*U/G) (stream-K), so every SM gets the same number of MMAs whatever M, N and K are.
+// A run of units of one (tb, nb) tile is a segment; a segment that covers the whole K range is
+// written as fp16 directly, otherwise its fp32 partial goes to context scratch and the last CTA to
+// arrive at the tile (atomic ticket, no spinning) sums the partials in CTA order.
+//
+// Warp roles (384 threads): warp 0 lane 0 streams raw int4 chunks (1-D bulk copies) into a
+// 12-slot ring; warp 2 lane 0 loads activation tiles by TMA into a 3-stage ring; warp 1 owns TMEM
+// and lane 0 issues the MMAs; warps 4-7 dequantise int4 -> fp16 into the MMA's A stage; warps 8-11
+// drain TMEM (double-buffered accumulators) and write the output.
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace s4 {
-bool tc_available() { return false; }
-cudaError_t launch_tc_gemm(const uint8_t*, const uint8_t*, const __half*, __half*, uint32_t*, int, int, int, int, int,
-                           int, int, cudaStream_t) {
-  return cudaErrorNotSupported;
+
+constexpr int kTcMaxTn = 256;
+constexpr int kTcStagesA = 3;
+constexpr int kTcSlotsW = 12;
+constexpr int kTcThreads = 384;
+constexpr int kTcXStageBytes = kTcMaxTn * 128;  // tn rows x 64 fp16
+constexpr int kTcAStageBytes = 128 * 128;       // 128 rows x 64 fp16
+constexpr int kTcWSlotBytes = kChunkWBytes + kChunkSBytes;
+constexpr int kTcOffX = 0;
+constexpr int kTcOffA = kTcOffX + kTcStagesA * kTcXStageBytes;
+constexpr int kTcOffW = kTcOffA + kTcStagesA * kTcAStageBytes;
+constexpr int kTcOffBar = kTcOffW + kTcSlotsW * kTcWSlotBytes;
+constexpr int kTcNumBars = 3 * kTcStagesA + 2 * kTcSlotsW + 2 + 2 + 1;
+constexpr int kTcOffMisc = kTcOffBar + kTcNumBars * 8;
+constexpr size_t kTcSmem = (size_t)kTcOffMisc + 64 + 1024;  // + alignment slack
+constexpr uint32_t kTcTmemCols = 512;                       // two 256-column accumulators
+
+struct TcParams {
+  const uint8_t* wq;
+  const uint8_t* ws;
+  __half* y;
+  float* partials;    // [G][2][256][128] fp32
+  uint32_t* tickets;  // [ntb * nblk]
+  uint32_t* err;
+  int M, N, K;
+  int nblk, ktiles;
+  int tn;     // tokens per tile = MMA N (multiple of 16, <= 256)
+  int ntb;    // token blocks
+  int total;  // units = ntb * nblk * ktiles
+  int grid;
+};
+
+// ---- tcgen05 / TMA wrappers -----------------------------------------------------------------------
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
+  d |= (uint64_t)1u << 16;                  // leading byte offset (unused with 128-byte swizzle)
+  d |= (uint64_t)(1024u >> 4) << 32;        // stride byte offset: 8 rows x 128 bytes
+  d |= (uint64_t)1u << 46;                  // descriptor version (sm_100)
+  d |= (uint64_t)2u << 61;                  // 128-byte swizzle
+  return d;
 }
+__device__ __forceinline__ uint32_t f16_f32_idesc(int n) {
+  // dense, D f32 (bits 4-5 = 1), A/B f16 (0), both K-major, N >> 3 at 17, M >> 4 at 24
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ int tc_begin(int b, const TcParams& p) { return (int)(((int64_t)b * p.total) / p.grid); }
+__device__ __forceinline__ int tc_cta_of(int u, const TcParams& p) {
+  return (int)((((int64_t)u + 1) * p.grid - 1) / p.total);
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p, const __grid_constant__ CUtensorMap tmap_x) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* xs = smem + kTcOffX;
+  uint8_t* wa = smem + kTcOffA;
+  uint8_t* wraw = smem + kTcOffW;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
+  uint64_t* full_x = bars;
+  uint64_t* ddone = full_x + kTcStagesA;
+  uint64_t* empty_a = ddone + kTcStagesA;
+  uint64_t* full_w = empty_a + kTcStagesA;
+  uint64_t* empty_w = full_w + kTcSlotsW;
+  uint64_t* accf = empty_w + kTcSlotsW;
+  uint64_t* acce = accf + 2;
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTcOffMisc);
+  int* s_flag = reinterpret_cast<int*>(smem + kTcOffMisc + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = tc_begin(blockIdx.x, p), c1 = tc_begin(blockIdx.x + 1, p);
+  const int n = c1 - c0;
+  const int KT = p.ktiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStagesA; ++s) {
+      mbar_init(full_x + s, 1);
+      mbar_init(ddone + s, 4);
+      mbar_init(empty_a + s, 1);
+    }
+    for (int s = 0; s < kTcSlotsW; ++s) {
+      mbar_init(full_w + s, 1);
+      mbar_init(empty_w + s, 4);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf + b, 1);
+      mbar_init(acce + b, 128);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTcTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------- raw int4 chunks: producer -------------
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < n; ++i) {
+        const int slot = i % kTcSlotsW;
+        if (i >= kTcSlotsW && !mbar_wait(empty_w + slot, ((i / kTcSlotsW) - 1) & 1)) {
+          set_error(p.err, kErrWaitTimeout);
+          ok = false;
+          break;
+        }
+        const int u = c0 + i;
+        const int tile = u / KT, kt = u - tile * KT;
+        const int nb = tile % p.nblk;
+        const int64_t chunk = (int64_t)nb * KT + kt;
+        uint8_t* dst = wraw + slot * kTcWSlotBytes;
+        mbar_arrive_expect_tx(full_w + slot, kTcWSlotBytes);
+        bulk_g2s_plain(dst, p.wq + chunk * kChunkWBytes, kChunkWBytes, full_w + slot);
+        bulk_g2s_plain(dst + kChunkWBytes, p.ws + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
+        ++issued;
+      }
+      if (!ok) {
+        const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
+        for (int i = (issued > kTcSlotsW ? issued - kTcSlotsW : 0); i < issued; ++i)
+          if (!mbar_wait_until(full_w + (i % kTcSlotsW), (i / kTcSlotsW) & 1, deadline)) break;
+      }
+    }
+  } else if (warp == 2) {
+    // ------------- activation tiles: producer (TMA) -------------
+    if (lane == 0) {
+      pdl_wait();  // x is written by the previous kernel in the stream
+      int issued = 0;
+      bool ok = true;
+      const uint32_t xbytes = (uint32_t)p.tn * 128u;
+      for (int i = 0; i < n; ++i) {
+        const int s = i % kTcStagesA;
+        if (i >= kTcStagesA && !mbar_wait(empty_a + s, ((i / kTcStagesA) - 1) & 1)) {
+          set_error(p.err, kErrWaitTimeout);
+          ok = false;
+          break;
+        }
+        const int u = c0 + i;
+        const int tile = u / KT, kt = u - tile * KT;
+        const int tb = tile / p.nblk;
+        mbar_arrive_expect_tx(full_x + s, xbytes);
+        tma_load_2d(xs + s * kTcXStageBytes, &tmap_x, kt * 64, tb * p.tn, full_x + s);
+        ++issued;
+      }
+      if (!ok) {
+        const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
+        for (int i = (issued > kTcStagesA ? issued - kTcStagesA : 0); i < issued; ++i)
+          if (!mbar_wait_until(full_x + (i % kTcStagesA), (i / kTcStagesA) & 1, deadline)) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------- MMA issuer -------------
+    if (lane == 0) {
+      const uint32_t idesc = f16_f32_idesc(p.tn);
+      bool ok = true;
+      int si = 0;
+      int i = 0;
+      while (ok && i < n) {
+        const int u0 = c0 + i;
+        const int tile = u0 / KT;
+        const int seg_end = min(c1, (tile + 1) * KT);  // units [u0, seg_end) belong to this tile
+        const int buf = si & 1;
+        if (si >= 2 && !mbar_wait(acce + buf, ((si >> 1) - 1) & 1)) {
+          set_error(p.err, kErrWaitTimeout);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dcol = tmem_base + (uint32_t)(buf * 256);
+        for (int u = u0; u < seg_end; ++u, ++i) {
+          const int s = i % kTcStagesA;
+          const uint32_t par = (i / kTcStagesA) & 1;
+          if (!mbar_wait(full_x + s, par) || !mbar_wait(ddone + s, par)) {
+            set_error(p.err, kErrWaitTimeout);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(wa + s * kTcAStageBytes), b0 = smem_u32(xs + s * kTcXStageBytes);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tc_mma(dcol, sw128_kmajor_desc(a0 + j * 32), sw128_kmajor_desc(b0 + j * 32), idesc,
+                   (u != u0 || j > 0) ? 1u : 0u);
+          tc_commit(empty_a + s);
+        }
+        if (!ok) break;
+        tc_commit(accf + buf);
+        ++si;
+      }
+      tc_commit(drain);  // completes when every MMA issued above has finished
+      (void)mbar_wait(drain, 0);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------- dequantisers: int4 chunk -> fp16 A stage (128-byte swizzled, K-major) -------------
+    const int d = threadIdx.x - 128;
+    bool ok = true;
+    for (int i = 0; i < n && ok; ++i) {
+      const int s = i % kTcStagesA, slot = i % kTcSlotsW;
+      if (!mbar_wait(full_w + slot, (i / kTcSlotsW) & 1) ||
+          (i >= kTcStagesA && !mbar_wait(empty_a + s, ((i / kTcStagesA) - 1) & 1))) {
+        set_error(p.err, kErrWaitTimeout);
+        ok = false;
+        break;
+      }
+      const uint8_t* src = wraw + slot * kTcWSlotBytes;
+      const uint32_t dst = smem_u32(wa + s * kTcAStageBytes);
+#pragma unroll
+      for (int rep = 0; rep < 2; ++rep) {
+        const int L = d + rep * 128;  // 16-byte lane slot of the chunk: sub-tile L / 32, lane L % 32
+        const int sub = L >> 5, ln = L & 31, g = ln >> 2, t = ln & 3;
+        const uint4 v = *reinterpret_cast<const uint4*>(src + L * 16);
+        const uint2 sc = *reinterpret_cast<const uint2*>(src + kChunkWBytes + sub * 64 + g * 8);
+        const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+        const uint32_t sh[4] = {sc.x & 0xFFFFu, sc.x >> 16, sc.y & 0xFFFFu, sc.y >> 16};  // (g,b0) (g+8,b0) (g,b1) (g+8,b1)
+        const bool odd = (g & 1) != 0;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          // odd rows store the other quant block first: the 8 lanes of a store phase then hit
+          // 32 distinct banks
+          const int j = odd ? (jj ^ 2) : jj;
+          const uint32_t w = odd ? words[jj ^ 2] : words[jj];
+          const uint32_t sbits = odd ? sh[jj ^ 2] : sh[jj];
+          const int blk = j >> 1, h = j & 1;
+          const int r = sub * 16 + g + 8 * h;
+          const int c = blk * 4 + t;
+          uint32_t hv[4];
+          i4x8_to_h2x4_centered(w, hv);
+          const uint32_t s2 = sbits | (sbits << 16);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(hv[e]) : "r"(hv[e]), "r"(s2));
+          const uint32_t addr = dst + r * 128 + ((c ^ (r & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(hv[0]), "r"(hv[1]), "r"(hv[2]),
+                       "r"(hv[3])
+                       : "memory");
+        }
+      }
+      fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(ddone + s);
+        mbar_arrive(empty_w + slot);
+      }
+    }
+  } else if (warp >= 8) {
+    // ------------- epilogue: TMEM -> output (or fp32 partial + ticket fix-up) -------------
+    const int q = warp - 8;  // TMEM lane quarter this warp may access
+    const int nl = q * 32 + lane;
+    const int et = threadIdx.x - 256;
+    bool failed = false;
+    int si = 0;
+    for (int i = 0; i < n; ++si) {
+      const int u0 = c0 + i;
+      const int tile = u0 / KT;
+      const int seg_end = min(c1, (tile + 1) * KT);
+      const int ks = u0 - tile * KT, ke = seg_end - tile * KT;
+      i += seg_end - u0;
+      const int tb = tile / p.nblk, nb = tile - tb * p.nblk;
+      const int buf = si & 1;
+      const bool full = (ks == 0 && ke == KT);
+      const int tok0 = tb * p.tn;
+      const int ncol = nb * 128 + nl;
+      if (!failed && !mbar_wait(accf + buf, (si >> 1) & 1)) {
+        set_error(p.err, kErrWaitTimeout);
+        failed = true;  // keep walking segments so the named barriers below stay matched
+      }
+      const int sel = (u0 == c0) ? 0 : 1;
+      float* mine = p.partials + (((int64_t)blockIdx.x * 2 + sel) * kTcMaxTn) * 128 + nl;
+      if (!failed) {
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
+        for (int cb = 0; cb < p.tn; cb += 16) {
+          float v[16];
+          tmem_ld16(taddr + cb, v);
+          if (full) {
+            if (ncol < p.N) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int tok = tok0 + cb + e;
+                if (tok < p.M) p.y[(int64_t)tok * p.N + ncol] = __float2half_rn(v[e]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) __stcg(mine + (int64_t)(cb + e) * 128, v[e]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(acce + buf);
+      }
+      if (!full) {
+        __threadfence();
+        named_bar_sync(2, 128);
+        const int first = tc_cta_of(tile * KT, p), last = tc_cta_of(tile * KT + KT - 1, p);
+        if (et == 0) {
+          const uint32_t prev = atomicAdd(p.tickets + tile, 1u);
+          *s_flag = (prev == (uint32_t)(last - first)) ? 1 : 0;
+        }
+        named_bar_sync(2, 128);
+        if (*s_flag) {
+          __threadfence();
+          const int rows = min(p.tn, p.M - tok0);
+          for (int tl = 0; tl < rows; ++tl) {
+            float acc = 0.f;
+            for (int b = first; b <= last; ++b) {
+              const int bsel = (tc_begin(b, p) >= tile * KT) ? 0 : 1;
+              acc += __ldcg(p.partials + (((int64_t)b * 2 + bsel) * kTcMaxTn + tl) * 128 + nl);
+            }
+            if (ncol < p.N) p.y[(int64_t)(tok0 + tl) * p.N + ncol] = __float2half_rn(acc);
+          }
+          named_bar_sync(2, 128);
+          if (et == 0) atomicExch(p.tickets + tile, 0u);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTcTmemCols)
+                 : "memory");
+  }
+}
+
+// ---- host side -------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+bool tc_available() { return true; }
+
+size_t tc_partials_bytes(int max_grid) { return (size_t)max_grid * 2 * kTcMaxTn * 128 * sizeof(float); }
+
+// tile_n: requested tokens per tile (0 = automatic).
+cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
+                           uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
+                           int ktiles, int tile_n, int grid, cudaStream_t stream) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  int tn = tile_n > 0 ? tile_n : (M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16);
+  if (tn < 16 || tn > kTcMaxTn || tn % 16) return cudaErrorInvalidValue;
+  TcParams p;
+  p.wq = wq;
+  p.ws = ws;
+  p.y = y;
+  p.partials = partials;
+  p.tickets = tickets;
+  p.err = err;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.nblk = nblk;
+  p.ktiles = ktiles;
+  p.tn = tn;
+  p.ntb = (M + tn - 1) / tn;
+  if ((int64_t)p.ntb * nblk > max_tickets) return cudaErrorInvalidValue;
+  const int64_t total = (int64_t)p.ntb * nblk * ktiles;
+  if (total > INT32_MAX) return cudaErrorInvalidValue;
+  p.total = (int)total;
+  p.grid = grid < p.total ? grid : p.total;
+
+  CUtensorMap tmap;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64u, (cuuint32_t)tn};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid, 1, 1);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tc_gemm_kernel, p, tmap);
+}
+
 }  // namespace s4

@@ -37,8 +37,9 @@ struct GemvParams {
 };
 
 constexpr int kGemvComputeWarps = 8;
+constexpr int kGemvMaxCtasPerSm = 4;  // scratch is sized for this many CTAs per SM
 constexpr int kGemvThreads = (kGemvComputeWarps + 1) * 32;
-constexpr int kGemvSlots = 24;
+constexpr int kGemvSlots = 12;
 constexpr int kSlotBytes = kChunkWBytes + kChunkSBytes;
 constexpr size_t kGemvSmem = (size_t)kGemvSlots * kSlotBytes + 2 * kGemvSlots * sizeof(uint64_t) + 16;
 
@@ -122,7 +123,19 @@ __device__ __forceinline__ void flush_segment(const GemvParams& p, int nb, int s
 }
 
 template <int MG>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_streamk_kernel(const GemvParams p) {
+__device__ __forceinline__ void load_x(uint4 (&xv)[MG][2], const __half* const (&xr)[MG], const bool (&xok)[MG],
+                                       int kbase, int K, bool kfull) {
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg)
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const bool ok = xok[mg] && (kfull || kbase + blk * 32 < K);
+      xv[mg][blk] = ok ? __ldg(reinterpret_cast<const uint4*>(xr[mg] + kbase + blk * 32)) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+template <int MG>
+__global__ void __launch_bounds__(kGemvThreads, (MG == 1 ? 3 : (MG == 2 ? 2 : 1))) gemv_streamk_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* slots = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kGemvSlots * kSlotBytes);
@@ -148,20 +161,29 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_streamk_kernel(const Gem
     // ---------------- producer: stream this CTA's weight bytes into the slot ring ----------------
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
+      const uint8_t* wsrc = p.wq + (int64_t)c0 * kChunkWBytes;
+      const uint8_t* ssrc = p.ws + (int64_t)c0 * kChunkSBytes;
       int issued = 0;
       bool ok = true;
+      int s = 0;
+      uint32_t ph = 0;  // phase of empty[s] to wait for (used once the ring wraps)
       for (int i = 0; i < n; ++i) {
-        const int s = i % kGemvSlots;
-        if (i >= kGemvSlots && !mbar_wait(empty + s, ((i / kGemvSlots) - 1) & 1)) {
+        if (i >= kGemvSlots && !mbar_wait(empty + s, ph)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
           break;
         }
         uint8_t* dst = slots + (size_t)s * kSlotBytes;
         mbar_arrive_expect_tx(full + s, kSlotBytes);
-        bulk_g2s(dst, p.wq + (int64_t)(c0 + i) * kChunkWBytes, kChunkWBytes, full + s, pol);
-        bulk_g2s(dst + kChunkWBytes, p.ws + (int64_t)(c0 + i) * kChunkSBytes, kChunkSBytes, full + s, pol);
+        bulk_g2s(dst, wsrc, kChunkWBytes, full + s, pol);
+        bulk_g2s(dst + kChunkWBytes, ssrc, kChunkSBytes, full + s, pol);
+        wsrc += kChunkWBytes;
+        ssrc += kChunkSBytes;
         ++issued;
+        if (++s == kGemvSlots) {
+          s = 0;
+          if (i >= kGemvSlots) ph ^= 1;
+        }
       }
       if (!ok) {
         // drain: do not leave the CTA while copies into its shared memory are in flight
@@ -174,81 +196,96 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_streamk_kernel(const Gem
   }
 
   // ---------------- compute warps ----------------
-  pdl_wait();  // x is written by the previous kernel in the stream
   const int g = lane >> 2, t = lane & 3;
   const int KT = p.ktiles;
+  const bool kfull = (p.K & 63) == 0;
+  const __half* xr[MG];
+  bool xok[MG];
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg) {
+    const int m = p.token0 + mg * 8 + g;
+    xok[mg] = m < p.M;
+    xr[mg] = p.x + (int64_t)(xok[mg] ? m : 0) * p.K + 8 * t;
+  }
   float acc[MG][4];
 #pragma unroll
   for (int mg = 0; mg < MG; ++mg)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[mg][e] = 0.f;
 
-  int cur_nb = (n > 0) ? c0 / KT : 0;
+  int nb = c0 / KT, kt = c0 - nb * KT;  // the only division: chunk indices advance incrementally
+  int cur_nb = nb;
   int seg_start = c0;
   bool failed = false;
   int consumed = 0;  // chunks whose copies this warp has seen land
+  int s = 0;
+  uint32_t ph = 0;
+  const uint8_t* my_w = slots + warp * 512 + lane * 16;
+  const uint8_t* my_s = slots + kChunkWBytes + warp * 64 + g * 8;
+
+  pdl_wait();  // x is written by the previous kernel in the stream
+  uint4 xn[MG][2];
+  if (n > 0) load_x<MG>(xn, xr, xok, kt * 64, p.K, kfull);
   for (int i = 0; i < n; ++i) {
-    const int c = c0 + i;
-    const int nb = c / KT;
-    const int kt = c - nb * KT;
     if (nb != cur_nb) {
-      flush_segment<MG>(p, cur_nb, seg_start, c, c0, acc, warp, lane, s_flag);
+      flush_segment<MG>(p, cur_nb, seg_start, c0 + i, c0, acc, warp, lane, s_flag);
 #pragma unroll
       for (int mg = 0; mg < MG; ++mg)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[mg][e] = 0.f;
       cur_nb = nb;
-      seg_start = c;
+      seg_start = c0 + i;
     }
-    // activations for this k-tile: token 8mg+g, K = kt*64 + blk*32 + 8t .. +8
     uint4 xv[MG][2];
 #pragma unroll
     for (int mg = 0; mg < MG; ++mg) {
-      const int m = p.token0 + mg * 8 + g;
-#pragma unroll
-      for (int blk = 0; blk < 2; ++blk) {
-        const int k = kt * 64 + blk * 32 + 8 * t;
-        if (m < p.M && k < p.K)
-          xv[mg][blk] = ldg_nc_v4(p.x + (int64_t)m * p.K + k);
-        else
-          xv[mg][blk] = make_uint4(0, 0, 0, 0);
-      }
+      xv[mg][0] = xn[mg][0];
+      xv[mg][1] = xn[mg][1];
     }
-    const int s = i % kGemvSlots;
-    if (!failed && !mbar_wait(full + s, (i / kGemvSlots) & 1)) {
+    // prefetch the next chunk's activations while this one is computed
+    const int kt_next = (kt + 1 == KT) ? 0 : kt + 1;
+    if (i + 1 < n) load_x<MG>(xn, xr, xok, kt_next * 64, p.K, kfull);
+
+    if (!failed && !mbar_wait(full + s, ph)) {
       set_error(p.err, kErrWaitTimeout);
       failed = true;  // keep walking the chunk list so every warp meets the same named barriers
     }
-    if (failed) continue;
-    consumed = i + 1;
-    const uint8_t* slot = slots + (size_t)s * kSlotBytes;
-    const uint4 wv = *reinterpret_cast<const uint4*>(slot + warp * 512 + lane * 16);
-    const uint2 sv = *reinterpret_cast<const uint2*>(slot + kChunkWBytes + warp * 64 + g * 8);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty + s);
+    if (!failed) {
+      consumed = i + 1;
+      const uint4 wv = *reinterpret_cast<const uint4*>(my_w + s * kSlotBytes);
+      const uint2 sv = *reinterpret_cast<const uint2*>(my_s + s * kSlotBytes);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + s);
 
-    const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
-    const __half2 s01 = *reinterpret_cast<const __half2*>(&sv.x);  // (row g, blk0), (row g+8, blk0)
-    const __half2 s23 = *reinterpret_cast<const __half2*>(&sv.y);  // (row g, blk1), (row g+8, blk1)
-    const float2 sb0 = __half22float2(s01);
-    const float2 sb1 = __half22float2(s23);
+      const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+      const float2 sb0 = __half22float2(*reinterpret_cast<const __half2*>(&sv.x));  // (row g, blk0), (row g+8, blk0)
+      const float2 sb1 = __half22float2(*reinterpret_cast<const __half2*>(&sv.y));  // (row g, blk1), (row g+8, blk1)
 #pragma unroll
-    for (int blk = 0; blk < 2; ++blk) {
-      uint32_t ha[4], hb[4];
-      i4x8_to_h2x4_centered(wr[2 * blk + 0], ha);  // row g
-      i4x8_to_h2x4_centered(wr[2 * blk + 1], hb);  // row g + 8
-      const float sg = blk ? sb1.x : sb0.x;
-      const float sg8 = blk ? sb1.y : sb0.y;
+      for (int blk = 0; blk < 2; ++blk) {
+        uint32_t ha[4], hb[4];
+        i4x8_to_h2x4_centered(wr[2 * blk + 0], ha);  // row g
+        i4x8_to_h2x4_centered(wr[2 * blk + 1], hb);  // row g + 8
+        const float sg = blk ? sb1.x : sb0.x;
+        const float sg8 = blk ? sb1.y : sb0.y;
 #pragma unroll
-      for (int mg = 0; mg < MG; ++mg) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        mma_16816(d, ha[0], hb[0], ha[1], hb[1], xv[mg][blk].x, xv[mg][blk].y);
-        mma_16816(d, ha[2], hb[2], ha[3], hb[3], xv[mg][blk].z, xv[mg][blk].w);
-        acc[mg][0] = fmaf(sg, d[0], acc[mg][0]);
-        acc[mg][1] = fmaf(sg, d[1], acc[mg][1]);
-        acc[mg][2] = fmaf(sg8, d[2], acc[mg][2]);
-        acc[mg][3] = fmaf(sg8, d[3], acc[mg][3]);
+        for (int mg = 0; mg < MG; ++mg) {
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_16816(d, ha[0], hb[0], ha[1], hb[1], xv[mg][blk].x, xv[mg][blk].y);
+          mma_16816(d, ha[2], hb[2], ha[3], hb[3], xv[mg][blk].z, xv[mg][blk].w);
+          acc[mg][0] = fmaf(sg, d[0], acc[mg][0]);
+          acc[mg][1] = fmaf(sg, d[1], acc[mg][1]);
+          acc[mg][2] = fmaf(sg8, d[2], acc[mg][2]);
+          acc[mg][3] = fmaf(sg8, d[3], acc[mg][3]);
+        }
       }
+    }
+    if (++s == kGemvSlots) {
+      s = 0;
+      ph ^= 1;
+    }
+    if (++kt == KT) {
+      kt = 0;
+      ++nb;
     }
   }
   // Every compute warp walks the same chunk list (also after a failed wait, see above), so all of
@@ -263,18 +300,33 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_streamk_kernel(const Gem
   }
 }
 
+// CTAs of one launch when the caller leaves the split to the kernel: every resident slot.
 template <int MG>
-static cudaError_t launch_gemv_mg(const GemvParams& p, cudaStream_t stream, bool pdl) {
-  static bool configured[64] = {};
+static cudaError_t gemv_auto_grid(int sm_count, int* grid) {
+  static int occ[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
+  if (occ[dev] == 0) {
     e = cudaFuncSetAttribute(gemv_streamk_kernel<MG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmem);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    int blocks = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, gemv_streamk_kernel<MG>, kGemvThreads, kGemvSmem);
+    if (e != cudaSuccess) return e;
+    occ[dev] = blocks < 1 ? 1 : (blocks > kGemvMaxCtasPerSm ? kGemvMaxCtasPerSm : blocks);
   }
+  *grid = occ[dev] * sm_count;
+  return cudaSuccess;
+}
+
+template <int MG>
+static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t stream, bool pdl) {
+  int auto_grid = 0;
+  cudaError_t e = gemv_auto_grid<MG>(sm_count, &auto_grid);  // also sets the shared-memory attribute
+  if (e != cudaSuccess) return e;
+  if (p.grid <= 0) p.grid = auto_grid;
+  if (p.grid > p.total) p.grid = p.total;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid, 1, 1);
   cfg.blockDim = dim3(kGemvThreads, 1, 1);
@@ -293,7 +345,7 @@ constexpr int kGemvMaxGroups = 4;
 
 cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
                         uint32_t* tickets, uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0,
-                        int groups, int grid, cudaStream_t stream, bool pdl) {
+                        int groups, int grid, int sm_count, cudaStream_t stream, bool pdl) {
   GemvParams p;
   p.wq = wq;
   p.ws = ws;
@@ -308,19 +360,21 @@ cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, _
   p.nblk = nblk;
   p.ktiles = ktiles;
   p.total = nblk * ktiles;
-  p.grid = grid < p.total ? grid : p.total;
+  p.grid = grid;  // 0: one CTA per resident slot
   p.token0 = token0;
   switch (groups) {
-    case 1: return launch_gemv_mg<1>(p, stream, pdl);
-    case 2: return launch_gemv_mg<2>(p, stream, pdl);
-    case 3: return launch_gemv_mg<3>(p, stream, pdl);
-    case 4: return launch_gemv_mg<4>(p, stream, pdl);
+    case 1: return launch_gemv_mg<1>(p, sm_count, stream, pdl);
+    case 2: return launch_gemv_mg<2>(p, sm_count, stream, pdl);
+    case 3: return launch_gemv_mg<3>(p, sm_count, stream, pdl);
+    case 4: return launch_gemv_mg<4>(p, sm_count, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
-size_t gemv_partials_bytes(int max_grid) {
-  return (size_t)max_grid * 2 * kGemvMaxGroups * kGemvComputeWarps * 32 * sizeof(float4);
+int gemv_max_grid(int sm_count) { return kGemvMaxCtasPerSm * sm_count; }
+
+size_t gemv_partials_bytes(int sm_count) {
+  return (size_t)gemv_max_grid(sm_count) * 2 * kGemvMaxGroups * kGemvComputeWarps * 32 * sizeof(float4);
 }
 
 }  // namespace s4

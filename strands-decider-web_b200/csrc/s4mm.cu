@@ -1,5 +1,6 @@
 // C ABI of libs4mm.so: context, weight handles, dispatcher, launches. Declarations and the
 // reference interfaces each entry point replaces are in include/s4mm.h.
+#include <algorithm>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
@@ -16,12 +17,15 @@ cudaError_t launch_repack(const uint8_t* packed, const __half* scales, uint32_t*
                           int nblk, int ktiles, int sm_count, cudaStream_t stream);
 cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
                         uint32_t* tickets, uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0,
-                        int groups, int grid, cudaStream_t stream, bool pdl);
-size_t gemv_partials_bytes(int max_grid);
+                        int groups, int grid, int sm_count, cudaStream_t stream, bool pdl);
+int gemv_max_grid(int sm_count);
+size_t gemv_partials_bytes(int sm_count);
 cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
 bool tc_available();
-cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, uint32_t* err, int M,
-                           int N, int K, int nblk, int ktiles, int tile_n, int sm_count, cudaStream_t stream);
+size_t tc_partials_bytes(int max_grid);
+cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
+                           uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
+                           int ktiles, int tile_n, int grid, cudaStream_t stream);
 }  // namespace s4
 
 namespace {
@@ -309,10 +313,11 @@ int s4_init(int device, s4_ctx** out) {
   if (!ctx) return fail(S4_ERR_NOMEM, "out of host memory");
   ctx->device = device;
   ctx->sm_count = prop.multiProcessorCount;
-  ctx->gemv_grid = prop.multiProcessorCount;
+  ctx->gemv_grid = s4::gemv_max_grid(prop.multiProcessorCount);
   ctx->table = default_table();
   e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->partials, s4::gemv_partials_bytes(ctx->gemv_grid));
+  const size_t part_bytes = std::max(s4::gemv_partials_bytes(ctx->sm_count), s4::tc_partials_bytes(ctx->sm_count));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->partials, part_bytes);
   if (e == cudaSuccess) e = cudaMalloc(&ctx->tickets, kMaxTickets * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->err, sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMemsetAsync(ctx->tickets, 0, kMaxTickets * sizeof(uint32_t), ctx->stream);
@@ -429,19 +434,30 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
   const Bucket b = choose(ctx, M);
   cudaError_t e = cudaSuccess;
   if (b.family == S4_FAMILY_TC) {
-    e = s4::launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->err, M, w->N,
-                           w->K, w->nblk, w->ktiles, b.tile, ctx->sm_count, st);
-    if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
-    ++ctx->launches;
+    if (b.tile != 0 && (b.tile < 16 || b.tile > 256 || b.tile % 16))
+      return fail(S4_ERR_INVALID, "tc tile must be a multiple of 16 in [16, 256] (got %d)", b.tile);
+    const int tn = b.tile > 0 ? b.tile : (M >= 256 ? 256 : ((M + 15) / 16) * 16);
+    // token rows per launch: the arrival counters hold one entry per (token block, n-block) tile
+    const long long rows_cap = (long long)(kMaxTickets / w->nblk) * tn;
+    const int grid = b.split > 0 ? std::min(b.split, ctx->sm_count) : ctx->sm_count;
+    for (long long r0 = 0; r0 < M; r0 += rows_cap) {
+      const int rows = (int)std::min<long long>(rows_cap, M - r0);
+      e = s4::launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x) + r0 * w->K,
+                             static_cast<__half*>(y) + r0 * w->N, ctx->partials, ctx->tickets, kMaxTickets, ctx->err,
+                             rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st);
+      if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
+      ++ctx->launches;
+    }
     return S4_OK;
   }
-  const int grid = b.split > 0 ? b.split : ctx->gemv_grid;
+  const int grid = b.split;  // 0: the kernel fills every resident slot
   if (grid > ctx->gemv_grid) return fail(S4_ERR_INVALID, "GEMV split %d exceeds the scratch for %d CTAs", grid, ctx->gemv_grid);
   for (int tok0 = 0; tok0 < M; tok0 += kGemvMaxM) {
     const int rem = M - tok0;
     const int groups = rem >= kGemvMaxM ? kGemvMaxM / 8 : (rem + 7) / 8;
     e = s4::launch_gemv(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->partials,
-                        ctx->tickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tok0, groups, grid, st, true);
+                        ctx->tickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tok0, groups, grid,
+                        ctx->sm_count, st, true);
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     ++ctx->launches;
   }
@@ -517,7 +533,7 @@ int s4_plan(s4_ctx* ctx, int M, int N, int K, int* family, int* tile, int* split
   const Bucket b = choose(ctx, M < 1 ? 1 : M);
   if (family) *family = b.family;
   if (tile) *tile = b.tile;
-  if (split) *split = b.split > 0 ? b.split : (b.family == S4_FAMILY_GEMV ? ctx->gemv_grid : 0);
+  if (split) *split = b.split;
   return S4_OK;
 }
 

@@ -1,0 +1,87 @@
+"""The tcgen05 GEMM family forced through the dispatcher: every token count, tile size and
+stream-K split must agree with the CPU oracle within the north-star tolerance (max relative
+error 2e-3, per-row cosine 0.99999)."""
+import numpy as np
+import pytest
+
+from oracle import s4ref
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _run(ctx, W, x):
+    y = ctx.matmul(torch.from_numpy(x).cuda(), W)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+def _check(y, ref, what):
+    ok, mr, mc = s4ref.check(y, ref)
+    assert ok, f"{what}: max_rel={mr:.3e} min_cos={mc:.7f}"
+
+
+@pytest.fixture(scope="module")
+def shapes(ctx):
+    rng = np.random.default_rng(77)
+    out = {}
+    for K, N in [(2048, 3072), (6144, 2048), (96, 200), (2048, 8224)]:
+        packed, scales = s4ref.config_weights(rng, K, N)
+        out[(K, N)] = (packed, scales, s4ref.dequant(packed, scales), ctx.upload(packed, scales, N, K))
+    return out
+
+
+@pytest.fixture
+def forced(ctx):
+    def f(tile=0, split=0):
+        ctx.force("tc", tile, split)
+    yield f
+    ctx.force("auto")
+
+
+@pytest.mark.parametrize("M", [1, 5, 16, 33, 100, 256, 257, 600])
+@pytest.mark.parametrize("KN", [(2048, 3072), (6144, 2048), (96, 200)])
+def test_tc_all_m(ctx, shapes, forced, KN, M):
+    packed, scales, deq, W = shapes[KN]
+    forced()
+    x = s4ref.config_x(np.random.default_rng(M + KN[0]), M, KN[0])
+    _, ref = s4ref.matmul(x, packed, scales, deq)
+    _check(_run(ctx, W, x), ref, f"tc K,N={KN} M={M}")
+
+
+@pytest.mark.parametrize("tile", [16, 64, 128, 256])
+def test_tc_tiles(ctx, shapes, forced, tile):
+    packed, scales, deq, W = shapes[(2048, 8224)]
+    forced(tile=tile)
+    x = s4ref.config_x(np.random.default_rng(tile), 300, 2048)
+    _, ref = s4ref.matmul(x, packed, scales, deq)
+    _check(_run(ctx, W, x), ref, f"tile={tile}")
+
+
+@pytest.mark.parametrize("split", [1, 3, 7, 64, 148])
+def test_tc_stream_k_splits(ctx, shapes, forced, split):
+    packed, scales, deq, W = shapes[(6144, 2048)]
+    forced(split=split)
+    x = s4ref.config_x(np.random.default_rng(split), 70, 6144)
+    _, ref = s4ref.matmul(x, packed, scales, deq)
+    _check(_run(ctx, W, x), ref, f"split={split}")
+
+
+def test_tc_deterministic(ctx, shapes, forced):
+    packed, scales, deq, W = shapes[(2048, 3072)]
+    forced()
+    x = s4ref.config_x(np.random.default_rng(3), 200, 2048)
+    a, b = _run(ctx, W, x), _run(ctx, W, x)
+    np.testing.assert_array_equal(a.view(np.uint16), b.view(np.uint16))
+
+
+def test_tc_and_gemv_agree(ctx, shapes):
+    packed, scales, deq, W = shapes[(2048, 3072)]
+    x = s4ref.config_x(np.random.default_rng(9), 24, 2048)
+    ctx.force("gemv")
+    a = _run(ctx, W, x)
+    ctx.force("tc")
+    b = _run(ctx, W, x)
+    ctx.force("auto")
+    _check(b, a.astype(np.float32), "tc vs gemv")
+    assert ctx.check_errors() == 0
