@@ -221,6 +221,8 @@ def run_ours(args, rank, world, local_rank):
                                 device_id=dev)
     pkg = load_pkg()
     ctx = pkg.Context(local_rank)
+    if args.family != "auto":
+        ctx.force(args.family)
     stream = torch.cuda.current_stream(dev)
 
     rng = np.random.default_rng(0)
@@ -419,6 +421,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--quick", action="store_true", help="skip the per-call breakdown")
+    ap.add_argument("--family", choices=["auto", "gemv", "tc"], default="auto",
+                    help="pin the kernel family instead of the dispatch table")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rules: at least 3 untimed warm-up steps
     rank = int(os.environ.get("RANK", "0"))

@@ -48,14 +48,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// try_wait with a suspend-time hint: a warp whose phase is not complete sleeps (up to the hint)
+// until the phase completes instead of spinning and taking issue slots from working warps.
+constexpr uint32_t kSuspendHintNs = 1000000u;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -63,9 +66,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, uint64_t deadline) {
   const uint32_t a = smem_u32(bar);
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(a, parity)) return true;
+    if (mbar_try_wait(a, parity)) return true;
     if (globaltimer_ns() > deadline) return false;
   }
 }
@@ -73,12 +74,10 @@ __device__ __forceinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(a, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+    if (mbar_try_wait(a, parity)) return true;
+    if (globaltimer_ns() > deadline) return false;
   }
 }
 
@@ -160,6 +159,14 @@ __device__ __forceinline__ void i4x8_to_h2x4_centered(uint32_t w, uint32_t (&h)[
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[1]) : "r"(t1), "r"(mul16), "r"(add72));
   asm("sub.f16x2 %0, %1, %2;" : "=r"(h[2]) : "r"(t2), "r"(sub1032));
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[3]) : "r"(t3), "r"(mul16), "r"(add72));
+}
+
+// Atomic add with release (orders this thread's, and by cumulativity its CTA's barrier-ordered,
+// earlier writes) and acquire (orders later reads) semantics at GPU scope.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 __device__ __forceinline__ void set_error(uint32_t* err, uint32_t bits) {

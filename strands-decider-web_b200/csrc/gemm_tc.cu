@@ -365,24 +365,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         mbar_arrive(acce + buf);
       }
       if (!full) {
-        __threadfence();
+        // barrier, then one release/acquire ticket by thread 0 (see the GEMV fix-up)
         named_bar_sync(2, 128);
         const int first = tc_cta_of(tile * KT, p), last = tc_cta_of(tile * KT + KT - 1, p);
         if (et == 0) {
-          const uint32_t prev = atomicAdd(p.tickets + tile, 1u);
+          const uint32_t prev = atom_add_acq_rel_gpu(p.tickets + tile, 1u);
           *s_flag = (prev == (uint32_t)(last - first)) ? 1 : 0;
         }
         named_bar_sync(2, 128);
         if (*s_flag) {
-          __threadfence();
           const int rows = min(p.tn, p.M - tok0);
-          for (int tl = 0; tl < rows; ++tl) {
-            float acc = 0.f;
+          // 16 tokens at a time: the loads of one CTA's partial are independent, and CTAs are
+          // summed in order (deterministic)
+          for (int t0 = 0; t0 < rows; t0 += 16) {
+            float acc[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[e] = 0.f;
             for (int b = first; b <= last; ++b) {
               const int bsel = (tc_begin(b, p) >= tile * KT) ? 0 : 1;
-              acc += __ldcg(p.partials + (((int64_t)b * 2 + bsel) * kTcMaxTn + tl) * 128 + nl);
+              const float* src = p.partials + (((int64_t)b * 2 + bsel) * kTcMaxTn + t0) * 128 + nl;
+              float v[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) v[e] = (t0 + e < rows) ? __ldcg(src + e * 128) : 0.f;
+#pragma unroll
+              for (int e = 0; e < 16; ++e) acc[e] += v[e];
             }
-            if (ncol < p.N) p.y[(int64_t)(tok0 + tl) * p.N + ncol] = __float2half_rn(acc);
+            if (ncol < p.N) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                if (t0 + e < rows) p.y[(int64_t)(tok0 + t0 + e) * p.N + ncol] = __float2half_rn(acc[e]);
+            }
           }
           named_bar_sync(2, 128);
           if (et == 0) atomicExch(p.tickets + tile, 0u);
@@ -427,7 +439,7 @@ size_t tc_partials_bytes(int max_grid) { return (size_t)max_grid * 2 * kTcMaxTn 
 // tile_n: requested tokens per tile (0 = automatic).
 cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
                            uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
-                           int ktiles, int tile_n, int grid, cudaStream_t stream) {
+                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   int tn = tile_n > 0 ? tile_n : (M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16);
@@ -479,7 +491,7 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, tc_gemm_kernel, p, tmap);

@@ -15,23 +15,23 @@
 namespace s4 {
 cudaError_t launch_repack(const uint8_t* packed, const __half* scales, uint32_t* wq, __half* ws, int N, int K,
                           int nblk, int ktiles, int sm_count, cudaStream_t stream);
-cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
-                        uint32_t* tickets, uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0,
-                        int groups, int grid, int sm_count, cudaStream_t stream, bool pdl);
-int gemv_max_grid(int sm_count);
-size_t gemv_partials_bytes(int sm_count);
+cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, uint32_t* err, int M, int N,
+                        int K, int nblk, int ktiles, int token0, int groups, int split, int sm_count,
+                        cudaStream_t stream, bool pdl);
+int gemv_max_split();
+int gemv_max_tokens();
 cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
 bool tc_available();
 size_t tc_partials_bytes(int max_grid);
 cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
                            uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
-                           int ktiles, int tile_n, int grid, cudaStream_t stream);
+                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl);
 }  // namespace s4
 
 namespace {
 
 constexpr int kMaxTickets = 1 << 16;  // n-blocks per weight: N <= 8,388,608
-constexpr int kGemvMaxM = 32;
+constexpr int kGemvMaxM = 16;  // tokens one GEMV launch covers (two 8-token mma column groups)
 
 thread_local std::string g_last_error;
 
@@ -84,7 +84,7 @@ struct s4_ctx {
   std::vector<Bucket> table;
   Bucket forced{0, S4_FAMILY_AUTO, 0, 0};
   uint64_t launches = 0;
-  int gemv_grid = 0;  // CTAs of a GEMV launch (default: one per SM)
+  bool pdl = true;    // launch with programmatic dependent launch (env S4_PDL=0 turns it off)
 };
 
 struct s4_weight {
@@ -98,8 +98,8 @@ struct s4_weight {
 namespace {
 
 std::vector<Bucket> default_table() {
-  // M-bucket table (replaces engine.js:17-33). GEMV up to 32 tokens; tcgen05 GEMM above when the
-  // kernel is built in, else repeated GEMV launches of 32 tokens.
+  // M-bucket table (replaces engine.js:17-33). GEMV up to 16 tokens; tcgen05 GEMM above when the
+  // kernel is built in, else repeated GEMV launches of 16 tokens.
   std::vector<Bucket> t;
   t.push_back({kGemvMaxM, S4_FAMILY_GEMV, 0, 0});
   t.push_back({INT_MAX, s4::tc_available() ? S4_FAMILY_TC : S4_FAMILY_GEMV, 0, 0});
@@ -313,10 +313,10 @@ int s4_init(int device, s4_ctx** out) {
   if (!ctx) return fail(S4_ERR_NOMEM, "out of host memory");
   ctx->device = device;
   ctx->sm_count = prop.multiProcessorCount;
-  ctx->gemv_grid = s4::gemv_max_grid(prop.multiProcessorCount);
   ctx->table = default_table();
+  if (const char* v = getenv("S4_PDL")) ctx->pdl = (v[0] != '0');
   e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
-  const size_t part_bytes = std::max(s4::gemv_partials_bytes(ctx->sm_count), s4::tc_partials_bytes(ctx->sm_count));
+  const size_t part_bytes = s4::tc_partials_bytes(ctx->sm_count);
   if (e == cudaSuccess) e = cudaMalloc(&ctx->partials, part_bytes);
   if (e == cudaSuccess) e = cudaMalloc(&ctx->tickets, kMaxTickets * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->err, sizeof(uint32_t));
@@ -444,20 +444,17 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
       const int rows = (int)std::min<long long>(rows_cap, M - r0);
       e = s4::launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x) + r0 * w->K,
                              static_cast<__half*>(y) + r0 * w->N, ctx->partials, ctx->tickets, kMaxTickets, ctx->err,
-                             rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st);
+                             rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
       ++ctx->launches;
     }
     return S4_OK;
   }
-  const int grid = b.split;  // 0: the kernel fills every resident slot
-  if (grid > ctx->gemv_grid) return fail(S4_ERR_INVALID, "GEMV split %d exceeds the scratch for %d CTAs", grid, ctx->gemv_grid);
   for (int tok0 = 0; tok0 < M; tok0 += kGemvMaxM) {
     const int rem = M - tok0;
     const int groups = rem >= kGemvMaxM ? kGemvMaxM / 8 : (rem + 7) / 8;
-    e = s4::launch_gemv(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->partials,
-                        ctx->tickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tok0, groups, grid,
-                        ctx->sm_count, st, true);
+    e = s4::launch_gemv(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->err, M, w->N,
+                        w->K, w->nblk, w->ktiles, tok0, groups, b.split, ctx->sm_count, st, ctx->pdl);
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     ++ctx->launches;
   }
@@ -543,8 +540,8 @@ int s4_force(s4_ctx* ctx, int family, int tile, int split) {
     return fail(S4_ERR_INVALID, "unknown family %d", family);
   if (family == S4_FAMILY_TC && !s4::tc_available()) return fail(S4_ERR_UNSUPPORTED, "tc family is not built");
   if (tile < 0 || split < 0) return fail(S4_ERR_INVALID, "tile and split must be >= 0");
-  if (family == S4_FAMILY_GEMV && split > ctx->gemv_grid)
-    return fail(S4_ERR_INVALID, "GEMV split %d exceeds %d", split, ctx->gemv_grid);
+  if (family == S4_FAMILY_GEMV && split > s4::gemv_max_split())
+    return fail(S4_ERR_INVALID, "GEMV split %d exceeds %d", split, s4::gemv_max_split());
   ctx->forced = Bucket{INT_MAX, family, tile, split};
   return S4_OK;
 }
@@ -555,8 +552,8 @@ int s4_set_table(s4_ctx* ctx, const char* json) {
   std::string why;
   if (!parse_table(json, t, why)) return fail(S4_ERR_INVALID, "dispatch table: %s", why.c_str());
   for (const Bucket& b : t)
-    if (b.family == S4_FAMILY_GEMV && b.split > ctx->gemv_grid)
-      return fail(S4_ERR_INVALID, "GEMV split %d exceeds %d", b.split, ctx->gemv_grid);
+    if (b.family == S4_FAMILY_GEMV && b.split > s4::gemv_max_split())
+      return fail(S4_ERR_INVALID, "GEMV split %d exceeds %d", b.split, s4::gemv_max_split());
   ctx->table = t;
   return S4_OK;
 }

@@ -153,7 +153,7 @@ def test_deterministic(ctx, weights):
     np.testing.assert_array_equal(a.view(np.uint16), b.view(np.uint16))
 
 
-@pytest.mark.parametrize("split", [1, 7, 64, 0])
+@pytest.mark.parametrize("split", [1, 3, 7, 16, 0])
 def test_forced_gemv_splits(ctx, weights, split):
     packed, scales, deq, W = weights["attn_qkv"]
     x = s4ref.config_x(np.random.default_rng(split), 5, 2048)
@@ -209,8 +209,8 @@ def test_silu_mul(ctx, M, I):
 def test_dispatch_table(pkg):
     c = pkg.Context(0)
     try:
-        c.set_table({"buckets": [{"max_m": 8, "family": "gemv", "split": 32}, {"max_m": 1 << 30, "family": "gemv"}]})
-        assert c.plan(4) == ("gemv", 0, 32)
+        c.set_table({"buckets": [{"max_m": 8, "family": "gemv", "split": 12}, {"max_m": 1 << 30, "family": "gemv"}]})
+        assert c.plan(4) == ("gemv", 0, 12)
         assert c.plan(100)[0] == "gemv"
         with pytest.raises(pkg.S4Error):
             c.set_table('{"buckets": [{"max_m": 8, "family": "nope"}]}')
