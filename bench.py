@@ -367,6 +367,46 @@ def run_ours(args, rank, world, local_rank):
                 gbs = alg_bytes(M, K, N) / (us * 1e-6) / 1e9
                 per[f"{name}/M{M}"] = {"us": round(us, 3), "GBps": round(gbs, 1), "frac": round(gbs / peaks()[0], 3)}
 
+    # ---- prefill / mid-M GEMMs (BASELINE configs 1 and 3), rank 0 ------------------------------------
+    prefill = {}
+    if rank == 0 and not args.quick:
+        hbm_pk, tc_pk, _ = peaks()
+        pre_shapes = {"down": (6144, 2048), "gate_up": (2048, 12288)}
+        pre_w = {}
+        for name, (K, N) in pre_shapes.items():
+            src = Ws[name] if name in Ws else None
+            pre_w[name] = src[:2]
+        for name, (K, N) in pre_shapes.items():
+            for M in (16, 64, 128, 512, 2048):
+                x = torch.from_numpy(s4ref.config_x(np.random.default_rng(M), M, K)).to(dev)
+                y = torch.empty((M, N), dtype=torch.float16, device=dev)
+                reps = 8 if M >= 512 else 32
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(cap_stream):
+                    for r in range(2):
+                        ctx.matmul(x, pre_w[name][r % 2], M, y, cap_stream)
+                    cap_stream.synchronize()
+                    with torch.cuda.graph(g, stream=cap_stream):
+                        for r in range(reps):
+                            ctx.matmul(x, pre_w[name][r % 2], M, y, cap_stream)
+                torch.cuda.synchronize(dev)
+                g.replay()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(3):
+                    g.replay()
+                b.record(stream)
+                torch.cuda.synchronize(dev)
+                us = a.elapsed_time(b) * 1e3 / (3 * reps)
+                flops = 2.0 * M * N * K
+                tfs = flops / (us * 1e-6) / 1e12
+                gbs = alg_bytes(M, K, N) / (us * 1e-6) / 1e9
+                fam = ctx.plan(M, N, K)[0]
+                prefill[f"{name}/M{M}"] = {"us": round(us, 2), "TFLOPs": round(tfs, 1), "GBps": round(gbs, 1),
+                                           "tensor_frac": round(tfs / tc_pk, 3), "hbm_frac": round(gbs / hbm_pk, 3),
+                                           "family": fam}
+                del g
+
     # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------------------------------
     hbm, bf16, peak_kind = peaks()
     cpu = None
@@ -402,6 +442,7 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks.summary(),
             "parity": {"ok": bool(ok_all), "max_rel": worst, "tol": s4ref.TOL_MAX_REL},
             "per_call": per,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     del graphs
