@@ -11,6 +11,10 @@
 
 #include "../../include/s4mm.h"
 #include "common.cuh"
+#include "internal.h"
+
+using s4::Bucket;
+using s4::DeviceGuard;
 
 namespace s4 {
 cudaError_t launch_repack(const uint8_t* packed, const __half* scales, uint32_t* wq, __half* ws, int N, int K,
@@ -45,55 +49,22 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+}  // namespace
+
+namespace s4 {
+int record_error(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+}  // namespace s4
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(S4_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
-struct Bucket {
-  int max_m;
-  int family;
-  int tile;
-  int split;
-};
-
-// Restores the caller's current device on scope exit.
-struct DeviceGuard {
-  int prev = -1;
-  bool ok = false;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
-  }
-  ~DeviceGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
-  }
-};
-
 }  // namespace
-
-struct s4_ctx {
-  int device = 0;
-  int sm_count = 0;
-  cudaStream_t stream = nullptr;  // used by the synchronous host-pointer calls
-  float* partials = nullptr;      // GEMV split-K partials
-  uint32_t* tickets = nullptr;    // GEMV n-block arrival counters (self-resetting)
-  uint32_t* err = nullptr;        // device error word
-  void* dx = nullptr;             // staging for s4_matmul_host
-  void* dy = nullptr;
-  size_t dx_cap = 0, dy_cap = 0;
-  std::vector<Bucket> table;
-  Bucket forced{0, S4_FAMILY_AUTO, 0, 0};
-  uint64_t launches = 0;
-  bool pdl = true;    // launch with programmatic dependent launch (env S4_PDL=0 turns it off)
-};
-
-struct s4_weight {
-  s4_ctx* ctx = nullptr;
-  int N = 0, K = 0, nblk = 0, ktiles = 0;
-  uint8_t* wq = nullptr;
-  uint8_t* ws = nullptr;
-  size_t wq_bytes = 0, ws_bytes = 0;
-};
 
 namespace {
 
