@@ -100,6 +100,17 @@ S4_API int s4_matmul_host(s4_ctx* ctx, const s4_weight* w, const uint16_t* x, in
 S4_API int s4_matmul_host_async(s4_ctx* ctx, const s4_weight* w, const uint16_t* x, int M, uint16_t* y,
                                 void* stream);
 
+/* y[M][N] = x[M][K] @ W^T like s4_matmul, for callers that cannot allocate device memory when they
+ * run a matmul (a host whose memory manager already owns the whole device, or a serving loop that
+ * must not take cudaMalloc's implicit device synchronisation). It needs no context-owned scratch:
+ * the tcgen05 split-K GEMM keeps its partials and tile counters in one static 8 MiB device array
+ * that every GPU loading this library holds until exit. It calls no allocator. Limit:
+ * ceil(M/256) * ceil(N/128) <= 16384 (larger calls are rejected with S4_ERR_INVALID); at most 31
+ * CTAs split the work. The first call on a device looks up the array's device address (do it
+ * before any stream capture). All calls share the array: calls that overlap on the GPU race.
+ * No counterpart in the reference. DEVICE pointers, asynchronous on `stream`. */
+S4_API int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, void* stream);
+
 /* mid[M][I] = silu(big[:, :I]) * big[:, I:2I], fp16 in/out, fp32 math, DEVICE pointers,
  * asynchronous. Replaces SILU_MUL (web/public/engine/wgsl.js:81-90). */
 S4_API int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, void* stream);

@@ -21,7 +21,10 @@
 // drain TMEM (double-buffered accumulators) and write the output.
 #include <cuda.h>
 
+#include <cstdio>
+
 #include "common.cuh"
+#include "internal.h"
 
 namespace s4 {
 
@@ -498,3 +501,71 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x
 }
 
 }  // namespace s4
+
+// ---- allocation-free entry point ------------------------------------------------------------------
+// Some callers cannot allocate device memory when they run a matmul: a host whose memory manager
+// already owns the device's whole budget, or a serving loop that must not take cudaMalloc's implicit
+// device-wide synchronisation. s4_matmul_noalloc gives them the tcgen05 split-K GEMM with its scratch
+// (split-K partials, tile arrival counters, error word) in the static array below instead of context
+// memory. Every GPU that loads this library holds the array until the process exits. All calls share
+// it, so calls that overlap on the GPU (different streams, or concurrent host threads) race.
+namespace {
+constexpr size_t kStaticScratchBytes = 8u << 20;                         // 8 MiB
+constexpr size_t kStaticTicketCount = 16384;                             // tile counters
+constexpr size_t kStaticErrOffset = kStaticTicketCount * sizeof(uint32_t);
+constexpr size_t kStaticPartialOffset = kStaticErrOffset + 256;
+constexpr size_t kStaticPartialBytes = kStaticScratchBytes - kStaticPartialOffset;
+constexpr size_t kPartialBytesPerCta = 2ull * s4::kTcMaxTn * 128 * sizeof(float);  // two slots of 256 x 128 fp32
+constexpr int kStaticMaxGrid = (int)(kStaticPartialBytes / kPartialBytesPerCta);
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_s4_static_scratch[kStaticScratchBytes];
+
+// Device address of g_s4_static_scratch per device; the symbol itself names a host-side stand-in.
+static void* g_static_scratch_addr[64];
+
+extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, void* stream) {
+  using namespace s4;
+  if (!w) return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: NULL weight");
+  if (M < 0) return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: M must be >= 0");
+  if (M == 0) return S4_OK;
+  if (!x || !y) return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: NULL x or y");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+    return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: x and y must be 16-byte aligned");
+  const int dev = w->ctx->device;
+  if (dev < 0 || dev >= 64) return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: device ordinal out of range");
+  const int tn = M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16;
+  const long long tiles = (long long)((M + tn - 1) / tn) * w->nblk;
+  if (tiles > (long long)kStaticTicketCount) {
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "s4_matmul_noalloc: M=%d, N=%d needs %lld (token block, n-block) tiles; the static scratch holds "
+             "%zu (ceil(M/256) * ceil(N/128) <= %zu)",
+             M, w->N, tiles, kStaticTicketCount, kStaticTicketCount);
+    return record_error(S4_ERR_INVALID, msg);
+  }
+  DeviceGuard guard(dev);
+  if (!guard.ok) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: cudaSetDevice failed");
+  if (!g_static_scratch_addr[dev]) {
+    // set-up, once per device, with that device current
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_s4_static_scratch);
+    if (e != cudaSuccess || !ptr)
+      return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: cudaGetSymbolAddress of the static scratch failed");
+    g_static_scratch_addr[dev] = ptr;
+  }
+  uint8_t* base = static_cast<uint8_t*>(g_static_scratch_addr[dev]);
+  uint32_t* tickets = reinterpret_cast<uint32_t*>(base);
+  uint32_t* err = reinterpret_cast<uint32_t*>(base + kStaticErrOffset);
+  float* partials = reinterpret_cast<float*>(base + kStaticPartialOffset);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the previous call left its counters at zero unless it failed part-way: clear what must start at zero
+  cudaError_t e = cudaMemsetAsync(base, 0, (size_t)tiles * sizeof(uint32_t), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(err, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: clearing the static scratch failed");
+  const int grid = w->ctx->sm_count < kStaticMaxGrid ? w->ctx->sm_count : kStaticMaxGrid;
+  e = launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
+                     (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true);
+  if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: tcgen05 GEMM launch failed");
+  return S4_OK;
+}

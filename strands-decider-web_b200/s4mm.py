@@ -45,6 +45,7 @@ _SIGS = {
     "s4_matmul": (C.c_int, [_P, _P, _P, C.c_int, _P, _P]),
     "s4_matmul_host": (C.c_int, [_P, _P, _P, C.c_int, _P]),
     "s4_matmul_host_async": (C.c_int, [_P, _P, _P, C.c_int, _P, _P]),
+    "s4_matmul_noalloc": (C.c_int, [_P, _P, C.c_int, _P, _P]),
     "s4_silu_mul": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
     "s4_plan": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int),
                           C.POINTER(C.c_int)]),
