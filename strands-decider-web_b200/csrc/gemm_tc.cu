@@ -12,13 +12,14 @@
 // Work: units (token block tb, n-block nb, k-tile kt) of 64 K, kt fastest; CTA b of G takes units
 // [b*U/G, (b+1)*U/G) (stream-K), so every SM gets the same number of MMAs whatever M, N and K are.
 // A run of units of one (tb, nb) tile is a segment; a segment that covers the whole K range is
-// written as fp16 directly, otherwise its fp32 partial goes to context scratch and the last CTA to
-// arrive at the tile (atomic ticket, no spinning) sums the partials in CTA order.
+// written as fp16 directly, otherwise its fp32 partial goes to scratch and a fix-up kernel launched
+// right after sums the partials of each split tile in CTA order (the allocation-free entry point
+// instead lets the last CTA to arrive at the tile do it, through an atomic ticket).
 //
-// Warp roles (384 threads): warp 0 lane 0 streams raw int4 chunks (1-D bulk copies) into a
+// Warp roles (512 threads): warp 0 lane 0 streams raw int4 chunks (1-D bulk copies) into a
 // 12-slot ring; warp 2 lane 0 loads activation tiles by TMA into a 3-stage ring; warp 1 owns TMEM
-// and lane 0 issues the MMAs; warps 4-7 dequantise int4 -> fp16 into the MMA's A stage; warps 8-11
-// drain TMEM (double-buffered accumulators) and write the output.
+// and lane 0 issues the MMAs; warps 4-11 dequantise int4 -> fp16 into the MMA's A stage; warps
+// 12-15 drain TMEM (double-buffered accumulators) and write the output.
 #include <cuda.h>
 
 #include <cstdio>
@@ -31,7 +32,9 @@ namespace s4 {
 constexpr int kTcMaxTn = 256;
 constexpr int kTcStagesA = 3;
 constexpr int kTcSlotsW = 12;
-constexpr int kTcThreads = 384;
+constexpr int kTcThreads = 512;
+constexpr int kTcDequantWarps = 8;  // warps 4..11
+constexpr int kTcEpiWarp0 = 12;     // warps 12..15 drain TMEM (lane quarter = warp % 4)
 constexpr int kTcXStageBytes = kTcMaxTn * 128;  // tn rows x 64 fp16
 constexpr int kTcAStageBytes = 128 * 128;       // 128 rows x 64 fp16
 constexpr int kTcWSlotBytes = kChunkWBytes + kChunkSBytes;
@@ -120,6 +123,9 @@ __device__ __forceinline__ int tc_cta_of(int u, const TcParams& p) {
   return (int)((((int64_t)u + 1) * p.grid - 1) / p.total);
 }
 
+// kTicketFixup: split tiles are finished inside this kernel by the last CTA to arrive (atomic
+// ticket); otherwise partials are only published and tc_fixup_kernel, launched next, sums them.
+template <bool kTicketFixup>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p, const __grid_constant__ CUtensorMap tmap_x) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -147,12 +153,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStagesA; ++s) {
       mbar_init(full_x + s, 1);
-      mbar_init(ddone + s, 4);
+      mbar_init(ddone + s, kTcDequantWarps);
       mbar_init(empty_a + s, 1);
     }
     for (int s = 0; s < kTcSlotsW; ++s) {
       mbar_init(full_w + s, 1);
-      mbar_init(empty_w + s, 4);
+      mbar_init(empty_w + s, kTcDequantWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf + b, 1);
@@ -270,7 +276,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       tc_commit(drain);  // completes when every MMA issued above has finished
       (void)mbar_wait(drain, 0);
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 4 && warp < 4 + kTcDequantWarps) {
     // ------------- dequantisers: int4 chunk -> fp16 A stage (128-byte swizzled, K-major) -------------
     const int d = threadIdx.x - 128;
     bool ok = true;
@@ -285,8 +291,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       const uint8_t* src = wraw + slot * kTcWSlotBytes;
       const uint32_t dst = smem_u32(wa + s * kTcAStageBytes);
 #pragma unroll
-      for (int rep = 0; rep < 2; ++rep) {
-        const int L = d + rep * 128;  // 16-byte lane slot of the chunk: sub-tile L / 32, lane L % 32
+      for (int rep = 0; rep < 256 / (32 * kTcDequantWarps); ++rep) {
+        const int L = d + rep * 32 * kTcDequantWarps;  // 16-byte lane slot: sub-tile L / 32, lane L % 32
         const int sub = L >> 5, ln = L & 31, g = ln >> 2, t = ln & 3;
         const uint4 v = *reinterpret_cast<const uint4*>(src + L * 16);
         const uint2 sc = *reinterpret_cast<const uint2*>(src + kChunkWBytes + sub * 64 + g * 8);
@@ -321,11 +327,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         mbar_arrive(empty_w + slot);
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= kTcEpiWarp0) {
     // ------------- epilogue: TMEM -> output (or fp32 partial + ticket fix-up) -------------
-    const int q = warp - 8;  // TMEM lane quarter this warp may access
+    const int q = warp - kTcEpiWarp0;  // TMEM lane quarter this warp may access (warp % 4)
     const int nl = q * 32 + lane;
-    const int et = threadIdx.x - 256;
+    const int et = threadIdx.x - kTcEpiWarp0 * 32;
     bool failed = false;
     int si = 0;
     for (int i = 0; i < n; ++si) {
@@ -367,8 +373,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         tc_fence_before();
         mbar_arrive(acce + buf);
       }
-      if (!full) {
-        // barrier, then one release/acquire ticket by thread 0 (see the GEMV fix-up)
+      if (kTicketFixup && !full) {
+        // barrier, then one release/acquire ticket by thread 0
         named_bar_sync(2, 128);
         const int first = tc_cta_of(tile * KT, p), last = tc_cta_of(tile * KT + KT - 1, p);
         if (et == 0) {
@@ -416,6 +422,52 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   }
 }
 
+// Sums the published fp32 partials of every split tile in CTA order and writes fp16 (the REDUCE step,
+// kernels.js:269-282, fp32 throughout). CTA (b, row group) handles the tile that GEMM CTA b's range
+// starts inside of, when b is that tile's second CTA, so every split tile is done exactly once.
+__global__ void __launch_bounds__(128) tc_fixup_kernel(const TcParams p) {
+  pdl_wait();  // the partials come from the GEMM launched just before
+  const int b = blockIdx.x, KT = p.ktiles;
+  const int cb = tc_begin(b, p);
+  if (b == 0 || cb % KT == 0) return;
+  const int tile = cb / KT;
+  if (tc_cta_of(tile * KT, p) != b - 1) return;
+  const int first = b - 1, last = tc_cta_of(tile * KT + KT - 1, p);
+  const int tb = tile / p.nblk, nb = tile - tb * p.nblk;
+  const int tok0 = tb * p.tn;
+  const int rows = min(p.tn, p.M - tok0);
+  const int r0 = blockIdx.y * 8;
+  if (r0 >= rows) return;
+  const int nl = threadIdx.x, ncol = nb * 128 + nl;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  for (int b0 = first; b0 <= last; b0 += 4) {
+    float v[4][8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int bb = b0 + j;
+      if (bb <= last) {
+        const int bsel = (tc_begin(bb, p) >= tile * KT) ? 0 : 1;
+        const float* src = p.partials + (((int64_t)bb * 2 + bsel) * kTcMaxTn + r0) * 128 + nl;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[j][e] = (r0 + e < rows) ? __ldcg(src + e * 128) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (b0 + j <= last) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += v[j][e];
+      }
+  }
+  if (ncol < p.N) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (r0 + e < rows) p.y[(int64_t)(tok0 + r0 + e) * p.N + ncol] = __float2half_rn(acc[e]);
+  }
+}
+
 // ---- host side -------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -442,7 +494,7 @@ size_t tc_partials_bytes(int max_grid) { return (size_t)max_grid * 2 * kTcMaxTn 
 // tile_n: requested tokens per tile (0 = automatic).
 cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
                            uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
-                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl) {
+                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl, bool ticket_fixup) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   int tn = tile_n > 0 ? tile_n : (M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16);
@@ -483,7 +535,9 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    e = cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
@@ -497,7 +551,18 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, tc_gemm_kernel, p, tmap);
+  if (ticket_fixup) return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<true>, p, tmap);
+  e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<false>, p, tmap);
+  if (e != cudaSuccess) return e;
+  // any CTA whose range starts inside a tile leaves that tile split
+  bool split = false;
+  for (int b = 1; b < p.grid && !split; ++b) split = ((((int64_t)b * p.total) / p.grid) % ktiles) != 0;
+  if (!split) return cudaSuccess;
+  cudaLaunchConfig_t fcfg = cfg;
+  fcfg.gridDim = dim3(p.grid, (p.tn + 7) / 8, 1);
+  fcfg.blockDim = dim3(128, 1, 1);
+  fcfg.dynamicSmemBytes = 0;
+  return cudaLaunchKernelEx(&fcfg, tc_fixup_kernel, p);
 }
 
 }  // namespace s4
@@ -565,7 +630,7 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: clearing the static scratch failed");
   const int grid = w->ctx->sm_count < kStaticMaxGrid ? w->ctx->sm_count : kStaticMaxGrid;
   e = launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
-                     (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true);
+                     (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true, true);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: tcgen05 GEMM launch failed");
   return S4_OK;
 }

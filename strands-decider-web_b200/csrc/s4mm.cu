@@ -29,7 +29,7 @@ bool tc_available();
 size_t tc_partials_bytes(int max_grid);
 cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
                            uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
-                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl);
+                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl, bool ticket_fixup);
 }  // namespace s4
 
 namespace {
@@ -415,7 +415,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
       const int rows = (int)std::min<long long>(rows_cap, M - r0);
       e = s4::launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x) + r0 * w->K,
                              static_cast<__half*>(y) + r0 * w->N, ctx->partials, ctx->tickets, kMaxTickets, ctx->err,
-                             rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl);
+                             rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl, false);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
       ++ctx->launches;
     }
