@@ -453,6 +453,126 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+def run_stack(args, rank, world, local_rank):
+    """Configs 4 and 5 on the 24-layer linear stack (strands-decider-web_b200/serve.py)."""
+    import datetime
+    import importlib
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    pkg = load_pkg()
+    serve = importlib.import_module("strands_decider_web_b200.serve")
+    ctx = pkg.Context(local_rank)
+    stream = torch.cuda.current_stream(dev)
+    flops_tok = serve.stack_flops_per_token()
+    _, tc_peak, peak_kind = peaks()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    gather_ms = [0.0]
+    if args.workload == "stack":
+        stack = serve.CudaStack(ctx, rank=rank, world=world)
+        x = torch.from_numpy(np.random.default_rng(0).standard_normal((2048, serve.HIDDEN)).astype(np.float16)).to(dev)
+        timing = {"on": False}
+
+        def timers(kind, fn):
+            if not timing["on"]:
+                return fn()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            out = fn()
+            b.record(stream)
+            timing["events"].append((a, b))
+            return out
+
+        def step():
+            return stack.forward(x, timers=timers)
+        tokens_per_step = 2048 * 1  # the prompt, whatever the number of ranks (strong scaling)
+        label = "config4_stack_2048_prompt_colshard"
+    else:
+        stack = serve.CudaStack(ctx)  # weights replicated on every rank
+        lengths = serve.request_lengths(4096)[: args.requests]
+        mine = serve.lpt_shard(lengths, world)[rank]
+        chunks = serve.pack_chunks(lengths[mine], 8192)
+        xs = []
+        g = torch.Generator(device=dev)
+        g.manual_seed(1234 + rank)
+        for c in chunks:
+            n = int(lengths[mine][c].sum())
+            xs.append(torch.randn((n, serve.HIDDEN), generator=g, device=dev).to(torch.float16))
+
+        def step():
+            for xc in xs:
+                stack.forward(xc)
+        tokens_per_step = int(lengths.sum())
+        label = f"config5_serve_{args.requests}_requests_lpt"
+        timers = None
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ctx.launch_count
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        if args.workload == "stack":
+            timing.update(on=True, events=[])
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    launches = ctx.launch_count - launches0
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    comm_share = None
+    if args.workload == "stack" and world > 1:
+        gather_ms = sum(a.elapsed_time(b) for a, b in timing["events"])
+        comm_share = max_over_ranks(gather_ms) / ms
+    tok_s = tokens_per_step * args.steps / (ms / 1e3)
+    tflops = tok_s * flops_tok / 1e12
+    if ctx.check_errors():
+        raise RuntimeError("device error word set during the stack run")
+    if rank == 0:
+        line = {
+            "metric": "prefill tokens/s through the 24-layer int4 linear stack",
+            "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": label, "layers": 24, "hidden": serve.HIDDEN, "intermediate": serve.INTER,
+                       "parallelism": (f"colshard{world} (NCCL all-gather after every projection)"
+                                       if args.workload == "stack" else f"dp{world} (LPT request sharding, no collective)"),
+                       "l2": "weights 758 MB > L2"},
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": tflops / tc_peak, "traffic": None, "peak_kind": peak_kind,
+                         "note": "whole-stack FLOP rate (2 x weight parameters per token), all kernels included"},
+            "gather_share": comm_share,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -464,6 +584,12 @@ def main():
     ap.add_argument("--quick", action="store_true", help="skip the per-call breakdown")
     ap.add_argument("--family", choices=["auto", "gemv", "tc"], default="auto",
                     help="pin the kernel family instead of the dispatch table")
+    ap.add_argument("--workload", choices=["decode", "stack", "serve"], default="decode",
+                    help="decode: configs[1] GEMV sweep (default); stack: config 4, one 2048-token prompt "
+                         "through the 24-layer linear stack, column-sharded over the ranks; serve: config 5, "
+                         "requests sharded over the ranks (weights replicated)")
+    ap.add_argument("--requests", type=int, default=512,
+                    help="serve: number of config-5 requests timed per step (the first n of the seeded 4096)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rules: at least 3 untimed warm-up steps
     rank = int(os.environ.get("RANK", "0"))
@@ -474,6 +600,8 @@ def main():
         return 2
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload in ("stack", "serve"):
+        return run_stack(args, rank, world, local_rank)
     return run_ours(args, rank, world, local_rank)
 
 

@@ -1,0 +1,220 @@
+"""The 24-layer linear stack of BASELINE configs 4 and 5, and its two multi-GPU modes.
+
+The stack is the int4 part of the engine's per-layer step list (``plan()``, web/public/engine/
+engine.js:253-282): every layer runs its fused input projection (linear-attention qkv|z|a|b, K=2048,
+N=8224, or attention q|k|v, N=3072), the out projection (2048 -> 2048), the MLP gate|up (2048 ->
+12288), SiLU*mul (wgsl.js:81-90) and down (6144 -> 2048); layers follow the 3:1 pattern of the
+hybrid decoder (three linear-attention layers, then one attention layer). The non-linear-path
+operators between them (norms, conv, recurrence, attention) are outside this path; the synthetic
+wiring that replaces them is: the out projection reads columns [0, 2048) of the input projection's
+output, gate|up reads the out projection's output, and the down output is added to the layer input
+as an fp16 residual.
+
+Multi-GPU (one process per GPU, ``torch.distributed``):
+
+* data-parallel serving (config 5): independent requests are assigned to ranks by longest-
+  processing-time order (:func:`lpt_shard`); every rank holds all weights; there is no collective.
+* column-sharded prefill (config 4): each rank holds an N/g slice of every projection's output
+  rows (gate and up slices kept together so SiLU*mul stays local) and the slices are all-gathered
+  after every projection (:class:`ShardedStack`).
+
+The sharding logic takes its matmul / SiLU*mul / all-gather as callables, so the same code runs on
+the CUDA kernels with NCCL and on CPU ranks with gloo in the tests.
+"""
+from __future__ import annotations
+
+import heapq
+from dataclasses import dataclass
+
+import numpy as np
+
+HIDDEN = 2048
+INTER = 6144
+N_LINEAR_IN = 8224   # qkv | z | a | b of a linear-attention layer (export_engine.py:52-53, unpadded)
+N_ATTN_IN = 3072     # q | k | v of an attention layer: 16 q + 4 kv heads x 128 (export_engine.py:61-62)
+N_LAYERS = 24
+
+
+def layer_kinds(n_layers: int = N_LAYERS):
+    """``linear`` x3 then ``attn``, repeated (the 18 + 6 hybrid pattern)."""
+    return ["attn" if (i % 4) == 3 else "linear" for i in range(n_layers)]
+
+
+def projection_shapes(kind: str):
+    """(name, K, N) of the four int4 projections of one layer, in call order."""
+    n_in = N_LINEAR_IN if kind == "linear" else N_ATTN_IN
+    return [("in_proj", HIDDEN, n_in), ("out_proj", HIDDEN, HIDDEN), ("gate_up", HIDDEN, 2 * INTER), ("down", INTER, HIDDEN)]
+
+
+def stack_flops_per_token(n_layers: int = N_LAYERS) -> float:
+    """2 * (weight parameters of the stack): multiply-adds per token of the linear path."""
+    return 2.0 * sum(K * N for kind in layer_kinds(n_layers) for _, K, N in projection_shapes(kind))
+
+
+# --------------------------------------------------------------------------------------------------
+# request sharding for data-parallel serving
+# --------------------------------------------------------------------------------------------------
+def lpt_shard(lengths, world: int):
+    """Longest-processing-time assignment of requests to ``world`` ranks by token count.
+
+    Requests are taken longest first (ties by index) and each goes to the currently least-loaded
+    rank (ties by rank). Returns a list of index lists, one per rank, each in ascending order.
+    Deterministic; the max load is within one request of the mean (LPT's 4/3 bound in general)."""
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    heap = [(0, r) for r in range(world)]
+    heapq.heapify(heap)
+    out = [[] for _ in range(world)]
+    for i in order:
+        load, r = heapq.heappop(heap)
+        out[r].append(i)
+        heapq.heappush(heap, (load + int(lengths[i]), r))
+    return [sorted(v) for v in out]
+
+
+def request_lengths(n: int = 4096, lo: int = 64, hi: int = 2048, seed: int = 0):
+    """Config-5 request lengths: uniform integers in [lo, hi], numpy default_rng(seed)."""
+    return np.random.default_rng(seed).integers(lo, hi + 1, n)
+
+
+def pack_chunks(lengths, max_tokens: int):
+    """Group a rank's requests into chunks of at most ``max_tokens`` tokens (a request is never
+    split: the stack is row-independent, so packing only changes M). Returns lists of indices."""
+    chunks, cur, cur_tok = [], [], 0
+    for i, n in enumerate(lengths):
+        if cur and cur_tok + n > max_tokens:
+            chunks.append(cur)
+            cur, cur_tok = [], 0
+        cur.append(i)
+        cur_tok += int(n)
+    if cur:
+        chunks.append(cur)
+    return chunks
+
+
+# --------------------------------------------------------------------------------------------------
+# column sharding
+# --------------------------------------------------------------------------------------------------
+def shard_rows(name: str, N: int, rank: int, world: int):
+    """Row indices (output columns) of projection ``name`` held by ``rank``.
+
+    Every projection is split into ``world`` equal contiguous slices, except gate|up, whose rank
+    slice is (gate slice) followed by (the matching up slice), so SiLU*mul runs on local data."""
+    if name == "gate_up":
+        inter = N // 2
+        assert inter % world == 0
+        s = inter // world
+        return np.concatenate([np.arange(rank * s, (rank + 1) * s), inter + np.arange(rank * s, (rank + 1) * s)])
+    assert N % world == 0, f"{name}: N={N} not divisible by {world}"
+    s = N // world
+    return np.arange(rank * s, (rank + 1) * s)
+
+
+def gathered_to_rows(g, M: int, world: int, ns: int):
+    """All-gather output [world][M][ns] (rank-major) -> [M][world * ns]."""
+    return g.reshape(world, M, ns).transpose(1, 0, 2).reshape(M, world * ns) if isinstance(g, np.ndarray) else \
+        g.view(world, M, ns).permute(1, 0, 2).reshape(M, world * ns)
+
+
+@dataclass
+class Ops:
+    """The operators a stack forward needs; CUDA kernels + NCCL, or the CPU oracle + gloo."""
+    matmul: object      # (x [M,K] f16, weight handle) -> y [M,N] f16
+    silu_mul: object    # (big [M, 2I] f16, I) -> mid [M, I] f16
+    all_gather: object  # (local [M, ns]) -> [world][M][ns] stacked (None when world == 1)
+    add: object         # (a, b) -> a + b (fp16 residual)
+    cols: object        # (x, c0, c1) -> contiguous x[:, c0:c1]
+
+
+def stack_forward(x, layers, ops: Ops, world: int = 1, timers=None):
+    """Run the linear stack on activations ``x`` [M, 2048] (fp16).
+
+    ``layers`` is a list of dicts name -> weight handle (the rank's shard when ``world`` > 1).
+    ``timers``, if given, is called as timers("gather", fn) around every all-gather."""
+    M = x.shape[0]
+
+    def gather(local):
+        if world == 1:
+            return local
+        ns = local.shape[1]
+        g = timers("gather", lambda: ops.all_gather(local)) if timers else ops.all_gather(local)
+        return gathered_to_rows(g, M, world, ns)
+
+    for w in layers:
+        a = gather(ops.matmul(x, w["in_proj"]))
+        b = gather(ops.matmul(ops.cols(a, 0, HIDDEN), w["out_proj"]))
+        gu = ops.matmul(b, w["gate_up"])
+        mid = gather(ops.silu_mul(gu, gu.shape[1] // 2))
+        d = gather(ops.matmul(mid, w["down"]))
+        x = ops.add(x, d)
+    return x
+
+
+# --------------------------------------------------------------------------------------------------
+# synthetic weights (nibbles uniform, fp16 scales |N(0, 0.02)| / 7)
+# --------------------------------------------------------------------------------------------------
+def synthetic_projection(seed: int, K: int, N: int):
+    """MatMulNBits bytes of one projection (numpy), from its own seed."""
+    rng = np.random.default_rng(seed)
+    q = rng.integers(0, 16, size=(N, K // 32, 32), dtype=np.uint8)
+    packed = (q[..., 0::2] | (q[..., 1::2] << 4)).astype(np.uint8)
+    scales = (np.abs(rng.standard_normal((N, K // 32)) * 0.02) / 7.0).astype(np.float16)
+    return packed, scales
+
+
+def synthetic_projection_torch(seed: int, K: int, N: int, device):
+    """Same distribution, generated on the GPU (fast for the 758 MB stack); returns torch tensors."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    packed = torch.randint(0, 256, (N, K // 32, 16), dtype=torch.uint8, device=device, generator=g)
+    scales = (torch.randn((N, K // 32), device=device, generator=g).abs() * (0.02 / 7.0)).to(torch.float16)
+    return packed, scales
+
+
+def projection_seed(layer: int, name: str) -> int:
+    return 1000 * (layer + 1) + ["in_proj", "out_proj", "gate_up", "down"].index(name)
+
+
+class CudaStack:
+    """The stack's weights uploaded through the C ABI, optionally as this rank's column shard."""
+
+    def __init__(self, ctx, n_layers: int = N_LAYERS, rank: int = 0, world: int = 1, device=None, host_gen=False):
+        import torch
+        self.ctx, self.rank, self.world = ctx, rank, world
+        self.device = device or torch.device("cuda", ctx.device)
+        self.layers = []
+        self.n_layers = n_layers
+        for li, kind in enumerate(layer_kinds(n_layers)):
+            ws = {}
+            for name, K, N in projection_shapes(kind):
+                seed = projection_seed(li, name)
+                if host_gen:
+                    packed, scales = synthetic_projection(seed, K, N)
+                    packed, scales = torch.from_numpy(packed).to(self.device), torch.from_numpy(scales).to(self.device)
+                else:
+                    packed, scales = synthetic_projection_torch(seed, K, N, self.device)
+                if world > 1:
+                    rows = torch.from_numpy(shard_rows(name, N, rank, world)).to(self.device)
+                    packed, scales = packed.index_select(0, rows).contiguous(), scales.index_select(0, rows).contiguous()
+                ws[name] = ctx.upload(packed, scales, packed.shape[0], K)
+                del packed, scales
+            self.layers.append(ws)
+
+    def ops(self, group=None):
+        import torch
+        import torch.distributed as dist
+        ctx, world = self.ctx, self.world
+
+        def all_gather(local):
+            out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+            dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+            return out
+
+        return Ops(matmul=lambda x, w: ctx.matmul(x, w),
+                   silu_mul=lambda big, I: ctx.silu_mul(big, I),
+                   all_gather=all_gather,
+                   add=lambda a, b: a + b,
+                   cols=lambda x, c0, c1: x[:, c0:c1].contiguous())
+
+    def forward(self, x, group=None, timers=None):
+        return stack_forward(x, self.layers, self.ops(group), self.world, timers)
