@@ -486,8 +486,13 @@ def run_stack(args, rank, world, local_rank):
         return float(t.item())
 
     gather_ms = [0.0]
+    fused = None
     if args.workload == "stack":
-        stack = serve.CudaStack(ctx, rank=rank, world=world)
+        if args.gather == "fused":
+            fused = serve.FusedColshardStack(ctx, None, rank, world)
+            stack = fused.stack
+        else:
+            stack = serve.CudaStack(ctx, rank=rank, world=world)
         x = torch.from_numpy(np.random.default_rng(0).standard_normal((2048, serve.HIDDEN)).astype(np.float16)).to(dev)
         timing = {"on": False}
 
@@ -502,9 +507,11 @@ def run_stack(args, rank, world, local_rank):
             return out
 
         def step():
+            if fused is not None:
+                return fused.forward(x)
             return stack.forward(x, timers=timers)
         tokens_per_step = 2048 * 1  # the prompt, whatever the number of ranks (strong scaling)
-        label = "config4_stack_2048_prompt_colshard"
+        label = f"config4_stack_2048_prompt_colshard_{args.gather}"
     else:
         stack = serve.CudaStack(ctx)  # weights replicated on every rank
         lengths = serve.request_lengths(4096)[: args.requests]
@@ -555,7 +562,8 @@ def run_stack(args, rank, world, local_rank):
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
             "config": {"workload": label, "layers": 24, "hidden": serve.HIDDEN, "intermediate": serve.INTER,
-                       "parallelism": (f"colshard{world} (NCCL all-gather after every projection)"
+                       "parallelism": ((f"colshard{world} (all-gathers fused into the GEMM/SiLU epilogues, NVLink peer stores)"
+                                        if args.gather == "fused" else f"colshard{world} (NCCL all-gather after every projection)")
                                        if args.workload == "stack" else f"dp{world} (LPT request sharding, no collective)"),
                        "l2": "weights 758 MB > L2"},
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s",
@@ -566,6 +574,8 @@ def run_stack(args, rank, world, local_rank):
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    if fused is not None:
+        fused.close()
     ctx.close()
     if world > 1:
         dist.barrier()
@@ -588,6 +598,9 @@ def main():
                     help="decode: configs[1] GEMV sweep (default); stack: config 4, one 2048-token prompt "
                          "through the 24-layer linear stack, column-sharded over the ranks; serve: config 5, "
                          "requests sharded over the ranks (weights replicated)")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="stack: fuse the all-gathers into the producing kernels (peer stores over NVLink) or "
+                         "call NCCL all-gather after every projection")
     ap.add_argument("--requests", type=int, default=512,
                     help="serve: number of config-5 requests timed per step (the first n of the seeded 4096)")
     args = ap.parse_args()

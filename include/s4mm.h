@@ -40,7 +40,7 @@ extern "C" {
 
 /* Kernel families of the dispatcher (s4_force / s4_plan). */
 #define S4_FAMILY_AUTO 0
-#define S4_FAMILY_GEMV 1      /* decode GEMV, M <= 32: stream-K over the weight bytes */
+#define S4_FAMILY_GEMV 1      /* decode GEMV, M <= 16: cluster split-K over the weight bytes */
 #define S4_FAMILY_TC 2        /* tcgen05 GEMM, weights dequantised to fp16 in shared memory */
 
 typedef struct s4_ctx s4_ctx;
@@ -114,6 +114,37 @@ S4_API int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, 
 /* mid[M][I] = silu(big[:, :I]) * big[:, I:2I], fp16 in/out, fp32 math, DEVICE pointers,
  * asynchronous. Replaces SILU_MUL (web/public/engine/wgsl.js:81-90). */
 S4_API int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, void* stream);
+
+/* ---- column-sharded prefill over NVLink (one process per GPU on one node) ----
+ * Each rank computes an N/g slice of every projection and writes it straight into every rank's
+ * gathered output buffer through peer mappings (the all-gather fused into the GEMM epilogue; the
+ * north star's NCCL all-gather of outputs, engine calls engine.js:257-281, sharded). */
+
+/* A device buffer of its own cudaMalloc allocation, so that peers can map it (s4_ipc_*). Zeroed. */
+S4_API int s4_buffer_alloc(s4_ctx* ctx, size_t bytes, void** ptr);
+S4_API int s4_buffer_free(s4_ctx* ctx, void* ptr);
+
+/* CUDA IPC: export a buffer from s4_buffer_alloc as a 64-byte handle; map a peer's handle on the
+ * context's device; unmap. Plain peer mappings (no multicast objects). */
+S4_API int s4_ipc_handle(s4_ctx* ctx, const void* ptr, void* handle64);
+S4_API int s4_ipc_open(s4_ctx* ctx, const void* handle64, void** ptr);
+S4_API int s4_ipc_close(s4_ctx* ctx, void* ptr);
+
+/* y = x @ W^T (tcgen05 GEMM) with x of row stride ldx (elements, ldx >= K, ldx*2 % 16 == 0), the
+ * result written to each of ndst (<= 8) buffers at dst[d][m * ldy + col0 + n] (this rank's column
+ * slice of every rank's gathered buffer; the pointers may be peer mappings). Asynchronous. */
+S4_API int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, int M, void* const* dst,
+                            int ndst, int ldy, int col0, void* stream);
+
+/* SiLU*mul of this rank's gate|up slice big[M][2*Is] written to dst[d][m * ldd + col0 + j]
+ * (Is, ldd, col0 multiples of 8; 16-byte aligned buffers). Asynchronous. */
+S4_API int s4_silu_mul_gather(s4_ctx* ctx, const void* big, int M, int Is, void* const* dst, int ndst, int ldd,
+                              int col0, void* stream);
+
+/* Barrier across nranks GPUs: flags[q] is rank q's flag array (>= 8 uint32, zeroed, peer-mapped);
+ * every rank passes the same increasing epoch. A wait that exceeds 1 s sets the context's error
+ * word (s4_check_errors) instead of hanging. Asynchronous on `stream`. */
+S4_API int s4_peer_barrier(s4_ctx* ctx, void* const* flags, int nranks, int rank, uint32_t epoch, void* stream);
 
 /* Dispatcher. s4_plan reports the (family, tile, split) s4_matmul will use for M on an
  * (N, K) weight; replaces matmulKernel(M) (engine.js:17-33). s4_force pins a choice for every

@@ -47,10 +47,15 @@ constexpr int kTcOffMisc = kTcOffBar + kTcNumBars * 8;
 constexpr size_t kTcSmem = (size_t)kTcOffMisc + 64 + 1024;  // + alignment slack
 constexpr uint32_t kTcTmemCols = 512;                       // two 256-column accumulators
 
+constexpr int kTcMaxDst = 8;  // output copies one launch writes (this GPU + peers)
+
 struct TcParams {
   const uint8_t* wq;
   const uint8_t* ws;
-  __half* y;
+  __half* ydst[kTcMaxDst];  // output buffers: y[tok * ldy + ycol0 + n] is written to each
+  int ndst;
+  int64_t ldy;
+  int ycol0;
   float* partials;    // [G][2][256][128] fp32
   uint32_t* tickets;  // [ntb * nblk]
   uint32_t* err;
@@ -61,6 +66,14 @@ struct TcParams {
   int total;  // units = ntb * nblk * ktiles
   int grid;
 };
+
+// One output element to every destination (local buffer and, for the column-sharded prefill, the
+// peers' gathered buffers over NVLink).
+__device__ __forceinline__ void tc_store(const TcParams& p, int tok, int ncol, float v) {
+  const __half h = __float2half_rn(v);
+  const int64_t off = (int64_t)tok * p.ldy + p.ycol0 + ncol;
+  for (int d = 0; d < p.ndst; ++d) p.ydst[d][off] = h;
+}
 
 // ---- tcgen05 / TMA wrappers -----------------------------------------------------------------------
 __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
@@ -362,7 +375,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
 #pragma unroll
               for (int e = 0; e < 16; ++e) {
                 const int tok = tok0 + cb + e;
-                if (tok < p.M) p.y[(int64_t)tok * p.N + ncol] = __float2half_rn(v[e]);
+                if (tok < p.M) tc_store(p, tok, ncol, v[e]);
               }
             }
           } else {
@@ -402,7 +415,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
             if (ncol < p.N) {
 #pragma unroll
               for (int e = 0; e < 16; ++e)
-                if (t0 + e < rows) p.y[(int64_t)(tok0 + t0 + e) * p.N + ncol] = __float2half_rn(acc[e]);
+                if (t0 + e < rows) tc_store(p, tok0 + t0 + e, ncol, acc[e]);
             }
           }
           named_bar_sync(2, 128);
@@ -464,7 +477,7 @@ __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcParams p) {
   if (ncol < p.N) {
 #pragma unroll
     for (int e = 0; e < 8; ++e)
-      if (r0 + e < rows) p.y[(int64_t)(tok0 + r0 + e) * p.N + ncol] = __float2half_rn(acc[e]);
+      if (r0 + e < rows) tc_store(p, tok0 + r0 + e, ncol, acc[e]);
   }
 }
 
@@ -492,17 +505,24 @@ bool tc_available() { return true; }
 size_t tc_partials_bytes(int max_grid) { return (size_t)max_grid * 2 * kTcMaxTn * 128 * sizeof(float); }
 
 // tile_n: requested tokens per tile (0 = automatic).
-cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
-                           uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
-                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl, bool ticket_fixup) {
+// General form: x has row stride ldx (elements); the output goes to ndst buffers with row stride ldy,
+// starting at column ycol0 (a rank's slice of a gathered buffer).
+cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half* x, int64_t ldx, __half* const* ydst,
+                              int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
+                              uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
+                              cudaStream_t stream, bool pdl, bool ticket_fixup) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   int tn = tile_n > 0 ? tile_n : (M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16);
   if (tn < 16 || tn > kTcMaxTn || tn % 16) return cudaErrorInvalidValue;
+  if (ndst < 1 || ndst > kTcMaxDst || ldx < K || (ldx * 2) % 16 != 0) return cudaErrorInvalidValue;
   TcParams p;
   p.wq = wq;
   p.ws = ws;
-  p.y = y;
+  for (int d = 0; d < kTcMaxDst; ++d) p.ydst[d] = d < ndst ? ydst[d] : nullptr;
+  p.ndst = ndst;
+  p.ldy = ldy;
+  p.ycol0 = ycol0;
   p.partials = partials;
   p.tickets = tickets;
   p.err = err;
@@ -521,7 +541,7 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x
 
   CUtensorMap tmap;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
   cuuint32_t box[2] = {64u, (cuuint32_t)tn};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x), dims, strides, box, estr,
@@ -563,6 +583,14 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x
   fcfg.blockDim = dim3(128, 1, 1);
   fcfg.dynamicSmemBytes = 0;
   return cudaLaunchKernelEx(&fcfg, tc_fixup_kernel, p);
+}
+
+cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
+                           uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
+                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl, bool ticket_fixup) {
+  __half* dst[1] = {y};
+  return launch_tc_gemm_ex(wq, ws, x, K, dst, 1, N, 0, partials, tickets, max_tickets, err, M, N, K, nblk, ktiles,
+                           tile_n, grid, stream, pdl, ticket_fixup);
 }
 
 }  // namespace s4

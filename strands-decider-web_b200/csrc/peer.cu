@@ -1,0 +1,46 @@
+// Cross-GPU barrier for the column-sharded prefill: after every rank's GEMM has written its output
+// slice into all ranks' gathered buffers (NVLink peer stores), each rank signals every peer and
+// waits until every peer has signalled it. Flags live in each rank's own memory and are mapped into
+// the peers' address spaces (CUDA IPC, plain peer mappings). Waits are bounded: after
+// kWaitTimeoutNs a rank stops waiting and sets the context's error word.
+#include "common.cuh"
+
+namespace s4 {
+
+struct FlagList {
+  uint32_t* p[8];  // flag array of rank q (kPeerMaxRanks slots), as mapped in this process
+};
+
+__global__ void peer_barrier_kernel(FlagList flags, int nranks, int rank, uint32_t epoch, uint32_t* err) {
+  const int q = threadIdx.x;
+  __threadfence_system();  // this GPU's earlier peer stores (previous kernels) before the signal
+  __syncthreads();
+  if (q < nranks)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags.p[q] + rank), "r"(epoch) : "memory");
+  if (q < nranks) {
+    const uint32_t* mine = flags.p[rank] + q;
+    const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if (globaltimer_ns() > deadline) {
+        set_error(err, kErrWaitTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+}
+
+cudaError_t launch_peer_barrier(uint32_t* const* flags, int nranks, int rank, uint32_t epoch, uint32_t* err,
+                                cudaStream_t stream) {
+  if (nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks) return cudaErrorInvalidValue;
+  FlagList fl = {};
+  for (int q = 0; q < nranks; ++q) fl.p[q] = flags[q];
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(fl, nranks, rank, epoch, err);
+  return cudaGetLastError();
+}
+
+}  // namespace s4

@@ -25,6 +25,14 @@ cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, _
 int gemv_max_split();
 int gemv_max_tokens();
 cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
+cudaError_t launch_silu_mul_gather(const __half* big, int M, int Is, __half* const* dst, int ndst, int64_t ldd, int col0,
+                                   int sm_count, cudaStream_t stream);
+cudaError_t launch_peer_barrier(uint32_t* const* flags, int nranks, int rank, uint32_t epoch, uint32_t* err,
+                                cudaStream_t stream);
+cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half* x, int64_t ldx, __half* const* ydst,
+                              int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
+                              uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
+                              cudaStream_t stream, bool pdl, bool ticket_fixup);
 bool tc_available();
 size_t tc_partials_bytes(int max_grid);
 cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
@@ -490,6 +498,101 @@ int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, void* str
   cudaError_t e = s4::launch_silu_mul(static_cast<const __half*>(big), static_cast<__half*>(mid), M, I, ctx->sm_count,
                                       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
+  ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_buffer_alloc(s4_ctx* ctx, size_t bytes, void** ptr) {
+  if (!ctx || !ptr || bytes == 0) return fail(S4_ERR_INVALID, "bad argument");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return fail(S4_ERR_NOMEM, "buffer allocation of %zu bytes failed", bytes);
+  e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "buffer clear");
+  return S4_OK;
+}
+
+int s4_buffer_free(s4_ctx* ctx, void* ptr) {
+  if (!ctx) return fail(S4_ERR_INVALID, "NULL context");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "buffer free");
+  return S4_OK;
+}
+
+int s4_ipc_handle(s4_ctx* ctx, const void* ptr, void* handle64) {
+  if (!ctx || !ptr || !handle64) return fail(S4_ERR_INVALID, "NULL argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  DeviceGuard guard(ctx->device);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  memcpy(handle64, &h, sizeof(h));
+  return S4_OK;
+}
+
+int s4_ipc_open(s4_ctx* ctx, const void* handle64, void** ptr) {
+  if (!ctx || !handle64 || !ptr) return fail(S4_ERR_INVALID, "NULL argument");
+  DeviceGuard guard(ctx->device);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return S4_OK;
+}
+
+int s4_ipc_close(s4_ctx* ctx, void* ptr) {
+  if (!ctx || !ptr) return fail(S4_ERR_INVALID, "NULL argument");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return S4_OK;
+}
+
+int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, int M, void* const* dst, int ndst,
+                     int ldy, int col0, void* stream) {
+  if (!ctx || !w || !dst) return fail(S4_ERR_INVALID, "NULL argument");
+  if (w->ctx != ctx) return fail(S4_ERR_INVALID, "weight belongs to another context");
+  if (M < 0 || ndst < 1 || ndst > 8) return fail(S4_ERR_INVALID, "bad M or ndst");
+  if (M == 0) return S4_OK;
+  if (!x || ldx < w->K || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(x) & 15))
+    return fail(S4_ERR_INVALID, "x must be 16-byte aligned with ldx >= K and ldx*2 a multiple of 16");
+  if (ldy < 1 || col0 < 0 || (long long)col0 + w->N > ldy) return fail(S4_ERR_INVALID, "output slice outside the row");
+  for (int d = 0; d < ndst; ++d)
+    if (!dst[d]) return fail(S4_ERR_INVALID, "NULL destination %d", d);
+  DeviceGuard guard(ctx->device);
+  const int tn = M >= 256 ? 256 : ((M + 15) / 16) * 16;
+  if ((long long)((M + tn - 1) / tn) * w->nblk > kMaxTickets) return fail(S4_ERR_INVALID, "M too large for one launch");
+  cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, static_cast<const __half*>(x), ldx,
+                                        reinterpret_cast<__half* const*>(dst), ndst, ldy, col0, ctx->partials,
+                                        ctx->tickets, kMaxTickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tn,
+                                        ctx->sm_count, static_cast<cudaStream_t>(stream), ctx->pdl, false);
+  if (e != cudaSuccess) return cuda_fail(e, "gathered tc gemm launch");
+  ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_silu_mul_gather(s4_ctx* ctx, const void* big, int M, int Is, void* const* dst, int ndst, int ldd, int col0,
+                       void* stream) {
+  if (!ctx || !big || !dst) return fail(S4_ERR_INVALID, "NULL argument");
+  if (M < 0 || Is < 8) return fail(S4_ERR_INVALID, "bad shape");
+  if (M == 0) return S4_OK;
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = s4::launch_silu_mul_gather(static_cast<const __half*>(big), M, Is,
+                                             reinterpret_cast<__half* const*>(dst), ndst, ldd, col0, ctx->sm_count,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "silu_mul_gather launch (Is, ldd, col0 must be multiples of 8)");
+  ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_peer_barrier(s4_ctx* ctx, void* const* flags, int nranks, int rank, uint32_t epoch, void* stream) {
+  if (!ctx || !flags) return fail(S4_ERR_INVALID, "NULL argument");
+  if (nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks) return fail(S4_ERR_INVALID, "bad rank / nranks");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = s4::launch_peer_barrier(reinterpret_cast<uint32_t* const*>(flags), nranks, rank, epoch, ctx->err,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "peer barrier launch");
   ++ctx->launches;
   return S4_OK;
 }

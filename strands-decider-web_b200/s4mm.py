@@ -47,6 +47,14 @@ _SIGS = {
     "s4_matmul_host_async": (C.c_int, [_P, _P, _P, C.c_int, _P, _P]),
     "s4_matmul_noalloc": (C.c_int, [_P, _P, C.c_int, _P, _P]),
     "s4_silu_mul": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
+    "s4_buffer_alloc": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
+    "s4_buffer_free": (C.c_int, [_P, _P]),
+    "s4_ipc_handle": (C.c_int, [_P, _P, _P]),
+    "s4_ipc_open": (C.c_int, [_P, _P, C.POINTER(_P)]),
+    "s4_ipc_close": (C.c_int, [_P, _P]),
+    "s4_matmul_gather": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.POINTER(_P), C.c_int, C.c_int, C.c_int, _P]),
+    "s4_silu_mul_gather": (C.c_int, [_P, _P, C.c_int, C.c_int, C.POINTER(_P), C.c_int, C.c_int, C.c_int, _P]),
+    "s4_peer_barrier": (C.c_int, [_P, C.POINTER(_P), C.c_int, C.c_int, C.c_uint32, _P]),
     "s4_plan": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int),
                           C.POINTER(C.c_int)]),
     "s4_force": (C.c_int, [_P, C.c_int, C.c_int, C.c_int]),
@@ -213,6 +221,48 @@ class Context:
             mid = torch.empty((M, I), dtype=torch.float16, device=big.device)
         _check(_lib.s4_silu_mul(self.handle, big.data_ptr(), int(M), int(I), mid.data_ptr(), _stream_handle(stream)))
         return mid
+
+    # -- column-sharded prefill over peer memory --------------------------------------------------
+    def buffer_alloc(self, nbytes: int) -> int:
+        p = _P()
+        _check(_lib.s4_buffer_alloc(self.handle, int(nbytes), C.byref(p)))
+        return p.value
+
+    def buffer_free(self, ptr: int):
+        _check(_lib.s4_buffer_free(self.handle, ptr))
+
+    def ipc_handle(self, ptr: int) -> bytes:
+        h = C.create_string_buffer(64)
+        _check(_lib.s4_ipc_handle(self.handle, ptr, h))
+        return h.raw
+
+    def ipc_open(self, handle: bytes) -> int:
+        p = _P()
+        hb = C.create_string_buffer(handle, 64)
+        _check(_lib.s4_ipc_open(self.handle, hb, C.byref(p)))
+        return p.value
+
+    def ipc_close(self, ptr: int):
+        _check(_lib.s4_ipc_close(self.handle, ptr))
+
+    @staticmethod
+    def _ptr_array(ptrs):
+        return (_P * len(ptrs))(*[_P(int(p)) for p in ptrs])
+
+    def matmul_gather(self, x_ptr: int, ldx: int, M: int, W: Weight, dst_ptrs, ldy: int, col0: int, stream=None):
+        arr = self._ptr_array(dst_ptrs)
+        _check(_lib.s4_matmul_gather(self.handle, W.handle, x_ptr, int(ldx), int(M), arr, len(dst_ptrs), int(ldy),
+                                     int(col0), _stream_handle(stream)))
+
+    def silu_mul_gather(self, big, Is: int, dst_ptrs, ldd: int, col0: int, stream=None):
+        arr = self._ptr_array(dst_ptrs)
+        _check(_lib.s4_silu_mul_gather(self.handle, big.data_ptr(), int(big.shape[0]), int(Is), arr, len(dst_ptrs),
+                                       int(ldd), int(col0), _stream_handle(stream)))
+
+    def peer_barrier(self, flag_ptrs, rank: int, epoch: int, stream=None):
+        arr = self._ptr_array(flag_ptrs)
+        _check(_lib.s4_peer_barrier(self.handle, arr, len(flag_ptrs), int(rank), int(epoch) & 0xFFFFFFFF,
+                                    _stream_handle(stream)))
 
     # -- dispatcher ------------------------------------------------------------------------------
     def plan(self, M: int, N: int = 0, K: int = 0):

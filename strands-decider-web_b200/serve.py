@@ -16,7 +16,9 @@ Multi-GPU (one process per GPU, ``torch.distributed``):
   processing-time order (:func:`lpt_shard`); every rank holds all weights; there is no collective.
 * column-sharded prefill (config 4): each rank holds an N/g slice of every projection's output
   rows (gate and up slices kept together so SiLU*mul stays local) and the slices are all-gathered
-  after every projection (:class:`ShardedStack`).
+  after every projection: by NCCL (:func:`stack_forward` on a sharded :class:`CudaStack`), or fused
+  into the producing kernels, which store into every rank's buffer over NVLink
+  (:class:`FusedColshardStack`).
 
 The sharding logic takes its matmul / SiLU*mul / all-gather as callables, so the same code runs on
 the CUDA kernels with NCCL and on CPU ranks with gloo in the tests.
@@ -218,3 +220,91 @@ class CudaStack:
 
     def forward(self, x, group=None, timers=None):
         return stack_forward(x, self.layers, self.ops(group), self.world, timers)
+
+
+def _raw_tensor(ptr: int, shape, device):
+    """A torch fp16 view of device memory owned elsewhere (a library buffer or a peer mapping)."""
+    import torch
+
+    class _Holder:
+        pass
+
+    h = _Holder()
+    h.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f2", "data": (int(ptr), False), "version": 3,
+                                  "strides": None}
+    return torch.as_tensor(h, device=device)
+
+
+class FusedColshardStack:
+    """Column-sharded stack whose all-gathers are fused into the producing kernels.
+
+    Every rank allocates its gathered activation buffers (one cudaMalloc each), exports them with
+    CUDA IPC and maps the peers' buffers, so each GEMM epilogue (and the SiLU*mul kernel) stores
+    its column slice into all ranks' buffers over NVLink while it computes. A bounded flag barrier
+    between projections orders the writes before the next projection reads them."""
+
+    def __init__(self, ctx, group, rank: int, world: int, max_tokens: int = 2048, n_layers: int = N_LAYERS):
+        import torch
+        import torch.distributed as dist
+        self.ctx, self.group, self.rank, self.world = ctx, group, rank, world
+        self.device = torch.device("cuda", ctx.device)
+        self.stack = CudaStack(ctx, n_layers, rank, world, self.device)
+        self.max_tokens = max_tokens
+        self.widths = {"a": N_LINEAR_IN, "b": HIDDEN, "mid": INTER, "d": HIDDEN}
+        sizes = {k: max_tokens * w * 2 for k, w in self.widths.items()}
+        sizes["flags"] = 64
+        self.local = {k: ctx.buffer_alloc(v) for k, v in sizes.items()}
+        every = [None] * world
+        if world > 1:
+            handles = {k: ctx.ipc_handle(p) for k, p in self.local.items()}
+            dist.all_gather_object(every, handles, group=group)
+        self.ptrs = {k: [self.local[k] if q == rank else ctx.ipc_open(every[q][k]) for q in range(world)]
+                     for k in sizes}
+        self.gu = torch.empty((max_tokens, 2 * INTER // world), dtype=torch.float16, device=self.device)
+        self.epoch = 0
+        torch.cuda.synchronize(self.device)
+        if world > 1:
+            dist.barrier(group=group)
+
+    def _view(self, key, M, width):
+        return _raw_tensor(self.local[key], (M, width), self.device)
+
+    def barrier(self):
+        if self.world > 1:
+            self.epoch += 1
+            self.ctx.peer_barrier(self.ptrs["flags"], self.rank, self.epoch)
+
+    def forward(self, x):
+        """x: [M, 2048] fp16, contiguous, the same on every rank."""
+        ctx, r, g = self.ctx, self.rank, self.world
+        M = x.shape[0]
+        assert M <= self.max_tokens and x.is_contiguous()
+        for w in self.stack.layers:
+            nin = w["in_proj"].N * g
+            ctx.matmul_gather(x.data_ptr(), HIDDEN, M, w["in_proj"], self.ptrs["a"], nin, r * w["in_proj"].N)
+            self.barrier()
+            ctx.matmul_gather(self.local["a"], nin, M, w["out_proj"], self.ptrs["b"], HIDDEN, r * (HIDDEN // g))
+            self.barrier()
+            gu = ctx.matmul(self._view("b", M, HIDDEN), w["gate_up"], M, self.gu[:M])
+            ctx.silu_mul_gather(gu, INTER // g, self.ptrs["mid"], INTER, r * (INTER // g))
+            self.barrier()
+            ctx.matmul_gather(self.local["mid"], INTER, M, w["down"], self.ptrs["d"], HIDDEN, r * (HIDDEN // g))
+            self.barrier()
+            x = x + self._view("d", M, HIDDEN)
+        return x
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for k, ps in self.ptrs.items():
+            for q, p in enumerate(ps):
+                if q != self.rank:
+                    self.ctx.ipc_close(p)
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # peers unmapped before anyone frees
+        for p in self.local.values():
+            self.ctx.buffer_free(p)

@@ -1,0 +1,83 @@
+"""Column-sharded prefill on two GPUs: the all-gather fused into the GEMM / SiLU*mul kernels (peer
+stores over NVLink) and the NCCL all-gather variant must both match the unsharded stack on one GPU
+within the north-star tolerance (max relative error 2e-3, per-row cosine 0.99999). Skipped when
+fewer than two GPUs are visible."""
+import importlib
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+N_LAYERS, M = 4, 256
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, port, q):
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "tests"))
+    sys.path.insert(0, root)
+    from conftest import load_package
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        pkg = load_package()
+        serve = importlib.import_module("strands_decider_web_b200.serve")
+        ctx = pkg.Context(rank)
+        x = torch.from_numpy(np.random.default_rng(11).standard_normal((M, serve.HIDDEN)).astype(np.float16)).cuda()
+        fused = serve.FusedColshardStack(ctx, None, rank, world, max_tokens=M, n_layers=N_LAYERS)
+        y_fused = fused.forward(x)
+        sharded = serve.CudaStack(ctx, N_LAYERS, rank, world)
+        y_nccl = sharded.forward(x)
+        torch.cuda.synchronize()
+        errs = ctx.check_errors()
+        out = {"fused": y_fused.cpu().numpy(), "nccl": y_nccl.cpu().numpy(), "errs": errs}
+        if rank == 0:
+            full = serve.CudaStack(ctx, N_LAYERS)
+            out["ref"] = full.forward(x).cpu().numpy()
+        fused.close()
+        q.put((rank, out))
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_and_nccl_colshard_match_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from oracle import s4ref
+    world = 2
+    mp = torch.multiprocessing.get_context("spawn")
+    q = mp.Queue()
+    port = _free_port()
+    procs = [mp.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ref = res[0]["ref"].astype(np.float32)
+    for r in range(world):
+        assert res[r]["errs"] == 0
+        for kind in ("fused", "nccl"):
+            ok, mr, mc = s4ref.check(res[r][kind], ref)
+            assert ok, (r, kind, mr, mc)
+    np.testing.assert_array_equal(res[0]["fused"], res[1]["fused"])
