@@ -506,10 +506,11 @@ def run_stack(args, rank, world, local_rank):
             timing["events"].append((a, b))
             return out
 
-        def step():
+        def eager():
             if fused is not None:
                 return fused.forward(x)
             return stack.forward(x, timers=timers)
+        step = eager
         tokens_per_step = 2048 * 1  # the prompt, whatever the number of ranks (strong scaling)
         label = f"config4_stack_2048_prompt_colshard_{args.gather}"
     else:
@@ -534,23 +535,49 @@ def run_stack(args, rank, world, local_rank):
     for _ in range(args.warmup):
         step()
     barrier()
+    graph = None
+    launches_per_step = None
+    if args.workload == "stack" and args.graph:
+        # the whole forward (GEMMs, norms, SiLU*mul, barriers or NCCL all-gathers) as one CUDA graph
+        l0 = ctx.launch_count
+        if fused is not None:
+            fused.capture(x)
+            step = fused.replay
+        else:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                stack.forward(x)
+            step = graph.replay
+        launches_per_step = ctx.launch_count - l0
+        for _ in range(args.warmup):
+            step()
+        barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = ctx.launch_count
     with ClockSampler(local_rank) as clocks:
         barrier()
-        if args.workload == "stack":
-            timing.update(on=True, events=[])
         e0.record(stream)
         for _ in range(args.steps):
             step()
         e1.record(stream)
         barrier()
     launches = ctx.launch_count - launches0
+    if launches_per_step is not None:
+        launches = launches_per_step * args.steps
     ms = max_over_ranks(e0.elapsed_time(e1))
     comm_share = None
-    if args.workload == "stack" and world > 1:
-        gather_ms = sum(a.elapsed_time(b) for a, b in timing["events"])
-        comm_share = max_over_ranks(gather_ms) / ms
+    if args.workload == "stack" and world > 1 and fused is None:
+        # NCCL all-gather share of one eager step (events around each all-gather), outside the timed region
+        timing.update(on=True, events=[])
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        a.record(stream)
+        eager()
+        b.record(stream)
+        barrier()
+        timing["on"] = False
+        gather_ms = sum(p.elapsed_time(q) for p, q in timing["events"])
+        comm_share = max_over_ranks(gather_ms / a.elapsed_time(b))
     tok_s = tokens_per_step * args.steps / (ms / 1e3)
     tflops = tok_s * flops_tok / 1e12
     if ctx.check_errors():
@@ -570,10 +597,15 @@ def run_stack(args, rank, world, local_rank):
                          "frac": tflops / tc_peak, "traffic": None, "peak_kind": peak_kind,
                          "note": "whole-stack FLOP rate (2 x weight parameters per token), all kernels included"},
             "gather_share": comm_share,
+            "cuda_graph": bool(args.workload == "stack" and args.graph),
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    # a graph that holds NCCL calls must be gone before destroy_process_group (the bound replay
+    # method in `step` keeps it alive too)
+    step = graph = None
+    torch.cuda.synchronize(dev)
     if fused is not None:
         fused.close()
     ctx.close()
@@ -601,6 +633,8 @@ def main():
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="stack: fuse the all-gathers into the producing kernels (peer stores over NVLink) or "
                          "call NCCL all-gather after every projection")
+    ap.add_argument("--graph", type=int, default=1,
+                    help="stack: replay the whole forward as one CUDA graph (1, default) or launch eagerly (0)")
     ap.add_argument("--requests", type=int, default=512,
                     help="serve: number of config-5 requests timed per step (the first n of the seeded 4096)")
     args = ap.parse_args()

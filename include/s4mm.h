@@ -115,6 +115,13 @@ S4_API int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, 
  * asynchronous. Replaces SILU_MUL (web/public/engine/wgsl.js:81-90). */
 S4_API int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, void* stream);
 
+/* Residual add + RMSNorm between projections (ADD_NORM, web/public/engine/wgsl.js:55-78):
+ * x[M][D] fp32 residual stream, updated in place by x += y when y (fp16) is not NULL; then
+ * h[M][D] = f16(x * rsqrt(mean(x^2) + eps) * w), w fp32 [D] (the stored 1 + weight) or NULL for
+ * ones. DEVICE pointers, asynchronous. */
+S4_API int s4_add_rmsnorm(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps, void* h,
+                          void* stream);
+
 /* ---- column-sharded prefill over NVLink (one process per GPU on one node) ----
  * Each rank computes an N/g slice of every projection and writes it straight into every rank's
  * gathered output buffer through peer mappings (the all-gather fused into the GEMM epilogue; the
@@ -141,9 +148,11 @@ S4_API int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int 
 S4_API int s4_silu_mul_gather(s4_ctx* ctx, const void* big, int M, int Is, void* const* dst, int ndst, int ldd,
                               int col0, void* stream);
 
-/* Barrier across nranks GPUs: flags[q] is rank q's flag array (>= 8 uint32, zeroed, peer-mapped);
- * every rank passes the same increasing epoch. A wait that exceeds 1 s sets the context's error
- * word (s4_check_errors) instead of hanging. Asynchronous on `stream`. */
+/* Barrier across nranks GPUs: flags[q] is rank q's flag array (>= 16 uint32, zeroed, peer-mapped);
+ * every rank passes the same increasing epoch, or every rank passes 0 on every call: the epoch is
+ * then counted on the device (slot 8 of the rank's own array), so the barrier can be captured in
+ * a CUDA graph and replayed. Do not mix the two forms on one flag array. A wait that exceeds 1 s
+ * sets the context's error word (s4_check_errors) instead of hanging. Asynchronous on `stream`. */
 S4_API int s4_peer_barrier(s4_ctx* ctx, void* const* flags, int nranks, int rank, uint32_t epoch, void* stream);
 
 /* Dispatcher. s4_plan reports the (family, tile, split) s4_matmul will use for M on an

@@ -185,6 +185,22 @@ def silu_mul(big: np.ndarray, I: int) -> np.ndarray:
 
 
 # --------------------------------------------------------------------------------------------
+# residual add + RMSNorm  (web/public/engine/wgsl.js:55-78)
+# --------------------------------------------------------------------------------------------
+def add_rmsnorm(x: np.ndarray, y=None, w=None, eps: float = 1e-6):
+    """ADD_NORM: fp32 residual ``x += y`` (y fp16, optional), then ``h = f16(x * (mean(x^2) + eps)^-1/2
+    * w)`` per row (wgsl.js:55-78; ``w`` is the stored 1 + weight). Returns (x_new f32, h f16)."""
+    x = np.asarray(x, dtype=np.float32)
+    if y is not None:
+        x = x + np.asarray(y, dtype=np.float16).astype(np.float32)
+    inv = 1.0 / np.sqrt((x.astype(np.float64) ** 2).mean(1, keepdims=True) + eps)
+    h = x * inv.astype(np.float32)
+    if w is not None:
+        h = h * np.asarray(w, dtype=np.float32)
+    return x, h.astype(np.float16)
+
+
+# --------------------------------------------------------------------------------------------
 # device layout (the layout the upload kernel writes; checked bit-exactly against the GPU)
 # --------------------------------------------------------------------------------------------
 NB_ROWS = 128   # output rows (N) per n-block

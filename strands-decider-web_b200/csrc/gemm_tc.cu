@@ -44,7 +44,9 @@ constexpr int kTcOffW = kTcOffA + kTcStagesA * kTcAStageBytes;
 constexpr int kTcOffBar = kTcOffW + kTcSlotsW * kTcWSlotBytes;
 constexpr int kTcNumBars = 3 * kTcStagesA + 2 * kTcSlotsW + 2 + 2 + 1;
 constexpr int kTcOffMisc = kTcOffBar + kTcNumBars * 8;
-constexpr size_t kTcSmem = (size_t)kTcOffMisc + 64 + 1024;  // + alignment slack
+constexpr int kTcOffEpi = (kTcOffMisc + 64 + 127) & ~127;  // epilogue staging: 4 warps x 16 tokens x 32 n fp16
+constexpr int kTcEpiStageBytes = 16 * 32 * 2;
+constexpr size_t kTcSmem = (size_t)kTcOffEpi + 4 * kTcEpiStageBytes + 1024;  // + alignment slack
 constexpr uint32_t kTcTmemCols = 512;                       // two 256-column accumulators
 
 constexpr int kTcMaxDst = 8;  // output copies one launch writes (this GPU + peers)
@@ -56,6 +58,7 @@ struct TcParams {
   int ndst;
   int64_t ldy;
   int ycol0;
+  int vec;  // 16-byte output stores allowed: ldy and ycol0 multiples of 8, every ydst 16-byte aligned
   float* partials;    // [G][2][256][128] fp32
   uint32_t* tickets;  // [ntb * nblk]
   uint32_t* err;
@@ -67,11 +70,15 @@ struct TcParams {
   int grid;
 };
 
-// One output element to every destination (local buffer and, for the column-sharded prefill, the
-// peers' gathered buffers over NVLink).
-__device__ __forceinline__ void tc_store(const TcParams& p, int tok, int ncol, float v) {
-  const __half h = __float2half_rn(v);
-  const int64_t off = (int64_t)tok * p.ldy + p.ycol0 + ncol;
+// Output stores. Each destination is the local buffer or, for the column-sharded prefill, a peer's
+// gathered buffer over NVLink. Call sites branch on ndst == 1 once, outside their element loops:
+// the epilogue runs 256 stores per thread per tile, and per-element guards for the other
+// destinations (predicated code, issued even when off) made a K = 2048 GEMM's epilogue outlast the
+// next tile's main loop.
+__device__ __forceinline__ int64_t tc_out_off(const TcParams& p, int tok, int ncol) {
+  return (int64_t)tok * p.ldy + p.ycol0 + ncol;
+}
+__device__ __forceinline__ void tc_store_all(const TcParams& p, int64_t off, __half h) {
   for (int d = 0; d < p.ndst; ++d) p.ydst[d][off] = h;
 }
 
@@ -345,6 +352,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     const int q = warp - kTcEpiWarp0;  // TMEM lane quarter this warp may access (warp % 4)
     const int nl = q * 32 + lane;
     const int et = threadIdx.x - kTcEpiWarp0 * 32;
+    __half* epi_stage = reinterpret_cast<__half*>(smem + kTcOffEpi + q * kTcEpiStageBytes);
     bool failed = false;
     int si = 0;
     for (int i = 0; i < n; ++si) {
@@ -370,12 +378,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         for (int cb = 0; cb < p.tn; cb += 16) {
           float v[16];
           tmem_ld16(taddr + cb, v);
-          if (full) {
-            if (ncol < p.N) {
+          if (full && p.vec) {
+            // transpose 32 n x 16 tokens through shared memory, then 16-byte stores of 8 n
 #pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                const int tok = tok0 + cb + e;
-                if (tok < p.M) tc_store(p, tok, ncol, v[e]);
+            for (int e = 0; e < 16; ++e) epi_stage[e * 32 + lane] = __float2half_rn(v[e]);
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int t = j * 8 + (lane >> 2), c = lane & 3;
+              const uint4 val = *reinterpret_cast<const uint4*>(epi_stage + t * 32 + c * 8);
+              const int tok = tok0 + cb + t;
+              const int n0 = nb * 128 + q * 32 + c * 8;
+              if (tok < p.M && n0 < p.N) {
+                const int64_t off = tc_out_off(p, tok, n0);
+                if (n0 + 8 <= p.N) {
+                  *reinterpret_cast<uint4*>(p.ydst[0] + off) = val;
+                  for (int d = 1; d < p.ndst; ++d) *reinterpret_cast<uint4*>(p.ydst[d] + off) = val;
+                } else {
+                  const __half* hv = reinterpret_cast<const __half*>(&val);
+#pragma unroll
+                  for (int k = 0; k < 8; ++k)
+                    if (n0 + k < p.N) tc_store_all(p, off + k, hv[k]);
+                }
+              }
+            }
+            __syncwarp();
+          } else if (full) {
+            if (ncol < p.N) {
+              const int64_t off0 = tc_out_off(p, tok0 + cb, ncol);
+              if (p.ndst == 1) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                  if (tok0 + cb + e < p.M) p.ydst[0][off0 + e * p.ldy] = __float2half_rn(v[e]);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                  if (tok0 + cb + e < p.M) tc_store_all(p, off0 + e * p.ldy, __float2half_rn(v[e]));
               }
             }
           } else {
@@ -415,7 +453,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
             if (ncol < p.N) {
 #pragma unroll
               for (int e = 0; e < 16; ++e)
-                if (t0 + e < rows) tc_store(p, tok0 + t0 + e, ncol, acc[e]);
+                if (t0 + e < rows) tc_store_all(p, tc_out_off(p, tok0 + t0 + e, ncol), __float2half_rn(acc[e]));
             }
           }
           named_bar_sync(2, 128);
@@ -475,9 +513,16 @@ __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcParams p) {
       }
   }
   if (ncol < p.N) {
+    const int64_t off0 = tc_out_off(p, tok0 + r0, ncol);
+    if (p.ndst == 1) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (r0 + e < rows) tc_store(p, tok0 + r0 + e, ncol, acc[e]);
+      for (int e = 0; e < 8; ++e)
+        if (r0 + e < rows) p.ydst[0][off0 + e * p.ldy] = __float2half_rn(acc[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (r0 + e < rows) tc_store_all(p, off0 + e * p.ldy, __float2half_rn(acc[e]));
+    }
   }
 }
 
@@ -523,6 +568,9 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
   p.ndst = ndst;
   p.ldy = ldy;
   p.ycol0 = ycol0;
+  p.vec = (ldy % 8 == 0 && ycol0 % 8 == 0) ? 1 : 0;
+  for (int d = 0; d < ndst; ++d)
+    if (reinterpret_cast<uintptr_t>(ydst[d]) & 15) p.vec = 0;
   p.partials = partials;
   p.tickets = tickets;
   p.err = err;

@@ -11,10 +11,24 @@ struct FlagList {
   uint32_t* p[8];  // flag array of rank q (kPeerMaxRanks slots), as mapped in this process
 };
 
+// Slot of a rank's own flag array that counts its barriers when the epoch is taken on the device.
+constexpr int kPeerCounterSlot = 8;
+
 __global__ void peer_barrier_kernel(FlagList flags, int nranks, int rank, uint32_t epoch, uint32_t* err) {
   const int q = threadIdx.x;
+  __shared__ uint32_t s_epoch;
+  if (q == 0) {
+    if (epoch == 0) {  // device-side epoch: this rank's barriers are ordered on its stream
+      uint32_t* ctr = flags.p[rank] + kPeerCounterSlot;
+      epoch = *ctr + 1;
+      if (epoch == 0) epoch = 1;
+      *ctr = epoch;
+    }
+    s_epoch = epoch;
+  }
   __threadfence_system();  // this GPU's earlier peer stores (previous kernels) before the signal
   __syncthreads();
+  epoch = s_epoch;
   if (q < nranks)
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags.p[q] + rank), "r"(epoch) : "memory");
   if (q < nranks) {

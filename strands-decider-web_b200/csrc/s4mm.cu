@@ -27,6 +27,8 @@ int gemv_max_tokens();
 cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
 cudaError_t launch_silu_mul_gather(const __half* big, int M, int Is, __half* const* dst, int ndst, int64_t ldd, int col0,
                                    int sm_count, cudaStream_t stream);
+cudaError_t launch_add_rmsnorm(float* x, const __half* y, const float* w, int M, int D, float eps, __half* h,
+                               cudaStream_t stream);
 cudaError_t launch_peer_barrier(uint32_t* const* flags, int nranks, int rank, uint32_t epoch, uint32_t* err,
                                 cudaStream_t stream);
 cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half* x, int64_t ldx, __half* const* ydst,
@@ -498,6 +500,19 @@ int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, void* str
   cudaError_t e = s4::launch_silu_mul(static_cast<const __half*>(big), static_cast<__half*>(mid), M, I, ctx->sm_count,
                                       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
+  ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_add_rmsnorm(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps, void* h,
+                   void* stream) {
+  if (!ctx || !x || !h) return fail(S4_ERR_INVALID, "NULL argument");
+  if (M < 0 || D < 1) return fail(S4_ERR_INVALID, "bad shape M=%d D=%d", M, D);
+  if (M == 0) return S4_OK;
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = s4::launch_add_rmsnorm(x, static_cast<const __half*>(y), w, M, D, eps, static_cast<__half*>(h),
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "add_rmsnorm launch");
   ++ctx->launches;
   return S4_OK;
 }

@@ -47,6 +47,7 @@ _SIGS = {
     "s4_matmul_host_async": (C.c_int, [_P, _P, _P, C.c_int, _P, _P]),
     "s4_matmul_noalloc": (C.c_int, [_P, _P, C.c_int, _P, _P]),
     "s4_silu_mul": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
+    "s4_add_rmsnorm": (C.c_int, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_float, _P, _P]),
     "s4_buffer_alloc": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
     "s4_buffer_free": (C.c_int, [_P, _P]),
     "s4_ipc_handle": (C.c_int, [_P, _P, _P]),
@@ -221,6 +222,22 @@ class Context:
             mid = torch.empty((M, I), dtype=torch.float16, device=big.device)
         _check(_lib.s4_silu_mul(self.handle, big.data_ptr(), int(M), int(I), mid.data_ptr(), _stream_handle(stream)))
         return mid
+
+    def add_rmsnorm(self, x, y=None, w=None, eps: float = 1e-6, h=None, stream=None):
+        """``x += y`` (fp32 residual, in place; skipped when y is None), then
+        ``h = f16(x * rsqrt(mean(x^2) + eps) * w)`` (w None = ones). Returns h."""
+        import torch
+        M, D = x.shape
+        if x.dtype != torch.float32 or not x.is_contiguous():
+            raise S4Error(1, "add_rmsnorm: x must be a contiguous fp32 tensor")
+        if y is not None and (y.dtype != torch.float16 or not y.is_contiguous() or tuple(y.shape) != (M, D)):
+            raise S4Error(1, "add_rmsnorm: y must be a contiguous fp16 tensor shaped like x")
+        if h is None:
+            h = torch.empty((M, D), dtype=torch.float16, device=x.device)
+        _check(_lib.s4_add_rmsnorm(self.handle, x.data_ptr(), y.data_ptr() if y is not None else None,
+                                   w.data_ptr() if w is not None else None, int(M), int(D), float(eps), h.data_ptr(),
+                                   _stream_handle(stream)))
+        return h
 
     # -- column-sharded prefill over peer memory --------------------------------------------------
     def buffer_alloc(self, nbytes: int) -> int:

@@ -4,11 +4,13 @@ The stack is the int4 part of the engine's per-layer step list (``plan()``, web/
 engine.js:253-282): every layer runs its fused input projection (linear-attention qkv|z|a|b, K=2048,
 N=8224, or attention q|k|v, N=3072), the out projection (2048 -> 2048), the MLP gate|up (2048 ->
 12288), SiLU*mul (wgsl.js:81-90) and down (6144 -> 2048); layers follow the 3:1 pattern of the
-hybrid decoder (three linear-attention layers, then one attention layer). The non-linear-path
-operators between them (norms, conv, recurrence, attention) are outside this path; the synthetic
-wiring that replaces them is: the out projection reads columns [0, 2048) of the input projection's
-output, gate|up reads the out projection's output, and the down output is added to the layer input
-as an fp16 residual.
+hybrid decoder (three linear-attention layers, then one attention layer). The residual stream and
+its norms follow the engine exactly (ADD_NORM, wgsl.js:55-78, engine.js:255, 277, 284): ``x`` is
+fp32; before the input projection ``x += y`` (the previous layer's down output; not at layer 0) and
+``h = rmsnorm(x)``; before gate|up ``x += y`` (the out projection's output) and ``h = rmsnorm(x)``;
+after the last layer ``x += y`` and the final norm gives the output. The mixers between the input
+and out projections (conv, recurrence, attention) are outside this path; the out projection reads
+columns [0, 2048) of the input projection's output in their place. Norm weights are ones.
 
 Multi-GPU (one process per GPU, ``torch.distributed``):
 
@@ -123,15 +125,18 @@ class Ops:
     matmul: object      # (x [M,K] f16, weight handle) -> y [M,N] f16
     silu_mul: object    # (big [M, 2I] f16, I) -> mid [M, I] f16
     all_gather: object  # (local [M, ns]) -> [world][M][ns] stacked (None when world == 1)
-    add: object         # (a, b) -> a + b (fp16 residual)
+    add_norm: object    # (x f32 [M, D], y f16 or None) -> (x + y f32, rmsnorm(x + y) f16)
     cols: object        # (x, c0, c1) -> contiguous x[:, c0:c1]
+    to_f32: object      # x f16 -> fp32 residual stream (a new tensor)
 
 
 def stack_forward(x, layers, ops: Ops, world: int = 1, timers=None):
-    """Run the linear stack on activations ``x`` [M, 2048] (fp16).
+    """Run the linear stack on embeddings ``x`` [M, 2048] (fp16); returns the final-normed hidden
+    states (fp16).
 
-    ``layers`` is a list of dicts name -> weight handle (the rank's shard when ``world`` > 1).
-    ``timers``, if given, is called as timers("gather", fn) around every all-gather."""
+    ``layers`` is a list of dicts name -> weight handle (the rank's shard when ``world`` > 1); the
+    norms are replicated on every rank. ``timers``, if given, is called as timers("gather", fn)
+    around every all-gather."""
     M = x.shape[0]
 
     def gather(local):
@@ -141,14 +146,18 @@ def stack_forward(x, layers, ops: Ops, world: int = 1, timers=None):
         g = timers("gather", lambda: ops.all_gather(local)) if timers else ops.all_gather(local)
         return gathered_to_rows(g, M, world, ns)
 
+    x = ops.to_f32(x)
+    y = None
     for w in layers:
-        a = gather(ops.matmul(x, w["in_proj"]))
-        b = gather(ops.matmul(ops.cols(a, 0, HIDDEN), w["out_proj"]))
-        gu = ops.matmul(b, w["gate_up"])
+        x, h = ops.add_norm(x, y)                                   # in_norm (engine.js:255)
+        a = gather(ops.matmul(h, w["in_proj"]))
+        y = gather(ops.matmul(ops.cols(a, 0, HIDDEN), w["out_proj"]))
+        x, h = ops.add_norm(x, y)                                   # post_norm (engine.js:277)
+        gu = ops.matmul(h, w["gate_up"])
         mid = gather(ops.silu_mul(gu, gu.shape[1] // 2))
-        d = gather(ops.matmul(mid, w["down"]))
-        x = ops.add(x, d)
-    return x
+        y = gather(ops.matmul(mid, w["down"]))
+    x, h = ops.add_norm(x, y)                                       # final norm (engine.js:284)
+    return h
 
 
 # --------------------------------------------------------------------------------------------------
@@ -212,11 +221,15 @@ class CudaStack:
             dist.all_gather_into_tensor(out, local.contiguous(), group=group)
             return out
 
+        def add_norm(x, y):
+            return x, ctx.add_rmsnorm(x, y)
+
         return Ops(matmul=lambda x, w: ctx.matmul(x, w),
                    silu_mul=lambda big, I: ctx.silu_mul(big, I),
                    all_gather=all_gather,
-                   add=lambda a, b: a + b,
-                   cols=lambda x, c0, c1: x[:, c0:c1].contiguous())
+                   add_norm=add_norm,
+                   cols=lambda x, c0, c1: x[:, c0:c1].contiguous(),
+                   to_f32=lambda x: x.float())
 
     def forward(self, x, group=None, timers=None):
         return stack_forward(x, self.layers, self.ops(group), self.world, timers)
@@ -261,42 +274,67 @@ class FusedColshardStack:
         self.ptrs = {k: [self.local[k] if q == rank else ctx.ipc_open(every[q][k]) for q in range(world)]
                      for k in sizes}
         self.gu = torch.empty((max_tokens, 2 * INTER // world), dtype=torch.float16, device=self.device)
-        self.epoch = 0
+        self.h = torch.empty((max_tokens, HIDDEN), dtype=torch.float16, device=self.device)
+        self.x = torch.empty((max_tokens, HIDDEN), dtype=torch.float32, device=self.device)
+        self.flat = {k: _raw_tensor(self.local[k], (max_tokens * w,), self.device) for k, w in self.widths.items()}
+        self.graph = None
         torch.cuda.synchronize(self.device)
         if world > 1:
             dist.barrier(group=group)
 
     def _view(self, key, M, width):
-        return _raw_tensor(self.local[key], (M, width), self.device)
+        return self.flat[key][: M * width].view(M, width)
 
     def barrier(self):
+        """Cross-GPU flag barrier with its epoch counted on the device (graph-replayable)."""
         if self.world > 1:
-            self.epoch += 1
-            self.ctx.peer_barrier(self.ptrs["flags"], self.rank, self.epoch)
+            self.ctx.peer_barrier(self.ptrs["flags"], self.rank, 0)
 
     def forward(self, x):
-        """x: [M, 2048] fp16, contiguous, the same on every rank."""
+        """x: [M, 2048] fp16 embeddings, the same on every rank; returns the final-normed hidden
+        states [M, 2048] fp16 (a view of this object's buffer, valid until the next call). The fp32
+        residual stream and the norms are replicated; the projections are sharded."""
         ctx, r, g = self.ctx, self.rank, self.world
         M = x.shape[0]
-        assert M <= self.max_tokens and x.is_contiguous()
+        assert M <= self.max_tokens
+        xs, h = self.x[:M], self.h[:M]
+        xs.copy_(x)
+        y = None
         for w in self.stack.layers:
+            ctx.add_rmsnorm(xs, y, h=h)                                 # in_norm
             nin = w["in_proj"].N * g
-            ctx.matmul_gather(x.data_ptr(), HIDDEN, M, w["in_proj"], self.ptrs["a"], nin, r * w["in_proj"].N)
+            ctx.matmul_gather(h.data_ptr(), HIDDEN, M, w["in_proj"], self.ptrs["a"], nin, r * w["in_proj"].N)
             self.barrier()
             ctx.matmul_gather(self.local["a"], nin, M, w["out_proj"], self.ptrs["b"], HIDDEN, r * (HIDDEN // g))
             self.barrier()
-            gu = ctx.matmul(self._view("b", M, HIDDEN), w["gate_up"], M, self.gu[:M])
+            ctx.add_rmsnorm(xs, self._view("b", M, HIDDEN), h=h)        # post_norm
+            gu = ctx.matmul(h, w["gate_up"], M, self.gu[:M])
             ctx.silu_mul_gather(gu, INTER // g, self.ptrs["mid"], INTER, r * (INTER // g))
             self.barrier()
             ctx.matmul_gather(self.local["mid"], INTER, M, w["down"], self.ptrs["d"], HIDDEN, r * (HIDDEN // g))
             self.barrier()
-            x = x + self._view("d", M, HIDDEN)
-        return x
+            y = self._view("d", M, HIDDEN)
+        ctx.add_rmsnorm(xs, y, h=h)                                     # final norm
+        return h
+
+    def capture(self, x):
+        """Record ``forward(x)`` into a CUDA graph (after at least one eager call, on every rank);
+        ``replay()`` then reruns the whole stack, barriers included, on ``x``'s memory."""
+        import torch
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            out = self.forward(x)
+        return out
+
+    def replay(self):
+        self.graph.replay()
 
     def close(self):
         import torch
         import torch.distributed as dist
         torch.cuda.synchronize(self.device)
+        self.graph = None
+        self.flat = {}
         if self.world > 1:
             dist.barrier(group=self.group)
         for k, ps in self.ptrs.items():

@@ -147,3 +147,23 @@ def test_metrics():
     assert s4ref.min_row_cosine(ref, ref) > 0.999999
     ok, _, _ = s4ref.check(ref * 1.01, ref)
     assert not ok
+
+
+def test_add_rmsnorm_restatement_matches_loop():
+    """ADD_NORM (wgsl.js:55-78) restated with numpy vs a per-element Python loop of the WGSL body:
+    fp32 residual add, sum of squares, inverseSqrt(mean + eps), fp16 store of v * inv * w."""
+    rng = np.random.default_rng(5)
+    M, D = 3, 40
+    x = rng.standard_normal((M, D)).astype(np.float32)
+    y = (rng.standard_normal((M, D)) * 3).astype(np.float16)
+    w = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    xn, h = s4ref.add_rmsnorm(x, y, w, eps=1e-6)
+    for m in range(M):
+        row = [float(np.float32(x[m, c]) + np.float32(y[m, c])) for c in range(D)]
+        inv = 1.0 / np.sqrt(sum(v * v for v in row) / D + 1e-6)
+        for c in range(D):
+            assert xn[m, c] == np.float32(row[c])
+            assert abs(float(h[m, c]) - row[c] * inv * w[c]) <= 1e-3 * max(1.0, abs(row[c] * inv * w[c]))
+    # no add, unit weight: rows come out with mean square ~1
+    _, h1 = s4ref.add_rmsnorm(x)
+    np.testing.assert_allclose((h1.astype(np.float64) ** 2).mean(1), 1.0, rtol=2e-3)

@@ -79,6 +79,11 @@ def _oracle_layers(serve, n_layers, rank=0, world=1):
     return layers
 
 
+def _add_norm(x, y):
+    xn, h = s4ref.add_rmsnorm(x.numpy(), None if y is None else y.numpy())
+    return torch.from_numpy(xn), torch.from_numpy(h)
+
+
 def _cpu_ops(serve, world):
     def matmul(x, w):
         y, _ = s4ref.matmul(x.numpy(), *w)
@@ -92,8 +97,9 @@ def _cpu_ops(serve, world):
     return serve.Ops(matmul=matmul,
                      silu_mul=lambda big, I: torch.from_numpy(s4ref.silu_mul(big.numpy(), I)),
                      all_gather=all_gather,
-                     add=lambda a, b: (a.float() + b.float()).half(),
-                     cols=lambda x, c0, c1: x[:, c0:c1].contiguous())
+                     add_norm=_add_norm,
+                     cols=lambda x, c0, c1: x[:, c0:c1].contiguous(),
+                     to_f32=lambda x: x.float())
 
 
 def _rank_main(rank, world, port, q):
