@@ -45,6 +45,7 @@ extern "C" {
 
 typedef struct s4_ctx s4_ctx;
 typedef struct s4_weight s4_weight;
+typedef struct s4_chain s4_chain;
 
 /* Library version, (major << 16) | minor. */
 S4_API int s4_version(void);
@@ -110,6 +111,21 @@ S4_API int s4_matmul_host_async(s4_ctx* ctx, const s4_weight* w, const uint16_t*
  * before any stream capture). All calls share the array: calls that overlap on the GPU race.
  * No counterpart in the reference. DEVICE pointers, asynchronous on `stream`. */
 S4_API int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, void* stream);
+
+/* Chained decode GEMV: a fixed list of matmuls y_i[M_i][N_i] = x_i @ W_i^T (1 <= M_i <= 16) run by ONE
+ * persistent launch, like the engine's recorded step list submitted at once (plan(), engine.js:236-282).
+ * The weights of later ops stream into shared memory while earlier ops finish, so a decode step's GEMVs
+ * move weight bytes back to back instead of paying a launch and a DRAM ramp each. dep[i] is the index
+ * of an earlier op whose output op i reads (its x_i aliases y_dep), or -1; dep may be NULL (all -1).
+ * Buffers are bound at creation (DEVICE pointers, x 16-byte aligned) and must stay valid while the
+ * chain is used; results equal s4_matmul's within fp32 summation order. s4_chain_run is asynchronous
+ * on `stream`; runs of one chain must not overlap. Creation is synchronous and allocates the chain's
+ * split-K scratch. S4_ERR_UNSUPPORTED if an op's activation window does not fit in shared memory. */
+S4_API int s4_chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y,
+                           const int* M, const int* dep, s4_chain** out);
+S4_API int s4_chain_run(s4_ctx* ctx, s4_chain* chain, void* stream);
+S4_API int s4_chain_info(const s4_chain* chain, int* grid, int* slots, int* smem_bytes);
+S4_API int s4_chain_free(s4_chain* chain);
 
 /* mid[M][I] = silu(big[:, :I]) * big[:, I:2I], fp16 in/out, fp32 math, DEVICE pointers,
  * asynchronous. Replaces SILU_MUL (web/public/engine/wgsl.js:81-90). */

@@ -5,10 +5,10 @@ Load this directory as a package (its name has hyphens, so import it by path)::
     spec = importlib.util.spec_from_file_location(
         "strands_decider_web_b200", "<dir>/__init__.py", submodule_search_locations=["<dir>"])
 
-Public API: :class:`Context`, :class:`Weight`, :class:`Gemm`, :class:`S4Error`, the stack runner
+Public API: :class:`Context`, :class:`Weight`, :class:`Chain`, :class:`Gemm`, :class:`S4Error`, the stack runner
 (:mod:`.stack`) and the multi-GPU drivers (:mod:`.serve`).
 """
-from .s4mm import (FAMILY_AUTO, FAMILY_GEMV, FAMILY_TC, LIB_PATH, Context, Gemm, S4Error, Weight,  # noqa: F401
+from .s4mm import (FAMILY_AUTO, FAMILY_GEMV, FAMILY_TC, LIB_PATH, Chain, Context, Gemm, S4Error, Weight,  # noqa: F401
                    load_library)
 
 

@@ -1,0 +1,707 @@
+// Chained decode GEMV: a list of small-M int4 matmuls (M <= 16) run by ONE persistent launch.
+//
+// The engine records a forward pass as one list of steps bound to fixed buffers and submits it at
+// once (plan() / forward, web/public/engine/engine.js:236-282); at decode every matmul step is a
+// GEMV over a few MB of weights. Launched one by one, each GEMV pays a launch, a DRAM ramp and a
+// split-K reduction in series (~4-8 us for 3.5-14 MB on B200, well below HBM speed). Here the whole
+// list is one launch with one CTA per SM and five warp roles:
+//
+//  * producer (warp 8, one lane): streams the CTA's weight chunks (128 rows x 64 K: 4096 bytes of
+//    nibbles + 512 bytes of scales, contiguous in the repacked layout) into a ring of shared-memory
+//    slots, four consecutive chunks per slot with two 1-D bulk copies (16 KB of nibbles, 2 KB of
+//    scales; TMA engine, no multicast), op after op without a pause. Copy size matters: the bytes
+//    an SM keeps in flight grow with it (4.6 KB copies streamed at under half the rate);
+//  * stager (warp 9): per op, waits until the op it depends on is complete (if any), then copies
+//    the op's activation window into one of two shared-memory buffers with cp.async (all of a
+//    lane's 16-byte pieces in flight at once), one op ahead of the consumers;
+//  * consumers (warps 0-7, one 16-row sub-tile each): only the tile math of gemv_tile.cuh, four
+//    chunks per batch. At the end of an n-block segment they leave their fp32 sums in shared memory
+//    and move on: they never touch global memory, so they never wait for it;
+//  * publisher (warp 10): writes the consumers' finished segments to global memory (fp16 outputs,
+//    or fp32 partials of split n-blocks), then issues one gpu-scope fence for its own stores and
+//    bumps the counters other CTAs wait on. It never waits on other CTAs;
+//  * reducer (warp 11): finishes the split n-blocks whose part 0 this CTA holds (below). It waits
+//    on other CTAs, which is why it is not the publisher.
+//
+// Work split: op i's chunks (n-block-major, k-tile-minor) are cut into G equal contiguous ranges,
+// one per CTA (stream-K). A 16-row sub-tile that one CTA covers over the whole K range is written
+// as fp16 by that CTA. A split sub-tile has parts 0..P-1 in CTA order. Parts 1..P-1 (the start of a
+// later CTA's range) are published as fp32 partials with a release-increment of the sub-tile's
+// counter. Part 0 belongs to the CTA whose range ends inside the n-block, which usually finishes it
+// last: its reducer waits for the counter to reach P-1, adds the parts in order 0..P-1
+// (deterministic), writes fp16 and resets the counter. Every final sub-tile increments the op's
+// completion counter (release); a dependent op's stager waits for the full count (acquire). All
+// waits are bounded (1 s) and report through the error word; a CTA whose wait expired stops.
+//
+// The launch is cooperative (all CTAs resident), so waiting on other CTAs of the grid cannot
+// deadlock. The last CTA to finish resets the completion counters for the next run.
+#include <vector>
+
+#include "common.cuh"
+#include "gemv_tile.cuh"
+#include "internal.h"
+
+namespace s4 {
+
+constexpr int kChainConsumers = 8;  // warps 0..7
+constexpr int kChainProducerWarp = 8;
+constexpr int kChainStagerWarp = 9;
+constexpr int kChainPublisherWarp = 10;
+constexpr int kChainReducerWarp = 11;
+constexpr int kChainThreads = 12 * 32;
+constexpr int kChainGroup = 4;  // chunks per ring slot (and per consumer batch)
+constexpr int kChainSlotBytes = kChainGroup * (kChunkWBytes + kChunkSBytes);
+constexpr int kChainSlotScales = kChainGroup * kChunkWBytes;  // scales follow the nibbles in a slot
+constexpr int kChainMaxSlots = 16;
+constexpr int kChainMinSlots = 3;
+constexpr int kChainCachedOps = 64;  // op descriptors kept in shared memory
+constexpr int kChainSmemBudget = 216 * 1024;  // dynamic; the static part holds the op cache
+constexpr int kChainSegBytes = kChainConsumers * 2 * 32 * 16;  // one segment's fp32 sums (MG <= 2)
+
+struct ChainOp {
+  const uint8_t* wq;
+  const uint8_t* ws;
+  const __half* x;    // [M][K]
+  __half* y;          // [M][N]
+  float* partials;    // [nblk][8][maxparts][MG][32] float4 (part 0 unused)
+  uint32_t* tickets;  // [nblk * 8] arrivals of parts 1.. of each split sub-tile
+  int M, N, K, nblk, ktiles;
+  int dep;            // op whose output this op reads (-1: none)
+  int maxparts;
+  int xrow;           // padded activation window row (bytes)
+};
+
+struct ChainParams {
+  const ChainOp* ops;
+  int nops;
+  int slots;           // weight ring slots
+  int x_off, x_bytes;  // two activation windows of x_bytes each
+  int ev_off;          // two part-0 buffers, then two publish buffers, kChainSegBytes each
+  int bar_off;         // mbarriers: full[slots], empty[slots], xfull[2], xempty[2], evfull[2],
+                       // evempty[2], pubfull[2], pubempty[2]
+  uint32_t* op_done;   // [nops] finished sub-tiles
+  uint32_t* exit_count;
+  uint32_t* err;
+};
+
+// A CTA's share of one op: chunks [c0, c1) of U = nblk * ktiles, split over min(G, U) CTAs.
+struct ChainRange {
+  int U, G, c0, c1;
+};
+__device__ __forceinline__ int chain_begin(int b, int U, int G) { return (int)(((int64_t)b * U) / G); }
+__device__ __forceinline__ int chain_cta_of(int u, int U, int G) { return (int)((((int64_t)u + 1) * G - 1) / U); }
+__device__ __forceinline__ ChainRange chain_range(const ChainOp& op, int b, int grid) {
+  ChainRange r;
+  r.U = op.nblk * op.ktiles;
+  r.G = min(grid, r.U);
+  r.c0 = b < r.G ? chain_begin(b, r.U, r.G) : 0;
+  r.c1 = b < r.G ? chain_begin(b + 1, r.U, r.G) : 0;
+  return r;
+}
+// Kind of the segment of n-block nb inside range r.
+enum ChainSeg { kSegDirect = 0, kSegPart0 = 1, kSegPartial = 2 };
+__device__ __forceinline__ int chain_seg_kind(const ChainOp& op, const ChainRange& r, int nb, int* part, int* nparts) {
+  const int KT = op.ktiles;
+  const int first = chain_cta_of(nb * KT, r.U, r.G), last = chain_cta_of(nb * KT + KT - 1, r.U, r.G);
+  *nparts = last - first + 1;
+  *part = (int)blockIdx.x - first;
+  if (first == last) return kSegDirect;
+  return *part == 0 ? kSegPart0 : kSegPartial;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_relaxed_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// Bounded spin until *p >= target (acquire); false on expiry.
+__device__ __forceinline__ bool wait_count(const uint32_t* p, uint32_t target) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
+  while (ld_acquire_gpu(p) < target) {
+    if (globaltimer_ns() > deadline) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+// 16-byte global -> shared copy through L2 (no L1: the source may have been written by other CTAs
+// of this launch), asynchronous until cp_async_wait_all.
+__device__ __forceinline__ void cp_async_cg16(void* dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+struct ChainSmem {
+  uint8_t* ring;
+  uint8_t* xbuf;
+  float4* ev;   // [2] part-0 sums for the reducer
+  float4* pub;  // [2] finished segments for the publisher
+  uint64_t *full, *empty, *xfull, *xempty, *evfull, *evempty, *pubfull, *pubempty;
+  const ChainOp* ops;  // op descriptor cache (the first kChainCachedOps)
+  int* fail;
+};
+__device__ __forceinline__ ChainOp chain_op_at(const ChainParams& p, const ChainSmem& sm, int i) {
+  return i < kChainCachedOps ? sm.ops[i] : p.ops[i];
+}
+
+// fp32 sums of one 16-row sub-tile (lane layout of gemv_tile: rows g, g+8; tokens 2t, 2t+1 per
+// 8-token group) -> fp16 y.
+template <int MG>
+__device__ __forceinline__ void chain_store_y(const ChainOp& op, int nb, int sub, const float (&v)[MG][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int n0 = nb * 128 + sub * 16 + g;
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg) {
+    const int tok = mg * 8 + 2 * t;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int m = tok + (e & 1);
+      const int nn = n0 + ((e >> 1) << 3);
+      if (m < op.M && nn < op.N) op.y[(int64_t)m * op.N + nn] = __float2half_rn(v[mg][e]);
+    }
+  }
+}
+
+// ---- consumers: end of an n-block segment -----------------------------------------------------------
+template <int MG>
+__device__ __forceinline__ bool chain_flush(const ChainOp& op, const ChainRange& r, const ChainParams& p,
+                                            const ChainSmem& sm, int nb, float (&acc)[MG][4], int& evk, int& pubk) {
+  const int sub = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int part, nparts;
+  const int kind = chain_seg_kind(op, r, nb, &part, &nparts);
+  float4* dst;
+  uint64_t* full;
+  if (kind == kSegPart0) {
+    const int e = evk & 1;
+    if (evk >= 2 && !mbar_wait(sm.evempty + e, (uint32_t)((evk >> 1) - 1) & 1u)) return false;
+    dst = sm.ev + (size_t)e * (kChainSegBytes / 16);
+    full = sm.evfull + e;
+    ++evk;
+  } else {
+    const int e = pubk & 1;
+    if (pubk >= 2 && !mbar_wait(sm.pubempty + e, (uint32_t)((pubk >> 1) - 1) & 1u)) return false;
+    dst = sm.pub + (size_t)e * (kChainSegBytes / 16);
+    full = sm.pubfull + e;
+    ++pubk;
+  }
+  dst += (sub * MG) * 32 + lane;
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg) dst[mg * 32] = make_float4(acc[mg][0], acc[mg][1], acc[mg][2], acc[mg][3]);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(full);
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[mg][e] = 0.f;
+  return true;
+}
+
+// ---- consumers: one op ------------------------------------------------------------------------
+template <int MG>
+__device__ bool chain_consume(const ChainOp& op, const ChainRange& r, const ChainParams& p, const ChainSmem& sm,
+                              int& slot, uint32_t& phase, int xk, int& evk, int& pubk) {
+  const int KT = op.ktiles;
+  const int sub = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int xb = xk & 1;
+  if (!mbar_wait(sm.xfull + xb, (uint32_t)(xk >> 1) & 1u) || *(volatile int*)sm.fail) return false;
+  const uint8_t* xs = sm.xbuf + xb * p.x_bytes;
+  bool xok[MG];
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg) xok[mg] = (mg * 8 + g) < op.M;
+  const int xgroup = 8 * op.xrow;
+  const uint8_t* xl = xs + g * op.xrow + 16 * t;
+
+  float acc[MG][4];
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[mg][e] = 0.f;
+  int nb = r.c0 / KT, kt = r.c0 - nb * KT, wpos = 0;
+  for (int g0 = r.c0; g0 < r.c1; g0 += kChainGroup) {
+    const int n = min(kChainGroup, r.c1 - g0);
+    if (!mbar_wait(sm.full + slot, phase)) return false;
+    const uint8_t* ch = sm.ring + slot * kChainSlotBytes;
+    uint4 wv[kChainGroup];
+    uint2 sc[kChainGroup];
+#pragma unroll
+    for (int j = 0; j < kChainGroup; ++j) {
+      if (j < n) {
+        wv[j] = *reinterpret_cast<const uint4*>(ch + j * kChunkWBytes + sub * 512 + lane * 16);
+        sc[j] = *reinterpret_cast<const uint2*>(ch + kChainSlotScales + j * kChunkSBytes + sub * 64 + g * 8);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.empty + slot);
+    if (++slot == p.slots) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    if (kt + n <= KT && wpos + n <= KT) {
+      // fast path: the group lies in one n-block and one stretch of the window; the tiles are
+      // independent, so the compiler can overlap their latencies
+      const uint8_t* xg = xl + wpos * 128;
+      if (n == kChainGroup && (kt + kChainGroup) * 64 <= op.K) {
+#pragma unroll
+        for (int j = 0; j < kChainGroup; ++j) gemv_tile<MG>(wv[j], sc[j], xg + j * 128, xgroup, true, xok, acc);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kChainGroup; ++j)
+          if (j < n) gemv_tile<MG>(wv[j], sc[j], xg + j * 128, xgroup, (kt + j) * 64 + 32 < op.K, xok, acc);
+      }
+      kt += n;
+      wpos += n;
+      if (wpos == KT) wpos = 0;
+      if (kt == KT || g0 + n == r.c1) {
+        if (!chain_flush<MG>(op, r, p, sm, nb, acc, evk, pubk)) return false;
+      }
+      if (kt == KT) {
+        kt = 0;
+        ++nb;
+      }
+    } else {
+      // the group crosses an n-block boundary or wraps the window: one chunk at a time
+      for (int j = 0; j < n; ++j) {
+        const int c = g0 + j;
+        gemv_tile<MG>(wv[j], sc[j], xl + wpos * 128, xgroup, kt * 64 + 32 < op.K, xok, acc);
+        if (kt == KT - 1 || c == r.c1 - 1) {
+          if (!chain_flush<MG>(op, r, p, sm, nb, acc, evk, pubk)) return false;
+        }
+        if (++kt == KT) {
+          kt = 0;
+          ++nb;
+        }
+        if (++wpos == KT) wpos = 0;  // window position of the next chunk: (c + 1 - c0) mod KT
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(sm.xempty + xb);
+  return true;
+}
+
+// ---- publisher: one op's direct and partial segments, in the consumers' order ------------------------
+template <int MG>
+__device__ bool chain_publish_op(const ChainOp& op, const ChainRange& r, const ChainParams& p, const ChainSmem& sm,
+                                 int i, int& pubk) {
+  const int lane = threadIdx.x & 31, KT = op.ktiles;
+  for (int c = r.c0; c < r.c1;) {
+    const int nb = c / KT;
+    c = min(r.c1, (nb + 1) * KT);
+    int part, nparts;
+    const int kind = chain_seg_kind(op, r, nb, &part, &nparts);
+    if (kind == kSegPart0) continue;  // the reducer's
+    const int e = pubk & 1;
+    if (!mbar_wait(sm.pubfull + e, (uint32_t)(pubk >> 1) & 1u)) return false;
+    const float4* src = sm.pub + (size_t)e * (kChainSegBytes / 16) + lane;
+    if (kind == kSegDirect) {
+      for (int sub = 0; sub < 8; ++sub) {
+        float v[MG][4];
+#pragma unroll
+        for (int mg = 0; mg < MG; ++mg) {
+          const float4 f = src[(sub * MG + mg) * 32];
+          v[mg][0] = f.x;
+          v[mg][1] = f.y;
+          v[mg][2] = f.z;
+          v[mg][3] = f.w;
+        }
+        chain_store_y<MG>(op, nb, sub, v);
+      }
+    } else {
+      float4* dst = reinterpret_cast<float4*>(op.partials) + lane;
+      for (int sub = 0; sub < 8; ++sub) {
+        const size_t base = ((((size_t)nb * 8 + sub) * op.maxparts) + part) * MG * 32;
+#pragma unroll
+        for (int mg = 0; mg < MG; ++mg) __stcg(dst + base + mg * 32, src[(sub * MG + mg) * 32]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.pubempty + e);
+    ++pubk;
+    fence_acq_rel_gpu();  // this warp's stores above, then the counter bumps (release pattern)
+    if (kind == kSegDirect) {
+      if (lane == 0) red_relaxed_gpu(p.op_done + i, 8u);
+    } else {
+      if (lane < 8) red_relaxed_gpu(op.tickets + nb * 8 + lane, 1u);
+    }
+  }
+  return true;
+}
+
+// ---- reducer: the split n-block whose part 0 this CTA holds ---------------------------------------
+template <int MG>
+__device__ bool chain_reduce(const ChainOp& op, const ChainRange& r, const ChainParams& p, const ChainSmem& sm, int i,
+                             int nb, int nparts, int evk) {
+  const int lane = threadIdx.x & 31;
+  const int e = evk & 1;
+  if (!mbar_wait(sm.evfull + e, (uint32_t)(evk >> 1) & 1u)) return false;
+  bool ok = true;
+  if (lane < 8) ok = wait_count(op.tickets + nb * 8 + lane, (uint32_t)(nparts - 1));
+  ok = __all_sync(0xffffffffu, ok);
+  __syncwarp();  // lanes 0-7 acquired the counters; order the whole warp's loads after them
+  if (!ok) return false;
+  float out[8][MG][4];
+  const float4* own = sm.ev + (size_t)e * (kChainSegBytes / 16) + lane;
+#pragma unroll
+  for (int sub = 0; sub < 8; ++sub)
+#pragma unroll
+    for (int mg = 0; mg < MG; ++mg) {
+      const float4 v = own[(sub * MG + mg) * 32];
+      out[sub][mg][0] = v.x;
+      out[sub][mg][1] = v.y;
+      out[sub][mg][2] = v.z;
+      out[sub][mg][3] = v.w;
+    }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(sm.evempty + e);  // part 0 is in registers now
+  const float4* src = reinterpret_cast<const float4*>(op.partials) + lane;
+  for (int q = 1; q < nparts; ++q) {  // parts added in order 1, 2, ...: one round trip per part
+    float4 v[8][MG];
+#pragma unroll
+    for (int sub = 0; sub < 8; ++sub)
+#pragma unroll
+      for (int mg = 0; mg < MG; ++mg) v[sub][mg] = __ldcg(src + ((((size_t)nb * 8 + sub) * op.maxparts + q) * MG + mg) * 32);
+#pragma unroll
+    for (int sub = 0; sub < 8; ++sub)
+#pragma unroll
+      for (int mg = 0; mg < MG; ++mg) {
+        out[sub][mg][0] += v[sub][mg].x;
+        out[sub][mg][1] += v[sub][mg].y;
+        out[sub][mg][2] += v[sub][mg].z;
+        out[sub][mg][3] += v[sub][mg].w;
+      }
+  }
+#pragma unroll
+  for (int sub = 0; sub < 8; ++sub) chain_store_y<MG>(op, nb, sub, out[sub]);
+  if (lane < 8) op.tickets[nb * 8 + lane] = 0u;  // every part has arrived: ready for the next run
+  fence_acq_rel_gpu();
+  if (lane == 0) red_relaxed_gpu(p.op_done + i, 8u);
+  return true;
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_fail;
+  __shared__ __align__(16) ChainOp s_ops[kChainCachedOps];
+  ChainSmem sm;
+  sm.ring = smem;
+  sm.xbuf = smem + p.x_off;
+  sm.ev = reinterpret_cast<float4*>(smem + p.ev_off);
+  sm.pub = sm.ev + 2 * (kChainSegBytes / 16);
+  sm.full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+  sm.empty = sm.full + p.slots;
+  sm.xfull = sm.empty + p.slots;
+  sm.xempty = sm.xfull + 2;
+  sm.evfull = sm.xempty + 2;
+  sm.evempty = sm.evfull + 2;
+  sm.pubfull = sm.evempty + 2;
+  sm.pubempty = sm.pubfull + 2;
+  sm.ops = s_ops;
+  sm.fail = &s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, b = blockIdx.x;
+  {
+    const int ncached = min(p.nops, kChainCachedOps) * (int)(sizeof(ChainOp) / 4);
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.ops);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(s_ops);
+    for (int q = threadIdx.x; q < ncached; q += kChainThreads) dst[q] = src[q];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.slots; ++s) {
+      mbar_init(sm.full + s, 1);
+      mbar_init(sm.empty + s, kChainConsumers);
+    }
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(sm.xfull + k, 1);
+      mbar_init(sm.xempty + k, kChainConsumers);
+      mbar_init(sm.evfull + k, kChainConsumers);
+      mbar_init(sm.evempty + k, 1);
+      mbar_init(sm.pubfull + k, kChainConsumers);
+      mbar_init(sm.pubempty + k, 1);
+    }
+    fence_mbar_init();
+    s_fail = 0;
+  }
+  __syncthreads();
+
+  bool ok = true;
+  if (warp == kChainProducerWarp) {
+    // ---------------- producer: the CTA's chunks of every op, in order ----------------
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int seq = 0;
+      for (int i = 0; i < p.nops && ok; ++i) {
+        const ChainOp op = chain_op_at(p, sm, i);
+        const ChainRange r = chain_range(op, b, G);
+        for (int g0 = r.c0; g0 < r.c1; g0 += kChainGroup, ++seq) {
+          const int n = min(kChainGroup, r.c1 - g0);
+          const int slot = seq % p.slots;
+          if ((seq >= p.slots && !mbar_wait(sm.empty + slot, (uint32_t)((seq / p.slots) - 1) & 1u)) ||
+              *(volatile int*)&s_fail) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = sm.ring + slot * kChainSlotBytes;
+          mbar_arrive_expect_tx(sm.full + slot, (uint32_t)n * (kChunkWBytes + kChunkSBytes));
+          bulk_g2s(dst, op.wq + (int64_t)g0 * kChunkWBytes, (uint32_t)n * kChunkWBytes, sm.full + slot, pol);
+          bulk_g2s(dst + kChainSlotScales, op.ws + (int64_t)g0 * kChunkSBytes, (uint32_t)n * kChunkSBytes, sm.full + slot,
+                   pol);
+        }
+      }
+      if (!ok) {
+        // copies still in flight land before the CTA exits (bounded)
+        const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
+        const int first = seq > p.slots ? seq - p.slots : 0;
+        for (int q = first; q < seq; ++q)
+          if (!mbar_wait_until(sm.full + (q % p.slots), (uint32_t)(q / p.slots) & 1u, deadline)) break;
+      }
+    }
+  } else if (warp == kChainStagerWarp) {
+    // ---------------- stager: dependency wait + activation window, one op ahead ----------------
+    int xk = 0;
+    for (int i = 0; i < p.nops && ok; ++i) {
+      const ChainOp op = chain_op_at(p, sm, i);
+      const ChainRange r = chain_range(op, b, G);
+      if (r.c0 >= r.c1) continue;
+      const int xb = xk & 1;
+      ok = !(xk >= 2 && !mbar_wait(sm.xempty + xb, (uint32_t)((xk >> 1) - 1) & 1u));
+      if (ok && op.dep >= 0) {
+        const ChainOp d = chain_op_at(p, sm, op.dep);
+        if (lane == 0) ok = wait_count(p.op_done + op.dep, (uint32_t)d.nblk * 8u);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __syncwarp();  // lane 0's acquire, then the warp's loads (memory-ordering warp barrier)
+      }
+      if (!ok || *(volatile int*)&s_fail) {
+        ok = false;
+        break;
+      }
+      const int KT = op.ktiles;
+      const int kt_start = r.c0 % KT;
+      const int n_win = min(r.c1 - r.c0, KT);
+      const int per_row = n_win * 8;
+      uint8_t* xs = sm.xbuf + xb * p.x_bytes;
+      for (int q = lane; q < op.M * per_row; q += 32) {
+        const int row = q / per_row, j = q - row * per_row;
+        const int w = j >> 3, e = j & 7;
+        int kt = kt_start + w;
+        if (kt >= KT) kt -= KT;
+        const int k = kt * 64 + e * 8;
+        // pieces past K (second half of a last half k-tile) are never read by the tile math
+        if (k < op.K) cp_async_cg16(xs + row * op.xrow + w * 128 + e * 16, op.x + (int64_t)row * op.K + k);
+      }
+      cp_async_wait_all();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.xfull + xb);
+      ++xk;
+    }
+  } else if (warp == kChainPublisherWarp) {
+    // ---------------- publisher ----------------
+    int pubk = 0;
+    for (int i = 0; i < p.nops && ok; ++i) {
+      const ChainOp op = chain_op_at(p, sm, i);
+      const ChainRange r = chain_range(op, b, G);
+      if (r.c0 >= r.c1) continue;
+      ok = op.M > 8 ? chain_publish_op<2>(op, r, p, sm, i, pubk) : chain_publish_op<1>(op, r, p, sm, i, pubk);
+    }
+  } else if (warp == kChainReducerWarp) {
+    // ---------------- reducer ----------------
+    int evk = 0;
+    for (int i = 0; i < p.nops && ok; ++i) {
+      const ChainOp op = chain_op_at(p, sm, i);
+      const ChainRange r = chain_range(op, b, G);
+      if (r.c0 >= r.c1) continue;
+      const int nb = (r.c1 - 1) / op.ktiles;  // only the last segment of a range can be a part 0
+      int part, nparts;
+      if (chain_seg_kind(op, r, nb, &part, &nparts) != kSegPart0) continue;
+      ok = op.M > 8 ? chain_reduce<2>(op, r, p, sm, i, nb, nparts, evk) : chain_reduce<1>(op, r, p, sm, i, nb, nparts, evk);
+      ++evk;
+    }
+  } else {
+    // ---------------- consumers ----------------
+    int slot = 0, xk = 0, evk = 0, pubk = 0;
+    uint32_t phase = 0;
+    for (int i = 0; i < p.nops && ok; ++i) {
+      const ChainOp op = chain_op_at(p, sm, i);
+      const ChainRange r = chain_range(op, b, G);
+      if (r.c0 >= r.c1) continue;
+      ok = op.M > 8 ? chain_consume<2>(op, r, p, sm, slot, phase, xk, evk, pubk)
+                    : chain_consume<1>(op, r, p, sm, slot, phase, xk, evk, pubk);
+      ++xk;
+    }
+  }
+  if (!ok && lane == 0) {
+    set_error(p.err, kErrWaitTimeout);
+    s_fail = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(p.exit_count, 1u);
+    if (prev == (uint32_t)(G - 1)) {  // last CTA of the run: completion counters back to zero
+      __threadfence();
+      for (int i = 0; i < p.nops; ++i) p.op_done[i] = 0u;
+      *p.exit_count = 0u;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace s4
+
+// ---- host side -------------------------------------------------------------------------------------
+using s4::ChainOp;
+
+struct s4_chain {
+  s4_ctx* ctx;
+  int nops;
+  int grid;
+  int slots;
+  int x_off, x_bytes, ev_off, bar_off, smem;
+  ChainOp* d_ops;
+  uint8_t* d_scratch;  // partials, tickets, op_done, exit_count
+  uint32_t* op_done;
+  uint32_t* exit_count;
+  std::vector<ChainOp> ops;
+};
+
+namespace s4 {
+
+int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y, const int* M,
+                 const int* dep, s4_chain** out, const char** why) {
+  *why = nullptr;
+  const int G = ctx->sm_count;
+  std::vector<ChainOp> ops(nops);
+  size_t scratch = 0;
+  int xmax = 0;
+  std::vector<size_t> part_off(nops), tick_off(nops);
+  for (int i = 0; i < nops; ++i) {
+    const s4_weight* wi = w[i];
+    ChainOp& o = ops[i];
+    o.wq = wi->wq;
+    o.ws = wi->ws;
+    o.x = static_cast<const __half*>(x[i]);
+    o.y = static_cast<__half*>(y[i]);
+    o.M = M[i];
+    o.N = wi->N;
+    o.K = wi->K;
+    o.nblk = wi->nblk;
+    o.ktiles = wi->ktiles;
+    o.dep = dep ? dep[i] : -1;
+    if (o.M < 1 || o.M > 16) return *why = "every op needs 1 <= M <= 16", S4_ERR_INVALID;
+    if (o.dep >= i || o.dep < -1) return *why = "dep must name an earlier op or be -1", S4_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(x[i]) & 15) || (o.K * 2) % 16) return *why = "x must be 16-byte aligned", S4_ERR_INVALID;
+    const int U = o.nblk * o.ktiles;
+    const int Gop = U < G ? U : G;
+    const int per_cta = (U + Gop - 1) / Gop;
+    const int min_cta = U / Gop;  // >= 1
+    o.maxparts = (o.ktiles + min_cta - 1) / min_cta + 1;  // CTAs one n-block can span
+    if (o.maxparts > Gop) o.maxparts = Gop;
+    const int n_win = per_cta < o.ktiles ? per_cta : o.ktiles;
+    o.xrow = n_win * 128 + 64;
+    const int xb = o.M * o.xrow;
+    if (xb > xmax) xmax = xb;
+    const int MG = o.M > 8 ? 2 : 1;
+    part_off[i] = scratch;
+    scratch += (size_t)o.nblk * 8 * o.maxparts * MG * 32 * 16;
+    tick_off[i] = scratch;
+    scratch += (size_t)o.nblk * 8 * 4;
+    scratch = (scratch + 255) & ~(size_t)255;
+  }
+  xmax = (xmax + 127) & ~127;
+  const int fixed = 2 * xmax + 4 * kChainSegBytes + 12 * 8 + 256;
+  int slots = (kChainSmemBudget - fixed - 2 * kChainMaxSlots * 8) / kChainSlotBytes;
+  if (slots > kChainMaxSlots) slots = kChainMaxSlots;
+  if (slots < kChainMinSlots) return *why = "activation window too large for shared memory (M * K range)", S4_ERR_UNSUPPORTED;
+
+  s4_chain* c = new s4_chain();
+  c->ctx = ctx;
+  c->nops = nops;
+  c->grid = G;
+  c->slots = slots;
+  c->x_off = slots * kChainSlotBytes;
+  c->x_bytes = xmax;
+  c->ev_off = c->x_off + 2 * xmax;
+  c->bar_off = c->ev_off + 4 * kChainSegBytes;
+  c->smem = c->bar_off + (2 * slots + 12) * 8;
+  const size_t ctr_off = scratch;
+  scratch += (size_t)(nops + 1) * 4;
+  cudaError_t e = cudaMalloc(&c->d_scratch, scratch);
+  if (e == cudaSuccess) e = cudaMemset(c->d_scratch, 0, scratch);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_ops, sizeof(ChainOp) * nops);
+  if (e != cudaSuccess) {
+    cudaFree(c->d_scratch);
+    delete c;
+    return *why = "device allocation failed", S4_ERR_NOMEM;
+  }
+  for (int i = 0; i < nops; ++i) {
+    ops[i].partials = reinterpret_cast<float*>(c->d_scratch + part_off[i]);
+    ops[i].tickets = reinterpret_cast<uint32_t*>(c->d_scratch + tick_off[i]);
+  }
+  c->op_done = reinterpret_cast<uint32_t*>(c->d_scratch + ctr_off);
+  c->exit_count = c->op_done + nops;
+  e = cudaMemcpy(c->d_ops, ops.data(), sizeof(ChainOp) * nops, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(c->d_ops);
+    cudaFree(c->d_scratch);
+    delete c;
+    return *why = "op table upload failed", S4_ERR_CUDA;
+  }
+  c->ops = ops;
+  *out = c;
+  return S4_OK;
+}
+
+cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kChainSmemBudget);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  ChainParams p;
+  p.ops = c->d_ops;
+  p.nops = c->nops;
+  p.slots = c->slots;
+  p.x_off = c->x_off;
+  p.x_bytes = c->x_bytes;
+  p.ev_off = c->ev_off;
+  p.bar_off = c->bar_off;
+  p.op_done = c->op_done;
+  p.exit_count = c->exit_count;
+  p.err = err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c->grid, 1, 1);
+  cfg.blockDim = dim3(kChainThreads, 1, 1);
+  cfg.dynamicSmemBytes = c->smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, chain_kernel, p);
+}
+
+void chain_destroy(s4_chain* c) {
+  cudaFree(c->d_ops);
+  cudaFree(c->d_scratch);
+  delete c;
+}
+
+int chain_info(const s4_chain* c, int* grid, int* slots, int* smem) {
+  if (grid) *grid = c->grid;
+  if (slots) *slots = c->slots;
+  if (smem) *smem = c->smem;
+  return S4_OK;
+}
+
+}  // namespace s4

@@ -128,7 +128,8 @@ __device__ __forceinline__ float4 ldcg_f4(const float4* p) { return __ldcg(p); }
 // D = A(16x16 f16, row) * B(16x8 f16, col) + C, f32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
-  asm volatile(
+  // not volatile: no side effects, so the compiler may interleave independent MMAs with other work
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

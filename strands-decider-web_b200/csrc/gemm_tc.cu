@@ -17,7 +17,7 @@
 // instead lets the last CTA to arrive at the tile do it, through an atomic ticket).
 //
 // Warp roles (512 threads): warp 0 lane 0 streams raw int4 chunks (1-D bulk copies) into a
-// 12-slot ring; warp 2 lane 0 loads activation tiles by TMA into a 3-stage ring; warp 1 owns TMEM
+// kTcSlotsW-slot ring; warp 2 lane 0 loads activation tiles by TMA into a kTcStagesX-stage ring; warp 1 owns TMEM
 // and lane 0 issues the MMAs; warps 4-11 dequantise int4 -> fp16 into the MMA's A stage; warps
 // 12-15 drain TMEM (double-buffered accumulators) and write the output.
 #include <cuda.h>
@@ -30,7 +30,8 @@
 namespace s4 {
 
 constexpr int kTcMaxTn = 256;
-constexpr int kTcStagesA = 3;
+constexpr int kTcStagesX = 3;  // activation tiles (TMA) ring
+constexpr int kTcStagesA = 3;  // dequantised weight (MMA operand A) ring
 constexpr int kTcSlotsW = 12;
 constexpr int kTcThreads = 512;
 constexpr int kTcDequantWarps = 8;  // warps 4..11
@@ -39,14 +40,15 @@ constexpr int kTcXStageBytes = kTcMaxTn * 128;  // tn rows x 64 fp16
 constexpr int kTcAStageBytes = 128 * 128;       // 128 rows x 64 fp16
 constexpr int kTcWSlotBytes = kChunkWBytes + kChunkSBytes;
 constexpr int kTcOffX = 0;
-constexpr int kTcOffA = kTcOffX + kTcStagesA * kTcXStageBytes;
+constexpr int kTcOffA = kTcOffX + kTcStagesX * kTcXStageBytes;
 constexpr int kTcOffW = kTcOffA + kTcStagesA * kTcAStageBytes;
 constexpr int kTcOffBar = kTcOffW + kTcSlotsW * kTcWSlotBytes;
-constexpr int kTcNumBars = 3 * kTcStagesA + 2 * kTcSlotsW + 2 + 2 + 1;
+constexpr int kTcNumBars = 2 * kTcStagesX + 2 * kTcStagesA + 2 * kTcSlotsW + 2 + 2 + 1;
 constexpr int kTcOffMisc = kTcOffBar + kTcNumBars * 8;
 constexpr int kTcOffEpi = (kTcOffMisc + 64 + 127) & ~127;  // epilogue staging: 4 warps x 16 tokens x 32 n fp16
 constexpr int kTcEpiStageBytes = 16 * 32 * 2;
 constexpr size_t kTcSmem = (size_t)kTcOffEpi + 4 * kTcEpiStageBytes + 1024;  // + alignment slack
+static_assert(kTcSmem <= 227 * 1024, "tcgen05 GEMM shared memory above the per-CTA limit");
 constexpr uint32_t kTcTmemCols = 512;                       // two 256-column accumulators
 
 constexpr int kTcMaxDst = 8;  // output copies one launch writes (this GPU + peers)
@@ -155,7 +157,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   uint8_t* wraw = smem + kTcOffW;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
   uint64_t* full_x = bars;
-  uint64_t* ddone = full_x + kTcStagesA;
+  uint64_t* empty_x = full_x + kTcStagesX;
+  uint64_t* ddone = empty_x + kTcStagesX;
   uint64_t* empty_a = ddone + kTcStagesA;
   uint64_t* full_w = empty_a + kTcStagesA;
   uint64_t* empty_w = full_w + kTcSlotsW;
@@ -171,8 +174,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   const int KT = p.ktiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStagesA; ++s) {
+    for (int s = 0; s < kTcStagesX; ++s) {
       mbar_init(full_x + s, 1);
+      mbar_init(empty_x + s, 1);
+    }
+    for (int s = 0; s < kTcStagesA; ++s) {
       mbar_init(ddone + s, kTcDequantWarps);
       mbar_init(empty_a + s, 1);
     }
@@ -235,8 +241,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       bool ok = true;
       const uint32_t xbytes = (uint32_t)p.tn * 128u;
       for (int i = 0; i < n; ++i) {
-        const int s = i % kTcStagesA;
-        if (i >= kTcStagesA && !mbar_wait(empty_a + s, ((i / kTcStagesA) - 1) & 1)) {
+        const int s = i % kTcStagesX;
+        if (i >= kTcStagesX && !mbar_wait(empty_x + s, ((i / kTcStagesX) - 1) & 1)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
           break;
@@ -250,8 +256,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
-        for (int i = (issued > kTcStagesA ? issued - kTcStagesA : 0); i < issued; ++i)
-          if (!mbar_wait_until(full_x + (i % kTcStagesA), (i / kTcStagesA) & 1, deadline)) break;
+        for (int i = (issued > kTcStagesX ? issued - kTcStagesX : 0); i < issued; ++i)
+          if (!mbar_wait_until(full_x + (i % kTcStagesX), (i / kTcStagesX) & 1, deadline)) break;
       }
     }
   } else if (warp == 1) {
@@ -274,20 +280,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)(buf * 256);
         for (int u = u0; u < seg_end; ++u, ++i) {
-          const int s = i % kTcStagesA;
-          const uint32_t par = (i / kTcStagesA) & 1;
-          if (!mbar_wait(full_x + s, par) || !mbar_wait(ddone + s, par)) {
+          const int sx = i % kTcStagesX, s = i % kTcStagesA;
+          if (!mbar_wait(full_x + sx, (i / kTcStagesX) & 1) || !mbar_wait(ddone + s, (i / kTcStagesA) & 1)) {
             set_error(p.err, kErrWaitTimeout);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(wa + s * kTcAStageBytes), b0 = smem_u32(xs + s * kTcXStageBytes);
+          const uint32_t a0 = smem_u32(wa + s * kTcAStageBytes), b0 = smem_u32(xs + sx * kTcXStageBytes);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             tc_mma(dcol, sw128_kmajor_desc(a0 + j * 32), sw128_kmajor_desc(b0 + j * 32), idesc,
                    (u != u0 || j > 0) ? 1u : 0u);
           tc_commit(empty_a + s);
+          tc_commit(empty_x + sx);
         }
         if (!ok) break;
         tc_commit(accf + buf);

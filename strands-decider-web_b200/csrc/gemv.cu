@@ -8,17 +8,21 @@
 //  * one thread-block cluster of S CTAs per n-block of 128 output rows; CTA r of the cluster
 //    takes k-tiles [r*KT/S, (r+1)*KT/S). S is chosen so that about two CTAs land on every SM,
 //    leaving room for some of the next launch's CTAs (programmatic dependent launch).
-//  * warp w of a CTA owns rows w*16 .. w*16+15. Each k-tile of its sub-tile is one coalesced
-//    512-byte line whose 16-byte lane slices are its mma.sync A fragments (weights as the 16-row
-//    operand, tokens as the 8 columns). Weights go straight to registers with non-coherent
-//    loads, four k-tiles per batch, double-buffered; the first batch is issued before the wait on
-//    the previous kernel, since weights do not depend on it.
+//  * a CTA's weights and scales are one contiguous span of the repacked layout (its k-tiles of one
+//    n-block). Thread 0 requests all of it at kernel start with 1-D bulk copies (TMA engine, no
+//    multicast) into shared memory, in groups of four k-tiles with one mbarrier each, before the
+//    wait on the previous kernel (weights do not depend on it): every byte of the launch is in
+//    flight at once, so DRAM latency is paid once per launch instead of once per batch per warp.
+//  * warp w of a CTA owns rows w*16 .. w*16+15. Each k-tile of its sub-tile is a 512-byte line
+//    whose 16-byte lane slices are its mma.sync A fragments (weights as the 16-row operand, tokens
+//    as the 8 columns), read from shared memory without bank conflicts.
 //  * activations (<= 16 rows x the CTA's K range) are staged once into padded shared-memory rows.
 //  * int4 is converted to exact fp16 (q - 8) and the block scale is applied in fp32 to the fp32
 //    block partial, so the only roundings are fp32 accumulation and the final fp16 store.
 //  * the S partials of an n-block are summed in rank order by rank 0 through distributed shared
 //    memory between two cluster barriers: deterministic, no global scratch, no atomics.
 #include "common.cuh"
+#include "gemv_tile.cuh"
 
 namespace s4 {
 
@@ -32,6 +36,9 @@ struct GemvParams {
   int nblk, ktiles;
   int split;          // S: CTAs per cluster / k-splits per n-block
   int token0;         // first token of this launch (tokens token0 .. token0 + 8*MG - 1)
+  // dynamic shared memory layout (bytes), from gemv_layout()
+  int s_off, x_off, red_off, bar_off;
+  int xrow;           // padded activation row: 128 bytes per k-tile + 64
 };
 
 constexpr int kGemvWarps = 8;                 // one per 16-row sub-tile of the n-block
@@ -39,11 +46,25 @@ constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kGemvMaxGroups = 2;             // GEMV serves M <= 16
 constexpr int kGemvMaxKtPerCta = 16;          // activation staging: <= 16 k-tiles per CTA
 constexpr int kGemvMaxSplit = 16;             // non-portable cluster size limit
-constexpr int kGemvBatch = 4;                 // k-tiles per load batch
-constexpr int kGemvXRow = kGemvMaxKtPerCta * 128 + 64;  // padded row (rows alternate bank halves)
-constexpr int kGemvXBytes = 8 * kGemvMaxGroups * kGemvXRow;
-constexpr int kGemvRedBytes = kGemvWarps * 32 * 16 * kGemvMaxGroups;
-constexpr size_t kGemvSmem = (size_t)kGemvXBytes + kGemvRedBytes;
+constexpr int kGemvGroup = 4;                 // k-tiles per bulk-copy group (one mbarrier each)
+constexpr int kGemvMaxCopyGroups = kGemvMaxKtPerCta / kGemvGroup;
+
+// Shared memory of one CTA holding at most `nkt` k-tiles for MG token groups: weights, scales,
+// activation rows (64 bytes of padding per row: consecutive rows start 16 banks apart),
+// reduction partials, mbarriers.
+struct GemvLayout {
+  int s_off, x_off, red_off, bar_off, total, xrow;
+};
+static GemvLayout gemv_layout(int nkt, int MG) {
+  GemvLayout L;
+  L.xrow = nkt * 128 + 64;
+  L.s_off = nkt * kChunkWBytes;
+  L.x_off = L.s_off + nkt * kChunkSBytes;
+  L.red_off = L.x_off + 8 * MG * L.xrow;
+  L.bar_off = L.red_off + kGemvWarps * 32 * 16 * MG;
+  L.total = L.bar_off + kGemvMaxCopyGroups * 8;
+  return L;
+}
 
 __device__ __forceinline__ uint32_t cluster_map(const void* p, uint32_t rank) {
   uint32_t r;
@@ -61,63 +82,37 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// One k-tile of one sub-tile: w = lane's 16 bytes (words (g,b0) (g+8,b0) (g,b1) (g+8,b1)),
-// sc = scales in the same order, xrow = this lane's activation row at the k-tile.
-template <int MG>
-__device__ __forceinline__ void gemv_tile(const uint4 w, const uint2 sc, const uint8_t* xrow, bool kin1,
-                                          const bool (&xok)[MG], float (&acc)[MG][4]) {
-  const uint32_t wr[4] = {w.x, w.y, w.z, w.w};
-  const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&sc.x));
-  const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&sc.y));
-#pragma unroll
-  for (int blk = 0; blk < 2; ++blk) {
-    uint32_t ha[4], hb[4];
-    i4x8_to_h2x4_centered(wr[2 * blk + 0], ha);  // row g
-    i4x8_to_h2x4_centered(wr[2 * blk + 1], hb);  // row g + 8
-    const float sg = blk ? s1.x : s0.x, sg8 = blk ? s1.y : s0.y;
-#pragma unroll
-    for (int mg = 0; mg < MG; ++mg) {
-      uint4 xv = make_uint4(0, 0, 0, 0);
-      if (xok[mg] && (blk == 0 || kin1))
-        xv = *reinterpret_cast<const uint4*>(xrow + mg * 8 * kGemvXRow + blk * 64);
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma_16816(d, ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
-      mma_16816(d, ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
-      acc[mg][0] = fmaf(sg, d[0], acc[mg][0]);
-      acc[mg][1] = fmaf(sg, d[1], acc[mg][1]);
-      acc[mg][2] = fmaf(sg8, d[2], acc[mg][2]);
-      acc[mg][3] = fmaf(sg8, d[3], acc[mg][3]);
-    }
-  }
-}
-
 template <int MG>
 __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* xs = smem;
-  float4* red = reinterpret_cast<float4*>(smem + kGemvXBytes);
+  uint8_t* wsm = smem;
+  uint8_t* ssm = smem + p.s_off;
+  uint8_t* xs = smem + p.x_off;
+  float4* red = reinterpret_cast<float4*>(smem + p.red_off);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
 
   const int S = p.split, KT = p.ktiles;
   const int rank = blockIdx.x % S, nb = blockIdx.x / S;
   const int kt0 = (int)(((int64_t)rank * KT) / S), kt1 = (int)(((int64_t)(rank + 1) * KT) / S);
   const int nkt = kt1 - kt0;
+  const int ngroups = (nkt + kGemvGroup - 1) / kGemvGroup;
   const int sub = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int rows = min(8 * MG, p.M - p.token0);
 
-  // this lane's weight and scale streams for the sub-tile, k-tile stride 8 sub-tiles
-  const uint4* wp = reinterpret_cast<const uint4*>(p.wq + ((int64_t)(nb * KT + kt0) * 8 + sub) * 512) + lane;
-  const uint2* sp = reinterpret_cast<const uint2*>(p.ws + ((int64_t)(nb * KT + kt0) * 8 + sub) * 64) + g;
-  constexpr int kWStride = 8 * 512 / 16, kSStride = 8 * 64 / 8;
-
-  uint4 wa[kGemvBatch], wb[kGemvBatch];
-  uint2 sa[kGemvBatch], sb[kGemvBatch];
-#pragma unroll
-  for (int i = 0; i < kGemvBatch; ++i)
-    if (i < nkt) {
-      wa[i] = ldg_nc_v4(wp + i * kWStride);
-      sa[i] = __ldg(sp + i * kSStride);
+  if (threadIdx.x == 0) {
+    // the CTA's whole weight and scale span, in groups of kGemvGroup k-tiles
+    for (int q = 0; q < ngroups; ++q) mbar_init(bars + q, 1);
+    fence_mbar_init();
+    const uint64_t pol = policy_evict_first();  // streamed once
+    const int64_t chunk0 = (int64_t)nb * KT + kt0;
+    for (int q = 0; q < ngroups; ++q) {
+      const int t0 = q * kGemvGroup, nt = min(kGemvGroup, nkt - t0);
+      mbar_arrive_expect_tx(bars + q, (uint32_t)nt * (kChunkWBytes + kChunkSBytes));
+      bulk_g2s(wsm + t0 * kChunkWBytes, p.wq + (chunk0 + t0) * kChunkWBytes, (uint32_t)nt * kChunkWBytes, bars + q, pol);
+      bulk_g2s(ssm + t0 * kChunkSBytes, p.ws + (chunk0 + t0) * kChunkSBytes, (uint32_t)nt * kChunkSBytes, bars + q, pol);
     }
+  }
   pdl_launch_dependents();
   pdl_wait();  // activations are written by the previous kernel in the stream
 
@@ -130,47 +125,35 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
       const int k = kbase + c * 8;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (k < p.K) v = *reinterpret_cast<const uint4*>(p.x + (int64_t)(p.token0 + r) * p.K + k);
-      *reinterpret_cast<uint4*>(xs + r * kGemvXRow + c * 16) = v;
+      *reinterpret_cast<uint4*>(xs + r * p.xrow + c * 16) = v;
     }
   }
-  __syncthreads();
+  __syncthreads();  // also orders the mbarrier initialisation before the waits below
 
   bool xok[MG];
 #pragma unroll
   for (int mg = 0; mg < MG; ++mg) xok[mg] = (mg * 8 + g) < rows;
-  const uint8_t* xl = xs + g * kGemvXRow + 16 * t;  // lane's row, k offset 8t (blk adds 64 bytes)
+  const int xgroup = 8 * p.xrow;
+  const uint8_t* xl = xs + g * p.xrow + 16 * t;  // lane's row, k offset 8t (blk adds 64 bytes)
+  const uint8_t* wl = wsm + sub * 512 + lane * 16;
+  const uint8_t* sl = ssm + sub * 64 + g * 8;
   float acc[MG][4];
 #pragma unroll
   for (int mg = 0; mg < MG; ++mg)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[mg][e] = 0.f;
 
-  for (int b = 0; b < nkt; b += 2 * kGemvBatch) {
-    // second batch in flight while the first is computed, and the other way round
+  for (int q = 0; q < ngroups; ++q) {
+    if (!mbar_wait(bars + q, 0)) set_error(p.err, kErrWaitTimeout);  // results invalid; error reported
 #pragma unroll
-    for (int i = 0; i < kGemvBatch; ++i)
-      if (b + kGemvBatch + i < nkt) {
-        wb[i] = ldg_nc_v4(wp + (b + kGemvBatch + i) * kWStride);
-        sb[i] = __ldg(sp + (b + kGemvBatch + i) * kSStride);
+    for (int i = 0; i < kGemvGroup; ++i) {
+      const int kk = q * kGemvGroup + i;
+      if (kk < nkt) {
+        const uint4 w = *reinterpret_cast<const uint4*>(wl + kk * kChunkWBytes);
+        const uint2 sc = *reinterpret_cast<const uint2*>(sl + kk * kChunkSBytes);
+        gemv_tile<MG>(w, sc, xl + kk * 128, xgroup, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
       }
-#pragma unroll
-    for (int i = 0; i < kGemvBatch; ++i)
-      if (b + i < nkt) {
-        const int kk = b + i;
-        gemv_tile<MG>(wa[i], sa[i], xl + kk * 128, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
-      }
-#pragma unroll
-    for (int i = 0; i < kGemvBatch; ++i)
-      if (b + 2 * kGemvBatch + i < nkt) {
-        wa[i] = ldg_nc_v4(wp + (b + 2 * kGemvBatch + i) * kWStride);
-        sa[i] = __ldg(sp + (b + 2 * kGemvBatch + i) * kSStride);
-      }
-#pragma unroll
-    for (int i = 0; i < kGemvBatch; ++i)
-      if (b + kGemvBatch + i < nkt) {
-        const int kk = b + kGemvBatch + i;
-        gemv_tile<MG>(wb[i], sb[i], xl + kk * 128, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
-      }
+    }
   }
 
   // ---- split-K reduction across the cluster (rank order, deterministic) ----
@@ -228,8 +211,15 @@ static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t strea
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const GemvLayout L = gemv_layout((p.ktiles + p.split - 1) / p.split, MG);
+  p.s_off = L.s_off;
+  p.x_off = L.x_off;
+  p.red_off = L.red_off;
+  p.bar_off = L.bar_off;
+  p.xrow = L.xrow;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(gemv_cluster_kernel<MG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmem);
+    const int max_smem = gemv_layout(kGemvMaxKtPerCta, kGemvMaxGroups).total;
+    e = cudaFuncSetAttribute(gemv_cluster_kernel<MG>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_cluster_kernel<MG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
@@ -237,7 +227,7 @@ static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t strea
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nblk * p.split, 1, 1);
   cfg.blockDim = dim3(kGemvThreads, 1, 1);
-  cfg.dynamicSmemBytes = kGemvSmem;
+  cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
   cudaLaunchAttribute attr[3];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -1,0 +1,38 @@
+// One 16-row x 64-K tile of the decode GEMV math, shared by the per-launch GEMV (gemv.cu) and the
+// chained persistent GEMV (chain.cu). Weights are the 16-row mma.sync operand, tokens the 8 columns.
+#pragma once
+#include "common.cuh"
+
+namespace s4 {
+
+// One k-tile of one sub-tile: w = lane's 16 bytes (words (g,b0) (g+8,b0) (g,b1) (g+8,b1)),
+// sc = scales in the same order, xrow = this lane's activation row at the k-tile.
+template <int MG>
+__device__ __forceinline__ void gemv_tile(const uint4 w, const uint2 sc, const uint8_t* xrow, int xgroup, bool kin1,
+                                          const bool (&xok)[MG], float (&acc)[MG][4]) {
+  const uint32_t wr[4] = {w.x, w.y, w.z, w.w};
+  const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&sc.x));
+  const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&sc.y));
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    uint32_t ha[4], hb[4];
+    i4x8_to_h2x4_centered(wr[2 * blk + 0], ha);  // row g
+    i4x8_to_h2x4_centered(wr[2 * blk + 1], hb);  // row g + 8
+    const float sg = blk ? s1.x : s0.x, sg8 = blk ? s1.y : s0.y;
+#pragma unroll
+    for (int mg = 0; mg < MG; ++mg) {
+      uint4 xv = make_uint4(0, 0, 0, 0);
+      if (xok[mg] && (blk == 0 || kin1))
+        xv = *reinterpret_cast<const uint4*>(xrow + mg * xgroup + blk * 64);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_16816(d, ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
+      mma_16816(d, ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
+      acc[mg][0] = fmaf(sg, d[0], acc[mg][0]);
+      acc[mg][1] = fmaf(sg, d[1], acc[mg][1]);
+      acc[mg][2] = fmaf(sg8, d[2], acc[mg][2]);
+      acc[mg][3] = fmaf(sg8, d[3], acc[mg][3]);
+    }
+  }
+}
+
+}  // namespace s4

@@ -35,6 +35,11 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
                               cudaStream_t stream, bool pdl, bool ticket_fixup);
+int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y, const int* M,
+                 const int* dep, s4_chain** out, const char** why);
+cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream);
+void chain_destroy(s4_chain* c);
+int chain_info(const s4_chain* c, int* grid, int* slots, int* smem);
 bool tc_available();
 size_t tc_partials_bytes(int max_grid);
 cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
@@ -501,6 +506,41 @@ int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, void* str
                                       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
   ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y,
+                    const int* M, const int* dep, s4_chain** out) {
+  if (!ctx || !w || !x || !y || !M || !out) return fail(S4_ERR_INVALID, "NULL argument");
+  if (nops < 1) return fail(S4_ERR_INVALID, "nops must be >= 1 (got %d)", nops);
+  for (int i = 0; i < nops; ++i) {
+    if (!w[i] || !x[i] || !y[i]) return fail(S4_ERR_INVALID, "NULL weight or buffer in op %d", i);
+    if (w[i]->ctx != ctx) return fail(S4_ERR_INVALID, "op %d: weight belongs to another context", i);
+  }
+  DeviceGuard guard(ctx->device);
+  const char* why = nullptr;
+  const int rc = s4::chain_create(ctx, nops, w, x, y, M, dep, out, &why);
+  if (rc != S4_OK) return fail(rc, "chain: %s", why ? why : "failed");
+  return S4_OK;
+}
+
+int s4_chain_run(s4_ctx* ctx, s4_chain* chain, void* stream) {
+  if (!ctx || !chain) return fail(S4_ERR_INVALID, "NULL argument");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = s4::chain_launch(chain, ctx->err, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "chain launch");
+  ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_chain_info(const s4_chain* chain, int* grid, int* slots, int* smem_bytes) {
+  if (!chain) return fail(S4_ERR_INVALID, "NULL chain");
+  return s4::chain_info(chain, grid, slots, smem_bytes);
+}
+
+int s4_chain_free(s4_chain* chain) {
+  if (!chain) return S4_OK;
+  s4::chain_destroy(chain);
   return S4_OK;
 }
 

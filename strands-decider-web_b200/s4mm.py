@@ -48,6 +48,11 @@ _SIGS = {
     "s4_matmul_noalloc": (C.c_int, [_P, _P, C.c_int, _P, _P]),
     "s4_silu_mul": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
     "s4_add_rmsnorm": (C.c_int, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_float, _P, _P]),
+    "s4_chain_create": (C.c_int, [_P, C.c_int, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(C.c_int),
+                                  C.POINTER(C.c_int), C.POINTER(_P)]),
+    "s4_chain_run": (C.c_int, [_P, _P, _P]),
+    "s4_chain_info": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "s4_chain_free": (C.c_int, [_P]),
     "s4_buffer_alloc": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
     "s4_buffer_free": (C.c_int, [_P, _P]),
     "s4_ipc_handle": (C.c_int, [_P, _P, _P]),
@@ -118,6 +123,33 @@ def _stream_handle(stream) -> int | None:
     if isinstance(stream, int):
         return stream
     return stream.cuda_stream
+
+
+class Chain:
+    """A bound list of decode matmuls run by one persistent launch (``s4_chain_*``)."""
+
+    def __init__(self, ctx: "Context", handle: int, ops):
+        self.ctx, self.handle, self.ops = ctx, handle, ops
+
+    def run(self, stream=None):
+        _check(_lib.s4_chain_run(self.ctx.handle, self.handle, _stream_handle(stream)))
+
+    def info(self):
+        g, s, m = C.c_int(), C.c_int(), C.c_int()
+        _check(_lib.s4_chain_info(self.handle, C.byref(g), C.byref(s), C.byref(m)))
+        return {"grid": g.value, "slots": s.value, "smem_bytes": m.value}
+
+    def free(self):
+        if self.handle:
+            _check(_lib.s4_chain_free(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            if self.handle and _lib is not None and self.ctx.handle:
+                _lib.s4_chain_free(self.handle)
+        except Exception:
+            pass
 
 
 class Weight:
@@ -280,6 +312,26 @@ class Context:
         arr = self._ptr_array(flag_ptrs)
         _check(_lib.s4_peer_barrier(self.handle, arr, len(flag_ptrs), int(rank), int(epoch) & 0xFFFFFFFF,
                                     _stream_handle(stream)))
+
+    # -- chained decode GEMV ------------------------------------------------------------------------
+    def chain(self, ops):
+        """Bind a list of decode matmuls into one persistent launch (``s4_chain_create``).
+
+        ``ops``: sequence of ``(x, W, y)`` or ``(x, W, y, dep)`` with CUDA fp16 tensors ``x [M, K]``
+        and ``y [M, N]`` (1 <= M <= 16) and ``dep`` the index of an earlier op whose output ``x``
+        is (or -1). The tensors are held by the returned :class:`Chain` so they stay alive."""
+        n = len(ops)
+        ws = (_P * n)(*[_P(o[1].handle) for o in ops])
+        xs = (_P * n)(*[_P(o[0].data_ptr()) for o in ops])
+        ys = (_P * n)(*[_P(o[2].data_ptr()) for o in ops])
+        ms = (C.c_int * n)(*[int(o[0].shape[0]) for o in ops])
+        deps = (C.c_int * n)(*[int(o[3]) if len(o) > 3 else -1 for o in ops])
+        for o in ops:
+            if o[0].shape[0] != o[2].shape[0] or o[0].shape[1] != o[1].K or o[2].shape[1] != o[1].N:
+                raise S4Error(1, "chain op shapes must be x [M, K], y [M, N] of its weight")
+        h = _P()
+        _check(_lib.s4_chain_create(self.handle, n, ws, xs, ys, ms, deps, C.byref(h)))
+        return Chain(self, h.value, list(ops))
 
     # -- dispatcher ------------------------------------------------------------------------------
     def plan(self, M: int, N: int = 0, K: int = 0):

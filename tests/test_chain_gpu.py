@@ -1,0 +1,135 @@
+"""Chained decode GEMV (one persistent launch for a list of M <= 16 matmuls) against the CPU oracle:
+independent ops over the decode shapes, dependent chains (an op reading the previous op's output),
+ragged shapes (N not a multiple of 128, an op with fewer 128 x 64 chunks than SMs, K not a multiple
+of 64), repeated runs (counters reset, results identical), CUDA-graph replay and argument errors.
+Tolerance: the north star's max relative error 2e-3 and per-row cosine 0.99999."""
+import numpy as np
+import pytest
+
+from oracle import s4ref
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _weights(ctx, rng, K, N):
+    packed, scales = s4ref.config_weights(rng, K, N)
+    return ctx.upload(packed, scales, N, K), packed, scales
+
+
+def _x(rng, M, K):
+    return torch.from_numpy(s4ref.config_x(rng, M, K)).cuda()
+
+
+DECODE = [(2048, 8224), (2048, 3072), (2048, 12288), (6144, 2048)]
+
+
+def test_independent_decode_ops_match_oracle(ctx):
+    rng = np.random.default_rng(1)
+    ops, refs = [], []
+    for K, N in DECODE:
+        W, packed, scales = _weights(ctx, rng, K, N)
+        deq = s4ref.dequant(packed, scales)
+        for M in (1, 3, 8, 16):
+            x = _x(rng, M, K)
+            y = torch.empty((M, N), dtype=torch.float16, device="cuda")
+            ops.append((x, W, y))
+            refs.append(s4ref.matmul(x.cpu().numpy(), packed, scales, deq)[1])
+    chain = ctx.chain(ops)
+    chain.run()
+    torch.cuda.synchronize()
+    assert ctx.check_errors() == 0
+    for (x, W, y), ref in zip(ops, refs):
+        ok, mr, mc = s4ref.check(y.cpu().numpy(), ref)
+        assert ok, (x.shape[0], W.K, W.N, mr, mc)
+    first = [o[2].clone() for o in ops]
+    for _ in range(3):  # counters and tickets reset between runs; results bit-identical
+        chain.run()
+    torch.cuda.synchronize()
+    assert ctx.check_errors() == 0
+    for (x, W, y), y0 in zip(ops, first):
+        assert torch.equal(y, y0)
+
+
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_dependent_chain_matches_sequential_oracle(ctx, M):
+    """x -> W0 (2048 -> 2048) -> W1 (2048 -> 6144) -> W2 (6144 -> 2048), each op reading the last
+    op's fp16 output inside the same launch."""
+    rng = np.random.default_rng(10 + M)
+    dims = [(2048, 2048), (2048, 6144), (6144, 2048)]
+    ws = [_weights(ctx, rng, K, N) for K, N in dims]
+    x0 = _x(rng, M, 2048)
+    ys = [torch.empty((M, N), dtype=torch.float16, device="cuda") for _, N in dims]
+    ops = [(x0, ws[0][0], ys[0], -1), (ys[0], ws[1][0], ys[1], 0), (ys[1], ws[2][0], ys[2], 1)]
+    chain = ctx.chain(ops)
+    for _ in range(2):
+        ys[0].zero_(), ys[1].zero_(), ys[2].zero_()
+        chain.run()
+        torch.cuda.synchronize()
+        assert ctx.check_errors() == 0
+        h = x0.cpu().numpy()
+        for i, (W, packed, scales) in enumerate(ws):
+            ref16, ref32 = s4ref.matmul(h, packed, scales)
+            # each stage compared with the oracle on the GPU's own fp16 input of that stage
+            got_in = h if i == 0 else ys[i - 1].cpu().numpy()
+            _, ref_i = s4ref.matmul(got_in, packed, scales)
+            ok, mr, mc = s4ref.check(ys[i].cpu().numpy(), ref_i)
+            assert ok, (i, mr, mc)
+            h = ref16
+        ok, mr, mc = s4ref.check(ys[2].cpu().numpy(), ref32)
+        assert ok, ("end to end", mr, mc)
+
+
+def test_ragged_shapes(ctx):
+    rng = np.random.default_rng(7)
+    shapes = [(96, 100, 2), (64, 128, 1), (32, 8, 3), (2048, 8224, 16), (160, 1000, 9), (6144, 130, 4)]
+    ops, refs = [], []
+    for K, N, M in shapes:
+        W, packed, scales = _weights(ctx, rng, K, N)
+        x = _x(rng, M, K)
+        y = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        ops.append((x, W, y))
+        refs.append(s4ref.matmul(x.cpu().numpy(), packed, scales)[1])
+    ctx.chain(ops).run()
+    torch.cuda.synchronize()
+    assert ctx.check_errors() == 0
+    for (x, W, y), ref in zip(ops, refs):
+        ok, mr, mc = s4ref.check(y.cpu().numpy(), ref)
+        assert ok, (W.K, W.N, x.shape[0], mr, mc)
+
+
+def test_chain_graph_replay(ctx):
+    rng = np.random.default_rng(3)
+    W, packed, scales = _weights(ctx, rng, 2048, 3072)
+    x = _x(rng, 4, 2048)
+    y1 = torch.empty((4, 3072), dtype=torch.float16, device="cuda")
+    W2, p2, s2 = _weights(ctx, rng, 3072, 2048)
+    y2 = torch.empty((4, 2048), dtype=torch.float16, device="cuda")
+    chain = ctx.chain([(x, W, y1), (y1, W2, y2, 0)])
+    chain.run()
+    torch.cuda.synchronize()
+    eager = y2.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain.run()
+    y2.zero_()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert ctx.check_errors() == 0
+    assert torch.equal(y2, eager)
+
+
+def test_chain_argument_errors(ctx, pkg):
+    rng = np.random.default_rng(4)
+    W, _, _ = _weights(ctx, rng, 64, 128)
+    x17 = _x(rng, 17, 64)
+    y17 = torch.empty((17, 128), dtype=torch.float16, device="cuda")
+    with pytest.raises(pkg.S4Error):
+        ctx.chain([(x17, W, y17)])
+    x = _x(rng, 2, 64)
+    y = torch.empty((2, 128), dtype=torch.float16, device="cuda")
+    with pytest.raises(pkg.S4Error):
+        ctx.chain([(x, W, y, 0)])  # an op cannot depend on itself
+    with pytest.raises(pkg.S4Error):
+        ctx.chain([(x, W, y), (x, W, y, 5)])  # nor on a later op
