@@ -70,8 +70,8 @@ def peaks():
 
 
 def profile_traffic():
-    """DRAM bytes per launch of the GEMV kernel from the committed ncu summary (or None)."""
-    p = os.path.join(ROOT, "profiles", "gemv_decode_sweep.md")
+    """DRAM bytes per launch of the chained decode kernel from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "chain_decode_sweep.md")
     try:
         for line in open(p):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -230,37 +230,61 @@ def run_ours(args, rank, world, local_rank):
     for name, K, N in SHAPES:
         packed, scales = s4ref.config_weights(rng, K, N)
         Ws[name] = [ctx.upload(packed, scales, N, K) for _ in range(COPIES)]
+    # all inputs of a sweep in one device buffer and all outputs in another (one copy each way for
+    # the host-buffer run); every slice starts on a 16-byte boundary (K, N multiples of 8)
+    keys = [(M, name, K, N) for M in MS for name, K, N in SHAPES]
+    xbuf = torch.empty(sum(M * K for M, _, K, _ in keys), dtype=torch.float16, device=dev)
+    ybuf = torch.empty(sum(M * N for M, _, _, N in keys), dtype=torch.float16, device=dev)
     xs, ys = {}, {}
-    for M in MS:
-        for name, K, N in SHAPES:
-            xs[(M, name)] = torch.from_numpy(s4ref.config_x(rng, M, K)).to(dev)
-            ys[(M, name)] = torch.empty((M, N), dtype=torch.float16, device=dev)
+    xo = yo = 0
+    for M, name, K, N in keys:
+        xs[(M, name)] = xbuf[xo:xo + M * K].view(M, K)
+        xs[(M, name)].copy_(torch.from_numpy(s4ref.config_x(rng, M, K)))
+        ys[(M, name)] = ybuf[yo:yo + M * N].view(M, N)
+        xo += M * K
+        yo += M * N
     counter = [0]
 
+    def weight_for(name, rot, mi):
+        return Ws[name][(rot * len(MS) + mi) % COPIES]
+
+    # The engine submits a decode step's recorded matmul steps at once (engine.js:236-282); the
+    # chained GEMV runs the 16 matmuls of one sweep step (on the step's weight copies) as ONE
+    # persistent launch. One chain per weight rotation.
+    chains = []
+    for rot in range(COPIES):
+        ops = [(xs[(M, name)], weight_for(name, rot, mi), ys[(M, name)])
+               for mi, M in enumerate(MS) for name, K, N in SHAPES]
+        chains.append(ctx.chain(ops))
+
     def sweep(rot: int, st):
-        # one step: the 16 matmuls, each on the next copy of its weight
+        # the same 16 matmuls as one launch each (the per-call path, s4_matmul)
         for mi, M in enumerate(MS):
             for name, K, N in SHAPES:
-                W = Ws[name][(rot * len(MS) + mi) % COPIES]
-                ctx.matmul(xs[(M, name)], W, M, ys[(M, name)], st)
+                ctx.matmul(xs[(M, name)], weight_for(name, rot, mi), M, ys[(M, name)], st)
 
-    # The engine replays a cached step list (engine.js:313-343); here each step is a CUDA graph
-    # (one per weight rotation) so the host does not pace the GPU.
-    graphs = []
+    # Each step is replayed from a CUDA graph (one per weight rotation) so the host does not pace
+    # the GPU: the chained launch for the headline, the 16 per-call launches for comparison.
+    graphs, call_graphs = [], []
     cap_stream = torch.cuda.Stream(dev)
     cap_stream.wait_stream(stream)
     with torch.cuda.stream(cap_stream):
         for rot in range(COPIES):
-            sweep(rot, cap_stream)          # eager warm-up of this rotation
+            chains[rot].run(cap_stream)      # eager warm-up
+            sweep(rot, cap_stream)
         cap_stream.synchronize()
         launches_per_step = None
         for rot in range(COPIES):
             g = torch.cuda.CUDAGraph()
             n0 = ctx.launch_count
             with torch.cuda.graph(g, stream=cap_stream):
-                sweep(rot, cap_stream)
+                chains[rot].run(cap_stream)
             launches_per_step = ctx.launch_count - n0
             graphs.append(g)
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=cap_stream):
+                sweep(rot, cap_stream)
+            call_graphs.append(g2)
     stream.wait_stream(cap_stream)
     torch.cuda.synchronize(dev)
 
@@ -299,19 +323,25 @@ def run_ours(args, rank, world, local_rank):
     total_bytes = sweep_bytes() * args.steps * world
     value = total_bytes / (ms / 1e3) / 1e9
 
+    # the same sweep as 16 separate launches (outside the timed region above)
+    for r in range(args.warmup):
+        call_graphs[r % COPIES].replay()
+    barrier()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    for r in range(args.steps):
+        call_graphs[r % COPIES].replay()
+    c1.record(stream)
+    barrier()
+    per_launch_value = total_bytes / (max_over_ranks(c0.elapsed_time(c1)) / 1e3) / 1e9
+
     # ---- e2e: the same sweep through the host-buffer C-ABI entry point ------------------------------
-    hx, hy = {}, {}
-    for M in MS:
-        for name, K, N in SHAPES:
-            hx[(M, name)] = xs[(M, name)].cpu().pin_memory()
-            hy[(M, name)] = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    hx = xbuf.cpu().pin_memory()
+    hy = torch.empty(ybuf.shape, dtype=torch.float16).pin_memory()
 
     def e2e_step():
-        # every call through the public host-buffer entry point, no graph
-        for mi, M in enumerate(MS):
-            for name, K, N in SHAPES:
-                W = Ws[name][(counter[0] * len(MS) + mi) % COPIES]
-                ctx.matmul_host_async(hx[(M, name)], W, hy[(M, name)], M, stream)
+        # inputs from pinned host memory, one chained launch, outputs back to pinned host memory
+        chains[counter[0] % COPIES].run_host(hx, xbuf, hy, ybuf, stream)
         counter[0] += 1
 
     for _ in range(args.warmup):
@@ -325,22 +355,25 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     ms_e2e = max_over_ranks(e2.elapsed_time(e3))
     e2e_value = total_bytes / (ms_e2e / 1e3) / 1e9
-    h2d = sum(2 * M * K for M in MS for _, K, _ in SHAPES)
-    d2h = sum(2 * M * N for M in MS for _, _, N in SHAPES)
+    h2d = hx.numel() * 2
+    d2h = hy.numel() * 2
 
-    # ---- parity spot check of the timed configuration (outside the timed region) ---------------------
+    # ---- parity of the timed configuration (outside the timed region): a chained run whose ops all
+    # use copy 0 of their weight, every output against the oracle --------------------------------------
     rng2 = np.random.default_rng(0)
-    packed, scales = s4ref.config_weights(rng2, SHAPES[0][1], SHAPES[0][2])
+    wref = {name: s4ref.config_weights(rng2, K, N) for name, K, N in SHAPES}
+    pchain = ctx.chain([(xs[(M, name)], Ws[name][0], ys[(M, name)]) for M in MS for name, _, _ in SHAPES])
+    pchain.run(stream)
+    torch.cuda.synchronize(dev)
     ok_all = True
     worst = 0.0
     for M in MS:
-        y = ys[(M, SHAPES[0][0])]
-        ctx.matmul(xs[(M, SHAPES[0][0])], Ws[SHAPES[0][0]][0], M, y, stream)
-        torch.cuda.synchronize(dev)
-        _, ref = s4ref.matmul(xs[(M, SHAPES[0][0])].cpu().numpy(), packed, scales)
-        ok, mr, _ = s4ref.check(y.cpu().numpy(), ref)
-        ok_all &= ok
-        worst = max(worst, mr)
+        for name, K, N in SHAPES:
+            _, ref = s4ref.matmul(xs[(M, name)].cpu().numpy(), *wref[name])
+            ok, mr, _ = s4ref.check(ys[(M, name)].cpu().numpy(), ref)
+            ok_all &= ok
+            worst = max(worst, mr)
+    pchain.free()
 
     # ---- per-(shape, M) breakdown on this rank (device time, 8 rotating copies) -------------------------
     per = {}
@@ -418,25 +451,25 @@ def run_ours(args, rank, world, local_rank):
                          f"(fake-quant route, export_engine.py:88-103)"}
 
     if rank == 0:
-        per_launch_bytes = sweep_bytes() / len(MS) / len(SHAPES)
-        gemv_launches_per_step = len(MS) * len(SHAPES)
-        per_rank_ms = ms / args.steps
-        avg_launch_us = per_rank_ms * 1e3 / gemv_launches_per_step
+        per_launch_bytes = sweep_bytes()  # one chained launch moves the whole sweep
+        avg_launch_us = ms / args.steps * 1e3
         achieved = per_launch_bytes / (avg_launch_us * 1e-6) / 1e9
         line = {
             "metric": "int4 GEMM GB/s (decode sweep M=1..8, algorithmic bytes)",
             "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "decode_gemv_sweep_config2", "M": MS,
+            "config": {"workload": "decode_gemv_sweep_config2 (16 matmuls per step, one chained launch)", "M": MS,
                        "shapes_KN": [[K, N] for _, K, N in SHAPES], "weight_copies": COPIES,
                        "l2": "inputs larger than L2: 8 rotating weight copies (272 MB) per step sequence",
                        "parallelism": f"dp{world} (weights replicated, no collective)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": profile_traffic(), "peak_kind": peak_kind,
-                         "kernel": "gemv_streamk_kernel", "launch_us_avg": avg_launch_us},
+                         "kernel": "chain_kernel", "launch_us_avg": avg_launch_us},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "s4_matmul_host_async (pinned host x -> device -> matmul -> pinned host y)"},
+                    "api": "s4_chain_run_host (pinned host x -> device, one chained launch, device -> pinned host y)"},
+            "per_launch_sweep": {"value": per_launch_value, "unit": "GB/s",
+                                 "note": "the same 16 matmuls as 16 s4_matmul launches (decode GEMV kernel)"},
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clocks.summary(),
@@ -445,7 +478,9 @@ def run_ours(args, rank, world, local_rank):
             "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
-    del graphs
+    del graphs, call_graphs
+    for ch in chains:
+        ch.free()
     ctx.close()
     if world > 1:
         dist.barrier()

@@ -124,6 +124,13 @@ S4_API int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, 
 S4_API int s4_chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y,
                            const int* M, const int* dep, s4_chain** out);
 S4_API int s4_chain_run(s4_ctx* ctx, s4_chain* chain, void* stream);
+/* Host-buffer form (the engine's write inputs / submit / read outputs): copies x_bytes from HOST
+ * x_host to DEVICE x_dev, runs the chain, copies y_bytes from DEVICE y_dev to HOST y_host, all on
+ * `stream`, nothing waited for. The chain's bound inputs must lie in [x_dev, x_dev + x_bytes) and its
+ * outputs of interest in [y_dev, y_dev + y_bytes); host buffers should be pinned and stay valid until
+ * the stream reaches this work. */
+S4_API int s4_chain_run_host(s4_ctx* ctx, s4_chain* chain, const void* x_host, void* x_dev, size_t x_bytes,
+                             void* y_host, const void* y_dev, size_t y_bytes, void* stream);
 S4_API int s4_chain_info(const s4_chain* chain, int* grid, int* slots, int* smem_bytes);
 S4_API int s4_chain_free(s4_chain* chain);
 

@@ -533,6 +533,23 @@ int s4_chain_run(s4_ctx* ctx, s4_chain* chain, void* stream) {
   return S4_OK;
 }
 
+int s4_chain_run_host(s4_ctx* ctx, s4_chain* chain, const void* x_host, void* x_dev, size_t x_bytes, void* y_host,
+                      const void* y_dev, size_t y_bytes, void* stream) {
+  if (!ctx || !chain) return fail(S4_ERR_INVALID, "NULL argument");
+  if ((x_bytes && (!x_host || !x_dev)) || (y_bytes && (!y_host || !y_dev)))
+    return fail(S4_ERR_INVALID, "NULL host or device buffer");
+  DeviceGuard guard(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = x_bytes ? cudaMemcpyAsync(x_dev, x_host, x_bytes, cudaMemcpyHostToDevice, st) : cudaSuccess;
+  if (e != cudaSuccess) return cuda_fail(e, "chain input upload");
+  e = s4::chain_launch(chain, ctx->err, st);
+  if (e != cudaSuccess) return cuda_fail(e, "chain launch");
+  ++ctx->launches;
+  e = y_bytes ? cudaMemcpyAsync(y_host, y_dev, y_bytes, cudaMemcpyDeviceToHost, st) : cudaSuccess;
+  if (e != cudaSuccess) return cuda_fail(e, "chain output download");
+  return S4_OK;
+}
+
 int s4_chain_info(const s4_chain* chain, int* grid, int* slots, int* smem_bytes) {
   if (!chain) return fail(S4_ERR_INVALID, "NULL chain");
   return s4::chain_info(chain, grid, slots, smem_bytes);

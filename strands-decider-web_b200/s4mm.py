@@ -51,6 +51,7 @@ _SIGS = {
     "s4_chain_create": (C.c_int, [_P, C.c_int, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(C.c_int),
                                   C.POINTER(C.c_int), C.POINTER(_P)]),
     "s4_chain_run": (C.c_int, [_P, _P, _P]),
+    "s4_chain_run_host": (C.c_int, [_P, _P, _P, _P, C.c_size_t, _P, _P, C.c_size_t, _P]),
     "s4_chain_info": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "s4_chain_free": (C.c_int, [_P]),
     "s4_buffer_alloc": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
@@ -133,6 +134,16 @@ class Chain:
 
     def run(self, stream=None):
         _check(_lib.s4_chain_run(self.ctx.handle, self.handle, _stream_handle(stream)))
+
+    def run_host(self, x_host, x_dev, y_host, y_dev, stream=None):
+        """Host-buffer run: ``x_host`` (pinned CPU tensor) -> ``x_dev``, the chain, ``y_dev`` ->
+        ``y_host``; asynchronous on ``stream``. ``x_dev``/``y_dev`` cover the bound buffers."""
+        xb = x_host.numel() * x_host.element_size()
+        yb = y_host.numel() * y_host.element_size()
+        if x_dev.numel() * x_dev.element_size() < xb or y_dev.numel() * y_dev.element_size() < yb:
+            raise S4Error(1, "run_host: device buffers smaller than the host buffers")
+        _check(_lib.s4_chain_run_host(self.ctx.handle, self.handle, x_host.data_ptr(), x_dev.data_ptr(), xb,
+                                      y_host.data_ptr(), y_dev.data_ptr(), yb, _stream_handle(stream)))
 
     def info(self):
         g, s, m = C.c_int(), C.c_int(), C.c_int()
