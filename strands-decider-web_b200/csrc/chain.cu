@@ -11,9 +11,10 @@
 //    slots, four consecutive chunks per slot with two 1-D bulk copies (16 KB of nibbles, 2 KB of
 //    scales; TMA engine, no multicast), op after op without a pause. Copy size matters: the bytes
 //    an SM keeps in flight grow with it (4.6 KB copies streamed at under half the rate);
-//  * stager (warp 9): per op, waits until the op it depends on is complete (if any), then copies
-//    the op's activation window into one of two shared-memory buffers with cp.async (all of a
-//    lane's 16-byte pieces in flight at once), one op ahead of the consumers;
+//  * stager (warp 9, one lane): per op, waits until the op it depends on is complete (if any), then
+//    fetches the op's activation window into one of two shared-memory buffers with at most two bulk
+//    copies per activation row, one op ahead of the consumers (16-byte pieces from every CTA at
+//    once made the window of an 8-row op take ~4 us);
 //  * consumers (warps 0-7, one 16-row sub-tile each): only the tile math of gemv_tile.cuh, four
 //    chunks per batch. At the end of an n-block segment they leave their fp32 sums in shared memory
 //    and move on: they never touch global memory, so they never wait for it;
@@ -54,9 +55,12 @@ constexpr int kChainSlotBytes = kChainGroup * (kChunkWBytes + kChunkSBytes);
 constexpr int kChainSlotScales = kChainGroup * kChunkWBytes;  // scales follow the nibbles in a slot
 constexpr int kChainMaxSlots = 16;
 constexpr int kChainMinSlots = 3;
+constexpr int kChainPreferSlots = 7;   // 126 KB of weights in flight per SM before more windows
+constexpr int kChainMaxWindows = 8;
 constexpr int kChainCachedOps = 64;  // op descriptors kept in shared memory
 constexpr int kChainSmemBudget = 216 * 1024;  // dynamic; the static part holds the op cache
 constexpr int kChainSegBytes = kChainConsumers * 2 * 32 * 16;  // one segment's fp32 sums (MG <= 2)
+constexpr int kChainEv = 2;  // part-0 buffers (the reducer may lag the consumers by this many)
 
 struct ChainOp {
   const uint8_t* wq;
@@ -75,10 +79,11 @@ struct ChainParams {
   const ChainOp* ops;
   int nops;
   int slots;           // weight ring slots
-  int x_off, x_bytes;  // two activation windows of x_bytes each
-  int ev_off;          // two part-0 buffers, then two publish buffers, kChainSegBytes each
-  int bar_off;         // mbarriers: full[slots], empty[slots], xfull[2], xempty[2], evfull[2],
-                       // evempty[2], pubfull[2], pubempty[2]
+  int x_off, x_bytes;  // nx activation windows of x_bytes each
+  int nx;
+  int ev_off;          // kChainEv part-0 buffers, then two publish buffers, kChainSegBytes each
+  int bar_off;         // mbarriers: full[slots], empty[slots], xfull[nx], xempty[nx], evfull[kChainEv],
+                       // evempty[kChainEv], pubfull[2], pubempty[2]
   uint32_t* op_done;   // [nops] finished sub-tiles
   uint32_t* exit_count;
   uint32_t* err;
@@ -176,8 +181,8 @@ __device__ __forceinline__ bool chain_flush(const ChainOp& op, const ChainRange&
   float4* dst;
   uint64_t* full;
   if (kind == kSegPart0) {
-    const int e = evk & 1;
-    if (evk >= 2 && !mbar_wait(sm.evempty + e, (uint32_t)((evk >> 1) - 1) & 1u)) return false;
+    const int e = evk % kChainEv;
+    if (evk >= kChainEv && !mbar_wait(sm.evempty + e, (uint32_t)((evk / kChainEv) - 1) & 1u)) return false;
     dst = sm.ev + (size_t)e * (kChainSegBytes / 16);
     full = sm.evfull + e;
     ++evk;
@@ -207,8 +212,8 @@ __device__ bool chain_consume(const ChainOp& op, const ChainRange& r, const Chai
   const int KT = op.ktiles;
   const int sub = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int xb = xk & 1;
-  if (!mbar_wait(sm.xfull + xb, (uint32_t)(xk >> 1) & 1u) || *(volatile int*)sm.fail) return false;
+  const int xb = xk % p.nx;
+  if (!mbar_wait(sm.xfull + xb, (uint32_t)(xk / p.nx) & 1u) || *(volatile int*)sm.fail) return false;
   const uint8_t* xs = sm.xbuf + xb * p.x_bytes;
   bool xok[MG];
 #pragma unroll
@@ -337,8 +342,8 @@ template <int MG>
 __device__ bool chain_reduce(const ChainOp& op, const ChainRange& r, const ChainParams& p, const ChainSmem& sm, int i,
                              int nb, int nparts, int evk) {
   const int lane = threadIdx.x & 31;
-  const int e = evk & 1;
-  if (!mbar_wait(sm.evfull + e, (uint32_t)(evk >> 1) & 1u)) return false;
+  const int e = evk % kChainEv;
+  if (!mbar_wait(sm.evfull + e, (uint32_t)(evk / kChainEv) & 1u)) return false;
   bool ok = true;
   if (lane < 8) ok = wait_count(op.tickets + nb * 8 + lane, (uint32_t)(nparts - 1));
   ok = __all_sync(0xffffffffu, ok);
@@ -391,14 +396,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
   sm.ring = smem;
   sm.xbuf = smem + p.x_off;
   sm.ev = reinterpret_cast<float4*>(smem + p.ev_off);
-  sm.pub = sm.ev + 2 * (kChainSegBytes / 16);
+  sm.pub = sm.ev + kChainEv * (kChainSegBytes / 16);
   sm.full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   sm.empty = sm.full + p.slots;
   sm.xfull = sm.empty + p.slots;
-  sm.xempty = sm.xfull + 2;
-  sm.evfull = sm.xempty + 2;
-  sm.evempty = sm.evfull + 2;
-  sm.pubfull = sm.evempty + 2;
+  sm.xempty = sm.xfull + p.nx;
+  sm.evfull = sm.xempty + p.nx;
+  sm.evempty = sm.evfull + kChainEv;
+  sm.pubfull = sm.evempty + kChainEv;
   sm.pubempty = sm.pubfull + 2;
   sm.ops = s_ops;
   sm.fail = &s_fail;
@@ -416,11 +421,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       mbar_init(sm.full + s, 1);
       mbar_init(sm.empty + s, kChainConsumers);
     }
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < p.nx; ++k) {
       mbar_init(sm.xfull + k, 1);
       mbar_init(sm.xempty + k, kChainConsumers);
+    }
+    for (int k = 0; k < kChainEv; ++k) {
       mbar_init(sm.evfull + k, kChainConsumers);
       mbar_init(sm.evempty + k, 1);
+    }
+    for (int k = 0; k < 2; ++k) {
       mbar_init(sm.pubfull + k, kChainConsumers);
       mbar_init(sm.pubempty + k, 1);
     }
@@ -463,41 +472,48 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     }
   } else if (warp == kChainStagerWarp) {
     // ---------------- stager: dependency wait + activation window, one op ahead ----------------
-    int xk = 0;
-    for (int i = 0; i < p.nops && ok; ++i) {
-      const ChainOp op = chain_op_at(p, sm, i);
-      const ChainRange r = chain_range(op, b, G);
-      if (r.c0 >= r.c1) continue;
-      const int xb = xk & 1;
-      ok = !(xk >= 2 && !mbar_wait(sm.xempty + xb, (uint32_t)((xk >> 1) - 1) & 1u));
-      if (ok && op.dep >= 0) {
-        const ChainOp d = chain_op_at(p, sm, op.dep);
-        if (lane == 0) ok = wait_count(p.op_done + op.dep, (uint32_t)d.nblk * 8u);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        __syncwarp();  // lane 0's acquire, then the warp's loads (memory-ordering warp barrier)
+    if (lane == 0) {
+      int xk = 0;
+      const uint64_t pol = policy_evict_last();  // every CTA reads the same activations
+      for (int i = 0; i < p.nops && ok; ++i) {
+        const ChainOp op = chain_op_at(p, sm, i);
+        const ChainRange r = chain_range(op, b, G);
+        if (r.c0 >= r.c1) continue;
+        const int xb = xk % p.nx;
+        ok = !(xk >= p.nx && !mbar_wait(sm.xempty + xb, (uint32_t)((xk / p.nx) - 1) & 1u));
+        if (ok && op.dep >= 0) {
+          const ChainOp d = chain_op_at(p, sm, op.dep);
+          ok = wait_count(p.op_done + op.dep, (uint32_t)d.nblk * 8u);
+          // the input was written by other CTAs through the generic proxy; the bulk copies below
+          // read it through the async proxy
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+        if (!ok || *(volatile int*)&s_fail) {
+          ok = false;
+          break;
+        }
+        // window k-tiles kt_start, kt_start + 1, ... (mod KT): one or two contiguous pieces per row
+        const int KT = op.ktiles;
+        const int kt_start = r.c0 % KT;
+        const int n_win = min(r.c1 - r.c0, KT);
+        const int n1 = min(n_win, KT - kt_start);
+        const uint32_t b1 = (uint32_t)(min((kt_start + n1) * 64, op.K) - kt_start * 64) * 2u;
+        const uint32_t b2 = n_win > n1 ? (uint32_t)min((n_win - n1) * 64, op.K) * 2u : 0u;
+        uint8_t* xs = sm.xbuf + xb * p.x_bytes;
+        mbar_arrive_expect_tx(sm.xfull + xb, (uint32_t)op.M * (b1 + b2));
+        for (int row = 0; row < op.M; ++row) {
+          const __half* xr = op.x + (int64_t)row * op.K;
+          bulk_g2s(xs + row * op.xrow, xr + kt_start * 64, b1, sm.xfull + xb, pol);
+          if (b2) bulk_g2s(xs + row * op.xrow + n1 * 128, xr, b2, sm.xfull + xb, pol);
+        }
+        ++xk;
       }
-      if (!ok || *(volatile int*)&s_fail) {
-        ok = false;
-        break;
+      if (!ok) {
+        // window copies still in flight land before the CTA exits (bounded)
+        const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
+        for (int q = (xk > p.nx ? xk - p.nx : 0); q < xk; ++q)
+          if (!mbar_wait_until(sm.xfull + (q % p.nx), (uint32_t)(q / p.nx) & 1u, deadline)) break;
       }
-      const int KT = op.ktiles;
-      const int kt_start = r.c0 % KT;
-      const int n_win = min(r.c1 - r.c0, KT);
-      const int per_row = n_win * 8;
-      uint8_t* xs = sm.xbuf + xb * p.x_bytes;
-      for (int q = lane; q < op.M * per_row; q += 32) {
-        const int row = q / per_row, j = q - row * per_row;
-        const int w = j >> 3, e = j & 7;
-        int kt = kt_start + w;
-        if (kt >= KT) kt -= KT;
-        const int k = kt * 64 + e * 8;
-        // pieces past K (second half of a last half k-tile) are never read by the tile math
-        if (k < op.K) cp_async_cg16(xs + row * op.xrow + w * 128 + e * 16, op.x + (int64_t)row * op.K + k);
-      }
-      cp_async_wait_all();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sm.xfull + xb);
-      ++xk;
     }
   } else if (warp == kChainPublisherWarp) {
     // ---------------- publisher ----------------
@@ -561,7 +577,7 @@ struct s4_chain {
   int nops;
   int grid;
   int slots;
-  int x_off, x_bytes, ev_off, bar_off, smem;
+  int x_off, x_bytes, nx, ev_off, bar_off, smem;
   ChainOp* d_ops;
   uint8_t* d_scratch;  // partials, tickets, op_done, exit_count
   uint32_t* op_done;
@@ -613,21 +629,31 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     scratch = (scratch + 255) & ~(size_t)255;
   }
   xmax = (xmax + 127) & ~127;
-  const int fixed = 2 * xmax + 4 * kChainSegBytes + 12 * 8 + 256;
-  int slots = (kChainSmemBudget - fixed - 2 * kChainMaxSlots * 8) / kChainSlotBytes;
+  // shared memory: the weight ring first (at least kChainPreferSlots slots when possible), then as
+  // many activation windows (2..kChainMaxWindows) as fit: more windows = more ops of lookahead for
+  // the stager, which hides the activation fetch of small ops
+  const int fixed = (kChainEv + 2) * kChainSegBytes + 2 * (2 * kChainMaxSlots + 2 * kChainMaxWindows + 12) * 8 + 256;
+  const int avail = kChainSmemBudget - fixed;
+  if (avail < 2 * xmax + kChainMinSlots * kChainSlotBytes)
+    return *why = "activation window too large for shared memory (M * K range)", S4_ERR_UNSUPPORTED;
+  int slots = (avail - 2 * xmax) / kChainSlotBytes;
+  if (slots > kChainPreferSlots) slots = kChainPreferSlots;
+  int nx = (avail - slots * kChainSlotBytes) / xmax;
+  if (nx > kChainMaxWindows) nx = kChainMaxWindows;
+  slots = (avail - nx * xmax) / kChainSlotBytes;
   if (slots > kChainMaxSlots) slots = kChainMaxSlots;
-  if (slots < kChainMinSlots) return *why = "activation window too large for shared memory (M * K range)", S4_ERR_UNSUPPORTED;
 
   s4_chain* c = new s4_chain();
   c->ctx = ctx;
   c->nops = nops;
   c->grid = G;
   c->slots = slots;
+  c->nx = nx;
   c->x_off = slots * kChainSlotBytes;
   c->x_bytes = xmax;
-  c->ev_off = c->x_off + 2 * xmax;
-  c->bar_off = c->ev_off + 4 * kChainSegBytes;
-  c->smem = c->bar_off + (2 * slots + 12) * 8;
+  c->ev_off = c->x_off + nx * xmax;
+  c->bar_off = c->ev_off + (kChainEv + 2) * kChainSegBytes;
+  c->smem = c->bar_off + (2 * slots + 2 * nx + 2 * kChainEv + 4) * 8;
   const size_t ctr_off = scratch;
   scratch += (size_t)(nops + 1) * 4;
   cudaError_t e = cudaMalloc(&c->d_scratch, scratch);
@@ -673,6 +699,7 @@ cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream) {
   p.slots = c->slots;
   p.x_off = c->x_off;
   p.x_bytes = c->x_bytes;
+  p.nx = c->nx;
   p.ev_off = c->ev_off;
   p.bar_off = c->bar_off;
   p.op_done = c->op_done;
