@@ -246,18 +246,12 @@ __device__ bool chain_consume(const ChainOp& op, const ChainRange& r, const Chai
       slot = 0;
       phase ^= 1u;
     }
-    if (kt + n <= KT && wpos + n <= KT) {
-      // fast path: the group lies in one n-block and one stretch of the window; the tiles are
-      // independent, so the compiler can overlap their latencies
+    if (n == kChainGroup && kt + n <= KT && wpos + n <= KT && (kt + n) * 64 <= op.K) {
+      // fast path: four chunks in one n-block and one stretch of the window, all of K in range;
+      // the tiles are independent, so the compiler can overlap their latencies
       const uint8_t* xg = xl + wpos * 128;
-      if (n == kChainGroup && (kt + kChainGroup) * 64 <= op.K) {
 #pragma unroll
-        for (int j = 0; j < kChainGroup; ++j) gemv_tile<MG>(wv[j], sc[j], xg + j * 128, xgroup, true, xok, acc);
-      } else {
-#pragma unroll
-        for (int j = 0; j < kChainGroup; ++j)
-          if (j < n) gemv_tile<MG>(wv[j], sc[j], xg + j * 128, xgroup, (kt + j) * 64 + 32 < op.K, xok, acc);
-      }
+      for (int j = 0; j < kChainGroup; ++j) gemv_tile<MG>(wv[j], sc[j], xg + j * 128, xgroup, true, xok, acc);
       kt += n;
       wpos += n;
       if (wpos == KT) wpos = 0;
@@ -388,6 +382,9 @@ __device__ bool chain_reduce(const ChainOp& op, const ChainRange& r, const Chain
   return true;
 }
 
+// MG: 8-token groups of every op of the launch (1 if all ops have M <= 8, else 2). One MG per
+// kernel keeps the code small enough for the instruction cache (five warp roles share it).
+template <int MG>
 __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_fail;
@@ -522,7 +519,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       const ChainOp op = chain_op_at(p, sm, i);
       const ChainRange r = chain_range(op, b, G);
       if (r.c0 >= r.c1) continue;
-      ok = op.M > 8 ? chain_publish_op<2>(op, r, p, sm, i, pubk) : chain_publish_op<1>(op, r, p, sm, i, pubk);
+      ok = chain_publish_op<MG>(op, r, p, sm, i, pubk);
     }
   } else if (warp == kChainReducerWarp) {
     // ---------------- reducer ----------------
@@ -534,7 +531,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       const int nb = (r.c1 - 1) / op.ktiles;  // only the last segment of a range can be a part 0
       int part, nparts;
       if (chain_seg_kind(op, r, nb, &part, &nparts) != kSegPart0) continue;
-      ok = op.M > 8 ? chain_reduce<2>(op, r, p, sm, i, nb, nparts, evk) : chain_reduce<1>(op, r, p, sm, i, nb, nparts, evk);
+      ok = chain_reduce<MG>(op, r, p, sm, i, nb, nparts, evk);
       ++evk;
     }
   } else {
@@ -545,8 +542,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       const ChainOp op = chain_op_at(p, sm, i);
       const ChainRange r = chain_range(op, b, G);
       if (r.c0 >= r.c1) continue;
-      ok = op.M > 8 ? chain_consume<2>(op, r, p, sm, slot, phase, xk, evk, pubk)
-                    : chain_consume<1>(op, r, p, sm, slot, phase, xk, evk, pubk);
+      ok = chain_consume<MG>(op, r, p, sm, slot, phase, xk, evk, pubk);
       ++xk;
     }
   }
@@ -578,6 +574,7 @@ struct s4_chain {
   int grid;
   int slots;
   int x_off, x_bytes, nx, ev_off, bar_off, smem;
+  int mg;  // token groups of the launch: 2 if any op has M > 8
   ChainOp* d_ops;
   uint8_t* d_scratch;  // partials, tickets, op_done, exit_count
   uint32_t* op_done;
@@ -621,7 +618,7 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     o.xrow = n_win * 128 + 64;
     const int xb = o.M * o.xrow;
     if (xb > xmax) xmax = xb;
-    const int MG = o.M > 8 ? 2 : 1;
+    const int MG = 2;  // partial layout for the launch's MG (<= 2); sized for the larger
     part_off[i] = scratch;
     scratch += (size_t)o.nblk * 8 * o.maxparts * MG * 32 * 16;
     tick_off[i] = scratch;
@@ -649,6 +646,9 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
   c->grid = G;
   c->slots = slots;
   c->nx = nx;
+  c->mg = 1;
+  for (int i = 0; i < nops; ++i)
+    if (ops[i].M > 8) c->mg = 2;
   c->x_off = slots * kChainSlotBytes;
   c->x_bytes = xmax;
   c->ev_off = c->x_off + nx * xmax;
@@ -689,7 +689,9 @@ cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kChainSmemBudget);
+    e = cudaFuncSetAttribute(chain_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kChainSmemBudget);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(chain_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kChainSmemBudget);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
@@ -715,7 +717,7 @@ cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, chain_kernel, p);
+  return c->mg == 2 ? cudaLaunchKernelEx(&cfg, chain_kernel<2>, p) : cudaLaunchKernelEx(&cfg, chain_kernel<1>, p);
 }
 
 void chain_destroy(s4_chain* c) {
