@@ -459,7 +459,7 @@ def run_ours(args, rank, world, local_rank):
             "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "decode_gemv_sweep_config2 (16 matmuls per step, one chained launch)", "M": MS,
+            "config": {"workload": "decode_gemv_sweep_config2", "launch": "the 16 matmuls of a step as one chained launch", "M": MS,
                        "shapes_KN": [[K, N] for _, K, N in SHAPES], "weight_copies": COPIES,
                        "l2": "inputs larger than L2: 8 rotating weight copies (272 MB) per step sequence",
                        "parallelism": f"dp{world} (weights replicated, no collective)"},
