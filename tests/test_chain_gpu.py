@@ -133,3 +133,32 @@ def test_chain_argument_errors(ctx, pkg):
         ctx.chain([(x, W, y, 0)])  # an op cannot depend on itself
     with pytest.raises(pkg.S4Error):
         ctx.chain([(x, W, y), (x, W, y, 5)])  # nor on a later op
+
+
+def test_chain_run_host_matches_device_run(ctx):
+    """s4_chain_run_host: inputs copied from pinned host memory, the chained launch, outputs copied
+    back, on one stream; equals the device-buffer run bit for bit."""
+    rng = np.random.default_rng(12)
+    (W1, p1, s1), (W2, p2, s2) = _weights(ctx, rng, 2048, 3072), _weights(ctx, rng, 6144, 2048)
+    xdev = torch.empty(3 * 2048 + 2 * 6144, dtype=torch.float16, device="cuda")
+    ydev = torch.empty(3 * 3072 + 2 * 2048, dtype=torch.float16, device="cuda")
+    x1, x2 = xdev[:3 * 2048].view(3, 2048), xdev[3 * 2048:].view(2, 6144)
+    y1, y2 = ydev[:3 * 3072].view(3, 3072), ydev[3 * 3072:].view(2, 2048)
+    chain = ctx.chain([(x1, W1, y1), (x2, W2, y2)])
+    hx = torch.from_numpy(np.concatenate([s4ref.config_x(rng, 3, 2048).ravel(),
+                                          s4ref.config_x(rng, 2, 6144).ravel()])).pin_memory()
+    hy = torch.empty(ydev.shape, dtype=torch.float16).pin_memory()
+    stream = torch.cuda.current_stream()
+    chain.run_host(hx, xdev, hy, ydev, stream)
+    stream.synchronize()
+    assert ctx.check_errors() == 0
+    got = hy.clone()
+    chain.run()
+    torch.cuda.synchronize()
+    assert torch.equal(got, ydev.cpu())
+    _, ref1 = s4ref.matmul(hx[:3 * 2048].view(3, 2048).numpy(), p1, s1)
+    ok, mr, mc = s4ref.check(got[:3 * 3072].view(3, 3072).numpy(), ref1)
+    assert ok, (mr, mc)
+    _, ref2 = s4ref.matmul(hx[3 * 2048:].view(2, 6144).numpy(), p2, s2)
+    ok, mr, mc = s4ref.check(got[3 * 3072:].view(2, 2048).numpy(), ref2)
+    assert ok, (mr, mc)
