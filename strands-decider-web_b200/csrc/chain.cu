@@ -57,6 +57,7 @@ constexpr int kChainMaxSlots = 16;
 constexpr int kChainMinSlots = 3;
 constexpr int kChainPreferSlots = 7;   // 126 KB of weights in flight per SM before more windows
 constexpr int kChainMaxWindows = 8;
+constexpr int kChainPhaseWindow = 36 * 1024;  // largest whole-K activation window of an op sharing a phase
 constexpr int kChainCachedOps = 64;  // op descriptors kept in shared memory
 constexpr int kChainSmemBudget = 216 * 1024;  // dynamic; the static part holds the op cache
 constexpr int kChainSegBytes = kChainConsumers * 2 * 32 * 16;  // one segment's fp32 sums (MG <= 2)
@@ -67,13 +68,20 @@ struct ChainOp {
   const uint8_t* ws;
   const __half* x;    // [M][K]
   __half* y;          // [M][N]
-  float* partials;    // [nblk][8][maxparts][MG][32] float4 (part 0 unused)
-  uint32_t* tickets;  // [nblk * 8] arrivals of parts 1.. of each split sub-tile
+  float* partials;    // [nblk][8][maxparts][2][32] float4 (part 0 unused), then the sub-tile
+                      // tickets [nblk * 8] (arrivals of parts 1..), see chain_tickets
   int M, N, K, nblk, ktiles;
   int dep;            // op whose output this op reads (-1: none)
   int maxparts;
   int xrow;           // padded activation window row (bytes)
+  int phase_base;     // first chunk of this op in its phase's concatenated chunk sequence
+  int phase_U;        // chunks of the whole phase
 };
+
+__device__ __forceinline__ uint32_t* chain_tickets(const ChainOp& op) {
+  return reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(op.partials) +
+                                     (size_t)op.nblk * 8 * op.maxparts * 2 * 32 * 16);
+}
 
 struct ChainParams {
   const ChainOp* ops;
@@ -89,25 +97,30 @@ struct ChainParams {
   uint32_t* err;
 };
 
-// A CTA's share of one op: chunks [c0, c1) of U = nblk * ktiles, split over min(G, U) CTAs.
+// A CTA's share of one op: op-local chunks [c0, c1). The chunks of a phase (consecutive ops none
+// of which reads another's output) are concatenated and cut into min(G, U) equal contiguous
+// ranges, U = the phase's chunk count, so an n-block is split only where a CTA's range ends.
 struct ChainRange {
-  int U, G, c0, c1;
+  int U, G, base, c0, c1;
 };
 __device__ __forceinline__ int chain_begin(int b, int U, int G) { return (int)(((int64_t)b * U) / G); }
 __device__ __forceinline__ int chain_cta_of(int u, int U, int G) { return (int)((((int64_t)u + 1) * G - 1) / U); }
 __device__ __forceinline__ ChainRange chain_range(const ChainOp& op, int b, int grid) {
   ChainRange r;
-  r.U = op.nblk * op.ktiles;
+  r.U = op.phase_U;
   r.G = min(grid, r.U);
-  r.c0 = b < r.G ? chain_begin(b, r.U, r.G) : 0;
-  r.c1 = b < r.G ? chain_begin(b + 1, r.U, r.G) : 0;
+  r.base = op.phase_base;
+  const int u0 = b < r.G ? chain_begin(b, r.U, r.G) : 0, u1 = b < r.G ? chain_begin(b + 1, r.U, r.G) : 0;
+  const int n = op.nblk * op.ktiles;
+  r.c0 = min(max(u0 - r.base, 0), n);
+  r.c1 = max(min(u1 - r.base, n), r.c0);
   return r;
 }
 // Kind of the segment of n-block nb inside range r.
 enum ChainSeg { kSegDirect = 0, kSegPart0 = 1, kSegPartial = 2 };
 __device__ __forceinline__ int chain_seg_kind(const ChainOp& op, const ChainRange& r, int nb, int* part, int* nparts) {
   const int KT = op.ktiles;
-  const int first = chain_cta_of(nb * KT, r.U, r.G), last = chain_cta_of(nb * KT + KT - 1, r.U, r.G);
+  const int first = chain_cta_of(r.base + nb * KT, r.U, r.G), last = chain_cta_of(r.base + nb * KT + KT - 1, r.U, r.G);
   *nparts = last - first + 1;
   *part = (int)blockIdx.x - first;
   if (first == last) return kSegDirect;
@@ -325,7 +338,7 @@ __device__ bool chain_publish_op(const ChainOp& op, const ChainRange& r, const C
     if (kind == kSegDirect) {
       if (lane == 0) red_relaxed_gpu(p.op_done + i, 8u);
     } else {
-      if (lane < 8) red_relaxed_gpu(op.tickets + nb * 8 + lane, 1u);
+      if (lane < 8) red_relaxed_gpu(chain_tickets(op) + nb * 8 + lane, 1u);
     }
   }
   return true;
@@ -339,7 +352,7 @@ __device__ bool chain_reduce(const ChainOp& op, const ChainRange& r, const Chain
   const int e = evk % kChainEv;
   if (!mbar_wait(sm.evfull + e, (uint32_t)(evk / kChainEv) & 1u)) return false;
   bool ok = true;
-  if (lane < 8) ok = wait_count(op.tickets + nb * 8 + lane, (uint32_t)(nparts - 1));
+  if (lane < 8) ok = wait_count(chain_tickets(op) + nb * 8 + lane, (uint32_t)(nparts - 1));
   ok = __all_sync(0xffffffffu, ok);
   __syncwarp();  // lanes 0-7 acquired the counters; order the whole warp's loads after them
   if (!ok) return false;
@@ -376,7 +389,7 @@ __device__ bool chain_reduce(const ChainOp& op, const ChainRange& r, const Chain
   }
 #pragma unroll
   for (int sub = 0; sub < 8; ++sub) chain_store_y<MG>(op, nb, sub, out[sub]);
-  if (lane < 8) op.tickets[nb * 8 + lane] = 0u;  // every part has arrived: ready for the next run
+  if (lane < 8) chain_tickets(op)[nb * 8 + lane] = 0u;  // every part has arrived: ready for the next run
   fence_acq_rel_gpu();
   if (lane == 0) red_relaxed_gpu(p.op_done + i, 8u);
   return true;
@@ -591,7 +604,7 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
   std::vector<ChainOp> ops(nops);
   size_t scratch = 0;
   int xmax = 0;
-  std::vector<size_t> part_off(nops), tick_off(nops);
+  std::vector<size_t> part_off(nops);
   for (int i = 0; i < nops; ++i) {
     const s4_weight* wi = w[i];
     ChainOp& o = ops[i];
@@ -608,20 +621,47 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     if (o.M < 1 || o.M > 16) return *why = "every op needs 1 <= M <= 16", S4_ERR_INVALID;
     if (o.dep >= i || o.dep < -1) return *why = "dep must name an earlier op or be -1", S4_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(x[i]) & 15) || (o.K * 2) % 16) return *why = "x must be 16-byte aligned", S4_ERR_INVALID;
+  }
+  // phases: runs of consecutive ops none of which reads another op of the run; an op whose whole-K
+  // activation window would exceed kChainPhaseWindow stays alone (its range within a shared phase
+  // could span whole n-blocks, i.e. all of K)
+  std::vector<int> phase_start(nops);
+  {
+    int start = 0;
+    for (int i = 0; i < nops; ++i) {
+      const ChainOp& o = ops[i];
+      const int wfull = o.M * (o.ktiles * 128 + 64);
+      const bool big = wfull > kChainPhaseWindow;
+      const bool prev_big = i > 0 && ops[i - 1].M * (ops[i - 1].ktiles * 128 + 64) > kChainPhaseWindow;
+      if (i == 0 || o.dep >= start || big || prev_big) start = i;
+      phase_start[i] = start;
+    }
+  }
+  for (int i = 0; i < nops;) {
+    int j = i, U = 0;
+    while (j < nops && phase_start[j] == i) {
+      ops[j].phase_base = U;
+      U += ops[j].nblk * ops[j].ktiles;
+      ++j;
+    }
+    for (int q = i; q < j; ++q) ops[q].phase_U = U;
+    i = j;
+  }
+  for (int i = 0; i < nops; ++i) {
+    ChainOp& o = ops[i];
     const int U = o.nblk * o.ktiles;
-    const int Gop = U < G ? U : G;
-    const int per_cta = (U + Gop - 1) / Gop;
-    const int min_cta = U / Gop;  // >= 1
+    const int Gp = o.phase_U < G ? o.phase_U : G;
+    const int per_cta = (o.phase_U + Gp - 1) / Gp;
+    const int min_cta = o.phase_U / Gp;  // >= 1
     o.maxparts = (o.ktiles + min_cta - 1) / min_cta + 1;  // CTAs one n-block can span
-    if (o.maxparts > Gop) o.maxparts = Gop;
-    const int n_win = per_cta < o.ktiles ? per_cta : o.ktiles;
+    if (o.maxparts > Gp) o.maxparts = Gp;
+    int n_win = per_cta < U ? per_cta : U;
+    if (n_win > o.ktiles) n_win = o.ktiles;
     o.xrow = n_win * 128 + 64;
     const int xb = o.M * o.xrow;
     if (xb > xmax) xmax = xb;
-    const int MG = 2;  // partial layout for the launch's MG (<= 2); sized for the larger
-    part_off[i] = scratch;
-    scratch += (size_t)o.nblk * 8 * o.maxparts * MG * 32 * 16;
-    tick_off[i] = scratch;
+    part_off[i] = scratch;  // partials sized for MG = 2, the tickets right after (chain_tickets)
+    scratch += (size_t)o.nblk * 8 * o.maxparts * 2 * 32 * 16;
     scratch += (size_t)o.nblk * 8 * 4;
     scratch = (scratch + 255) & ~(size_t)255;
   }
@@ -664,10 +704,7 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     delete c;
     return *why = "device allocation failed", S4_ERR_NOMEM;
   }
-  for (int i = 0; i < nops; ++i) {
-    ops[i].partials = reinterpret_cast<float*>(c->d_scratch + part_off[i]);
-    ops[i].tickets = reinterpret_cast<uint32_t*>(c->d_scratch + tick_off[i]);
-  }
+  for (int i = 0; i < nops; ++i) ops[i].partials = reinterpret_cast<float*>(c->d_scratch + part_off[i]);
   c->op_done = reinterpret_cast<uint32_t*>(c->d_scratch + ctr_off);
   c->exit_count = c->op_done + nops;
   e = cudaMemcpy(c->d_ops, ops.data(), sizeof(ChainOp) * nops, cudaMemcpyHostToDevice);
