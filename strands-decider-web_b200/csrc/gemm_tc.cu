@@ -9,12 +9,14 @@
 // shared memory with the 128-byte swizzle; B = tn tokens x 16 K of the activations, loaded by TMA
 // with the same swizzle; D = 128 x tn fp32 in TMEM (lane = n, column = token).
 //
-// Work: units (token block tb, n-block nb, k-tile kt) of 64 K, kt fastest; CTA b of G takes units
-// [b*U/G, (b+1)*U/G) (stream-K), so every SM gets the same number of MMAs whatever M, N and K are.
-// A run of units of one (tb, nb) tile is a segment; a segment that covers the whole K range is
-// written as fp16 directly, otherwise its fp32 partial goes to scratch and a fix-up kernel launched
-// right after sums the partials of each split tile in CTA order (the allocation-free entry point
-// instead lets the last CTA to arrive at the tile do it, through an atomic ticket).
+// Work: units (token block tb, n-block nb, k-tile kt) of 64 K, kt fastest; a (tb, nb) tile is KT
+// units. The first floor(T/G)*G of the T tiles are dealt out whole, floor(T/G) per CTA, and the units
+// of the remaining T mod G tiles are cut into G equal stream-K ranges, so every SM gets the same
+// number of MMAs and only those last tiles can be split. A run of units of one tile is a segment; a
+// segment that covers the whole K range is written as fp16 directly, otherwise its fp32 partial goes
+// to scratch and a fix-up kernel launched right after sums the partials of each split tile in CTA
+// order (the allocation-free entry point instead lets the last CTA to arrive at the tile do it,
+// through an atomic ticket).
 //
 // Warp roles (512 threads): warp 0 lane 0 streams raw int4 chunks (1-D bulk copies) into a
 // kTcSlotsW-slot ring; warp 2 lane 0 loads activation tiles by TMA into a kTcStagesX-stage ring; warp 1 owns TMEM
@@ -70,6 +72,9 @@ struct TcParams {
   int ntb;    // token blocks
   int total;  // units = ntb * nblk * ktiles
   int grid;
+  int dpq;       // whole tiles per CTA (data-parallel part): CTA b takes tiles [b*dpq, (b+1)*dpq)
+  int sk_base;   // first unit of the stream-K part (dpq * grid * ktiles)
+  int sk_total;  // units of the stream-K part, split evenly over the grid
 };
 
 // Output stores. Each destination is the local buffer or, for the column-sharded prefill, a peer's
@@ -140,9 +145,30 @@ __device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint3
                : "memory");
 }
 
-__device__ __forceinline__ int tc_begin(int b, const TcParams& p) { return (int)(((int64_t)b * p.total) / p.grid); }
+// Work split: the first dpq * grid tiles go whole to the CTAs (dpq each, no partials); the units of
+// the remaining tiles (fewer than grid tiles) are cut into grid equal stream-K ranges, so only those
+// tiles can be split. tc_begin(b) is where CTA b's stream-K range starts; tc_cta_of(u) is the CTA
+// whose stream-K range holds unit u.
+__device__ __forceinline__ int tc_begin(int b, const TcParams& p) {
+  return p.sk_base + (int)(((int64_t)b * p.sk_total) / p.grid);
+}
 __device__ __forceinline__ int tc_cta_of(int u, const TcParams& p) {
-  return (int)((((int64_t)u + 1) * p.grid - 1) / p.total);
+  return (int)((((int64_t)(u - p.sk_base) + 1) * p.grid - 1) / p.sk_total);
+}
+struct TcWork {
+  int dp0, ndp;  // whole-tile units [dp0, dp0 + ndp)
+  int sk0, sk1;  // stream-K units [sk0, sk1)
+  __device__ __forceinline__ int count() const { return ndp + (sk1 - sk0); }
+  __device__ __forceinline__ int unit(int i) const { return i < ndp ? dp0 + i : sk0 + (i - ndp); }
+  __device__ __forceinline__ int range_end(int i) const { return i < ndp ? dp0 + ndp : sk1; }
+};
+__device__ __forceinline__ TcWork tc_work(int b, const TcParams& p) {
+  TcWork w;
+  w.ndp = p.dpq * p.ktiles;
+  w.dp0 = b * w.ndp;
+  w.sk0 = tc_begin(b, p);
+  w.sk1 = tc_begin(b + 1, p);
+  return w;
 }
 
 // kTicketFixup: split tiles are finished inside this kernel by the last CTA to arrive (atomic
@@ -169,8 +195,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   int* s_flag = reinterpret_cast<int*>(smem + kTcOffMisc + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c0 = tc_begin(blockIdx.x, p), c1 = tc_begin(blockIdx.x + 1, p);
-  const int n = c1 - c0;
+  const TcWork wk = tc_work(blockIdx.x, p);
+  const int n = wk.count();
   const int KT = p.ktiles;
 
   if (threadIdx.x == 0) {
@@ -217,7 +243,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
           ok = false;
           break;
         }
-        const int u = c0 + i;
+        const int u = wk.unit(i);
         const int tile = u / KT, kt = u - tile * KT;
         const int nb = tile % p.nblk;
         const int64_t chunk = (int64_t)nb * KT + kt;
@@ -247,7 +273,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
           ok = false;
           break;
         }
-        const int u = c0 + i;
+        const int u = wk.unit(i);
         const int tile = u / KT, kt = u - tile * KT;
         const int tb = tile / p.nblk;
         mbar_arrive_expect_tx(full_x + s, xbytes);
@@ -268,9 +294,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       int si = 0;
       int i = 0;
       while (ok && i < n) {
-        const int u0 = c0 + i;
+        const int u0 = wk.unit(i);
         const int tile = u0 / KT;
-        const int seg_end = min(c1, (tile + 1) * KT);  // units [u0, seg_end) belong to this tile
+        const int seg_end = min(wk.range_end(i), (tile + 1) * KT);  // units [u0, seg_end) belong to this tile
         const int buf = si & 1;
         if (si >= 2 && !mbar_wait(acce + buf, ((si >> 1) - 1) & 1)) {
           set_error(p.err, kErrWaitTimeout);
@@ -362,9 +388,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     bool failed = false;
     int si = 0;
     for (int i = 0; i < n; ++si) {
-      const int u0 = c0 + i;
+      const int u0 = wk.unit(i);
       const int tile = u0 / KT;
-      const int seg_end = min(c1, (tile + 1) * KT);
+      const int seg_end = min(wk.range_end(i), (tile + 1) * KT);
       const int ks = u0 - tile * KT, ke = seg_end - tile * KT;
       i += seg_end - u0;
       const int tb = tile / p.nblk, nb = tile - tb * p.nblk;
@@ -376,7 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         set_error(p.err, kErrWaitTimeout);
         failed = true;  // keep walking segments so the named barriers below stay matched
       }
-      const int sel = (u0 == c0) ? 0 : 1;
+      const int sel = (u0 == wk.sk0) ? 0 : 1;  // partial slot: first or last stream-K segment
       float* mine = p.partials + (((int64_t)blockIdx.x * 2 + sel) * kTcMaxTn) * 128 + nl;
       if (!failed) {
         tc_fence_after();
@@ -592,6 +618,10 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
   if (total > INT32_MAX) return cudaErrorInvalidValue;
   p.total = (int)total;
   p.grid = grid < p.total ? grid : p.total;
+  const int tiles = p.ntb * nblk;
+  p.dpq = tiles / p.grid;
+  p.sk_base = p.dpq * p.grid * ktiles;
+  p.sk_total = p.total - p.sk_base;
 
   CUtensorMap tmap;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
@@ -630,7 +660,8 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
   if (e != cudaSuccess) return e;
   // any CTA whose range starts inside a tile leaves that tile split
   bool split = false;
-  for (int b = 1; b < p.grid && !split; ++b) split = ((((int64_t)b * p.total) / p.grid) % ktiles) != 0;
+  for (int b = 1; b < p.grid && !split; ++b)
+    split = ((p.sk_base + (((int64_t)b * p.sk_total) / p.grid)) % ktiles) != 0;
   if (!split) return cudaSuccess;
   cudaLaunchConfig_t fcfg = cfg;
   fcfg.gridDim = dim3(p.grid, (p.tn + 7) / 8, 1);
