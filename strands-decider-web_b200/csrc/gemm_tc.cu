@@ -619,6 +619,9 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
   p.total = (int)total;
   p.grid = grid < p.total ? grid : p.total;
   const int tiles = p.ntb * nblk;
+  // a little fewer tiles than CTAs: one whole tile per CTA (a few idle SMs cost less than splitting
+  // nearly every tile and fixing it up)
+  if (tiles < p.grid && tiles * 4 >= p.grid * 3) p.grid = tiles;
   p.dpq = tiles / p.grid;
   p.sk_base = p.dpq * p.grid * ktiles;
   p.sk_total = p.total - p.sk_base;
