@@ -407,6 +407,17 @@ int s4_weight_download_layout(const s4_weight* w, void* wq_host, size_t wq_bytes
   return S4_OK;
 }
 
+// Tokens per tcgen05 tile when the table does not fix it: 256 (M rounded up to 16 below that);
+// 128 when K is short (<= 4096) and 256-token tiles would fill under 3/4 of the SMs while 128-token
+// tiles still fit in one wave (measured: out_proj M = 256..1024, in_proj M = 256 faster by 20-25%;
+// long-K shapes keep 256, their split tiles are cheap relative to the main loop).
+static int auto_tile(int M, const s4_weight* w, int sms) {
+  if (M < 256) return ((M + 15) / 16) * 16;
+  const long long t256 = (long long)((M + 255) / 256) * w->nblk, t128 = (long long)((M + 127) / 128) * w->nblk;
+  if (w->K <= 4096 && t256 * 4 < (long long)sms * 3 && t128 <= sms) return 128;
+  return 256;
+}
+
 int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, void* stream) {
   if (!ctx || !w) return fail(S4_ERR_INVALID, "NULL context or weight");
   if (w->ctx != ctx) return fail(S4_ERR_INVALID, "weight belongs to another context");
@@ -422,7 +433,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
   if (b.family == S4_FAMILY_TC) {
     if (b.tile != 0 && (b.tile < 16 || b.tile > 256 || b.tile % 16))
       return fail(S4_ERR_INVALID, "tc tile must be a multiple of 16 in [16, 256] (got %d)", b.tile);
-    const int tn = b.tile > 0 ? b.tile : (M >= 256 ? 256 : ((M + 15) / 16) * 16);
+    const int tn = b.tile > 0 ? b.tile : auto_tile(M, w, ctx->sm_count);
     // token rows per launch: the arrival counters hold one entry per (token block, n-block) tile
     const long long rows_cap = (long long)(kMaxTickets / w->nblk) * tn;
     const int grid = b.split > 0 ? std::min(b.split, ctx->sm_count) : ctx->sm_count;
@@ -633,7 +644,7 @@ int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, in
   for (int d = 0; d < ndst; ++d)
     if (!dst[d]) return fail(S4_ERR_INVALID, "NULL destination %d", d);
   DeviceGuard guard(ctx->device);
-  const int tn = M >= 256 ? 256 : ((M + 15) / 16) * 16;
+  const int tn = auto_tile(M, w, ctx->sm_count);
   if ((long long)((M + tn - 1) / tn) * w->nblk > kMaxTickets) return fail(S4_ERR_INVALID, "M too large for one launch");
   cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, static_cast<const __half*>(x), ldx,
                                         reinterpret_cast<__half* const*>(dst), ndst, ldy, col0, ctx->partials,
