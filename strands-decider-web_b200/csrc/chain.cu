@@ -622,6 +622,20 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     if (o.dep >= i || o.dep < -1) return *why = "dep must name an earlier op or be -1", S4_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(x[i]) & 15) || (o.K * 2) % 16) return *why = "x must be 16-byte aligned", S4_ERR_INVALID;
   }
+  // With no dependencies at all the ops may run in any order: the ops that need a phase of their own
+  // (whole-K activation window above kChainPhaseWindow) go first, so their split-K reductions overlap
+  // the streaming of the merged phase and the launch ends on a phase split at most twice per CTA.
+  {
+    bool any_dep = false;
+    for (int i = 0; i < nops; ++i) any_dep |= ops[i].dep >= 0;
+    if (!any_dep) {
+      std::vector<ChainOp> big, small;
+      for (int i = 0; i < nops; ++i)
+        (ops[i].M * (ops[i].ktiles * 128 + 64) > kChainPhaseWindow ? big : small).push_back(ops[i]);
+      ops = big;
+      ops.insert(ops.end(), small.begin(), small.end());
+    }
+  }
   // phases: runs of consecutive ops none of which reads another op of the run; an op whose whole-K
   // activation window would exceed kChainPhaseWindow stays alone (its range within a shared phase
   // could span whole n-blocks, i.e. all of K)
