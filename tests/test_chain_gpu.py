@@ -162,3 +162,35 @@ def test_chain_run_host_matches_device_run(ctx):
     _, ref2 = s4ref.matmul(hx[3 * 2048:].view(2, 6144).numpy(), p2, s2)
     ok, mr, mc = s4ref.check(got[3 * 3072:].view(2, 2048).numpy(), ref2)
     assert ok, (mr, mc)
+
+
+def test_mixed_chain_phases_match_oracle(ctx):
+    """A (indep), B (indep), C (reads A), D (indep), E (reads C), F (indep, long K): phases break at
+    the dependencies, independent neighbours share a phase; every output against the oracle on the
+    GPU's own input of that op."""
+    rng = np.random.default_rng(21)
+    M = 4
+    WA, pA, sA = _weights(ctx, rng, 2048, 3072)
+    WB, pB, sB = _weights(ctx, rng, 2048, 8224)
+    WC, pC, sC = _weights(ctx, rng, 3072, 2048)
+    WD, pD, sD = _weights(ctx, rng, 2048, 12288)
+    WE, pE, sE = _weights(ctx, rng, 2048, 6144)
+    WF, pF, sF = _weights(ctx, rng, 6144, 2048)
+    xA, xB, xD = _x(rng, M, 2048), _x(rng, M, 2048), _x(rng, M, 2048)
+    xF = _x(rng, M, 6144)
+    yA = torch.empty((M, 3072), dtype=torch.float16, device="cuda")
+    yB = torch.empty((M, 8224), dtype=torch.float16, device="cuda")
+    yC = torch.empty((M, 2048), dtype=torch.float16, device="cuda")
+    yD = torch.empty((M, 12288), dtype=torch.float16, device="cuda")
+    yE = torch.empty((M, 6144), dtype=torch.float16, device="cuda")
+    yF = torch.empty((M, 2048), dtype=torch.float16, device="cuda")
+    chain = ctx.chain([(xA, WA, yA), (xB, WB, yB), (yA, WC, yC, 0), (xD, WD, yD), (yC, WE, yE, 2), (xF, WF, yF)])
+    for _ in range(2):
+        chain.run()
+        torch.cuda.synchronize()
+        assert ctx.check_errors() == 0
+        for x, y, pk, sc in ((xA, yA, pA, sA), (xB, yB, pB, sB), (yA, yC, pC, sC), (xD, yD, pD, sD),
+                             (yC, yE, pE, sE), (xF, yF, pF, sF)):
+            _, ref = s4ref.matmul(x.cpu().numpy(), pk, sc)
+            ok, mr, mc = s4ref.check(y.cpu().numpy(), ref)
+            assert ok, (y.shape, mr, mc)
