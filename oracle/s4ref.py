@@ -201,6 +201,48 @@ def add_rmsnorm(x: np.ndarray, y=None, w=None, eps: float = 1e-6):
 
 
 # --------------------------------------------------------------------------------------------
+# wire-format scale codec (web/public/engine/wire.js:1-33)
+# --------------------------------------------------------------------------------------------
+def decode_wire_scales(wire: bytes | np.ndarray, N: int, G: int) -> np.ndarray:
+    """8-bit log-coded scales -> fp16, restating ``decodeScales`` (wire.js:19-33).
+
+    Layout (wire.js:1-3, 20-22): N row headers of 4 bytes (``m`` = fp16 bits of the row's largest
+    magnitude, ``j`` = u16 step), then N*G codes ``sign << 7 | k``. A code decodes to
+    ``|scale| = fp16(f32(m * 2^(-k*j/4096)))`` (the product in float64, rounded to float32, then to
+    fp16, both to nearest even, wire.js:5-15), with the sign bit copied into the fp16 sign.
+    Returns fp16 ``[N, G]``."""
+    b = np.frombuffer(bytes(wire), dtype=np.uint8) if not isinstance(wire, np.ndarray) else wire.view(np.uint8).ravel()
+    hdr = b[:4 * N].view(np.uint16).reshape(N, 2)
+    codes = b[4 * N:4 * N + N * G].reshape(N, G)
+    m = hdr[:, 0].view(np.float16).astype(np.float64)[:, None]             # fromHalf (wire.js:5)
+    j = hdr[:, 1].astype(np.float64)[:, None]
+    k = (codes & 127).astype(np.float64)
+    mag = (m * np.power(2.0, -(k * j) / 4096.0)).astype(np.float32).astype(np.float16)  # toHalf (wire.js:8-15)
+    bits = mag.view(np.uint16) | ((codes.astype(np.uint16) & 128) << 8)
+    return bits.view(np.float16)
+
+
+def encode_wire_scales(scales: np.ndarray) -> bytes:
+    """A simple encoder for test data (the reference's pack_wire.py is not part of the checkout): per
+    row m = largest |scale|, j spans the row's dynamic range over codes 0..127, k = nearest code."""
+    s = np.asarray(scales, dtype=np.float16)
+    N, G = s.shape
+    a = np.abs(s.astype(np.float64))
+    mx = a.max(1)
+    m16 = np.where(mx > 0, mx, 1.0).astype(np.float16)
+    mf = m16.astype(np.float64)
+    nz = np.where(a > 0, a, np.inf).min(1)
+    span = np.where(np.isfinite(nz) & (nz < mf), np.log2(mf / np.minimum(nz, mf)), 0.0)
+    j = np.clip(np.ceil(span * 4096.0 / 127.0), 1, 65535).astype(np.uint16)
+    with np.errstate(divide="ignore"):
+        e = np.where(a > 0, -np.log2(a / mf[:, None]), np.inf)
+    k = np.clip(np.rint(e * 4096.0 / j[:, None].astype(np.float64)), 0, 127).astype(np.uint8)
+    codes = k | ((s.view(np.uint16) >> 8).astype(np.uint8) & 128)
+    hdr = np.stack([m16.view(np.uint16), j], 1).astype(np.uint16)
+    return hdr.tobytes() + codes.tobytes()
+
+
+# --------------------------------------------------------------------------------------------
 # device layout (the layout the upload kernel writes; checked bit-exactly against the GPU)
 # --------------------------------------------------------------------------------------------
 NB_ROWS = 128   # output rows (N) per n-block

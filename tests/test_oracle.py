@@ -167,3 +167,64 @@ def test_add_rmsnorm_restatement_matches_loop():
     # no add, unit weight: rows come out with mean square ~1
     _, h1 = s4ref.add_rmsnorm(x)
     np.testing.assert_allclose((h1.astype(np.float64) ** 2).mean(1), 1.0, rtol=2e-3)
+
+
+def _js_from_half(h):
+    e, f = (h >> 10) & 31, h & 1023
+    v = (1024 + f) * 2.0 ** (e - 25) if e else f * 2.0 ** -24
+    return -v if h & 0x8000 else v
+
+
+def _js_to_half(x):
+    """Line-by-line port of toHalf (wire.js:8-15): x rounded to float32, then to fp16 bits."""
+    b = int(np.array([x], dtype=np.float32).view(np.uint32)[0])
+    f32 = float(np.float32(x))
+    e, rest = ((b >> 23) & 255) - 112, b & 0x1FFF
+    if 0 < e < 31:
+        h = (e << 10) | ((b >> 13) & 1023)
+        return h + 1 if rest > 0x1000 or (rest == 0x1000 and h & 1) else h
+    if e >= 31:
+        return 0x7C00
+    u = f32 * 2.0 ** 24
+    f = int(np.floor(u))
+    return f + 1 if u - f > 0.5 or (u - f == 0.5 and f & 1) else f
+
+
+def _js_decode(wire, N, G):
+    """decodeScales (wire.js:19-33) as written, element by element."""
+    b = np.frombuffer(wire, dtype=np.uint8)
+    out = np.zeros(N * G, dtype=np.uint16)
+    for r in range(N):
+        m = _js_from_half(int(b[4 * r]) | int(b[4 * r + 1]) << 8)
+        j = int(b[4 * r + 2]) | int(b[4 * r + 3]) << 8
+        for g in range(G):
+            c = int(b[4 * N + r * G + g])
+            k = c & 127
+            out[r * G + g] = _js_to_half(m * 2.0 ** (-(k * j) / 4096)) | ((c & 128) << 8)
+    return out.view(np.float16).reshape(N, G)
+
+
+def test_wire_scale_decode_matches_js_restatement():
+    rng = np.random.default_rng(8)
+    N, G = 24, 40
+    hdr = np.stack([rng.choice([0x2C00, 0x1E66, 0x3555, 0x0400, 0x03FF, 0x7BFF], N).astype(np.uint16),
+                    rng.integers(0, 4000, N).astype(np.uint16)], 1)
+    codes = rng.integers(0, 256, N * G).astype(np.uint8)
+    wire = hdr.astype(np.uint16).tobytes() + codes.tobytes()
+    np.testing.assert_array_equal(s4ref.decode_wire_scales(wire, N, G).view(np.uint16),
+                                  _js_decode(wire, N, G).view(np.uint16))
+
+
+def test_wire_scale_encoder_round_trip():
+    rng = np.random.default_rng(9)
+    sc = (rng.standard_normal((64, 64)) * 0.02).astype(np.float16)
+    dec = s4ref.decode_wire_scales(s4ref.encode_wire_scales(sc), 64, 64).astype(np.float64)
+    ref = sc.astype(np.float64)
+    assert np.all(np.sign(dec) == np.sign(ref))
+    # 127 log steps over each row's range: a nearest code is within half a step (plus fp16 rounding)
+    b = s4ref.encode_wire_scales(sc)
+    j = np.frombuffer(b[:4 * 64], dtype=np.uint16).reshape(64, 2)[:, 1].astype(np.float64)
+    half_step = 2.0 ** (j / 8192.0) - 1.0
+    big = np.abs(ref) > 1e-4
+    rel = np.abs(dec / np.where(big, ref, 1.0) - 1)
+    assert np.all(rel[big] <= (half_step[:, None] + 1e-3).repeat(64, 1)[big])
