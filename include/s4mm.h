@@ -72,6 +72,33 @@ S4_API int s4_weight_upload(s4_ctx* ctx, const uint8_t* packed, const uint16_t* 
 S4_API int s4_weight_upload_device(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, int N,
                             int K, uint32_t flags, s4_weight** out);
 
+/* Download-format ("wire") scales: N row headers of 4 bytes (m = fp16 bits, j = u16, little-endian)
+ * then N*G codes sign << 7 | k, decoded to fp16 toHalf(fromHalf(m) * 2^(-k*j/4096)) | sign << 15 as
+ * web/public/engine/wire.js:5-33 does (decodeScales), bit for bit, on the device. wire_dev holds
+ * 4*N + N*G bytes (any alignment); scales_dev receives N*G fp16 (2-byte aligned). Stream-ordered
+ * and allocation-free except the context's first wire call, which uploads a 32 KB table (do that
+ * call outside stream capture). Replaces decodeScales in unpackShard (wire.js:37-46, engine.js:82)
+ * and putRows (engine.js:128-136, one row per call there, N rows per call here). */
+S4_API int s4_decode_wire_scales(s4_ctx* ctx, const void* wire_dev, int N, int G, void* scales_dev,
+                                 void* stream);
+
+/* s4_weight_upload with the scales in the wire format (4*N + N*(K/32) bytes of host memory):
+ * uploads, decodes on the device and repacks. Synchronous. */
+S4_API int s4_weight_upload_wire(s4_ctx* ctx, const uint8_t* packed, const uint8_t* wire_scales, int N, int K,
+                                 uint32_t flags, s4_weight** out);
+
+/* Non-default weight formats (web/public/gemmbench/kernels.js:5-12; a tensor's format is
+ * {bits, group, asym}, engine.js:36 fmtOf). A block of 32 consecutive K values of one row takes
+ * `bits` u32 words: 4 bits: element e at bits 4(e%8) of word e/8; 2 bits: element e at bits 2(e%16)
+ * of word e/16; 3 bits: words 0-1 the low two bits as in the 2-bit layout, bit e of word 2 the high
+ * bit. q: [N][K/32][bits] u32; scales: fp16 [N][K/group], group 32 or 64, K % group == 0.
+ * Symmetric: w = (q - 2^(bits-1)) * scale. bias: fp16 [N][K/group] for the asymmetric form
+ * w = q * scale + bias, or NULL. flags: S4_UPLOAD_DEVICE when q/scales/bias are device pointers,
+ * else host memory. Synchronous. 4-bit group-32 symmetric is s4_weight_upload. */
+#define S4_UPLOAD_DEVICE 1u
+S4_API int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, const void* bias, int N, int K,
+                                   int bits, int group, uint32_t flags, s4_weight** out);
+
 S4_API int s4_weight_free(s4_weight* w);
 
 /* Shape and device footprint of an uploaded weight. */
@@ -144,6 +171,12 @@ S4_API int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, vo
  * ones. DEVICE pointers, asynchronous. */
 S4_API int s4_add_rmsnorm(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps, void* h,
                           void* stream);
+
+/* Online input rotation of a tensor exported with `had: n` (engine.js:238, wgsl.js:94-110): every
+ * contiguous n-block of a[M][K] (fp16, K % n == 0, n a power of two in [2, 32768]) is replaced in place
+ * by its orthonormal Walsh-Hadamard transform, computed in fp32 with the shader's butterfly order and
+ * rounded to fp16 once. Run it on the matmul's input before s4_matmul. DEVICE pointer, asynchronous. */
+S4_API int s4_fwht(s4_ctx* ctx, void* a, int M, int K, int n, void* stream);
 
 /* ---- column-sharded prefill over NVLink (one process per GPU on one node) ----
  * Each rank computes an N/g slice of every projection and writes it straight into every rank's

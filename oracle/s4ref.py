@@ -201,24 +201,132 @@ def add_rmsnorm(x: np.ndarray, y=None, w=None, eps: float = 1e-6):
 
 
 # --------------------------------------------------------------------------------------------
+# non-default weight formats (web/public/gemmbench/kernels.js:5-12, 23-38) and FWHT (wgsl.js:94-110)
+# --------------------------------------------------------------------------------------------
+def pack_format(q: np.ndarray, bits: int) -> np.ndarray:
+    """q [N][K] in [0, 2^bits) -> u32 [N][K/32][bits] in the layout kernels.js:5-9 documents: 4 bits:
+    element e at bits 4(e%8) of word e/8; 2 bits: element e at bits 2(e%16) of word e/16; 3 bits:
+    the low two bits as in the 2-bit layout in words 0-1, bit e of word 2 the high bit. (The
+    exporter that writes these is not part of the reference checkout; this packs test data.)"""
+    N, K = q.shape
+    qb = q.reshape(N, K // BLOCK, BLOCK).astype(np.uint64)
+    e = np.arange(BLOCK, dtype=np.uint64)
+    if bits == 4:
+        words = [(qb[..., 8 * w:8 * w + 8] << (4 * e[:8])).sum(-1) for w in range(4)]
+    else:
+        lo = qb & 3
+        words = [(lo[..., 16 * w:16 * w + 16] << (2 * e[:16])).sum(-1) for w in range(2)]
+        if bits == 3:
+            words.append(((qb >> 2) << e).sum(-1))
+    return np.stack(words, -1).astype(np.uint32)
+
+
+def unpack_format(words: np.ndarray, bits: int) -> np.ndarray:
+    """u32 [N][B][bits] -> q [N][B*32] (decodeBlock's extraction, kernels.js:31-34)."""
+    w = words.astype(np.uint64)
+    e = np.arange(BLOCK, dtype=np.uint64)
+    if bits == 4:
+        q = (w[..., e // 8] >> (4 * (e % 8))) & 15
+    else:
+        q = (w[..., e // 16] >> (2 * (e % 16))) & 3
+        if bits == 3:
+            q |= ((w[..., 2:3] >> e) & 1) << 2
+    N, B = words.shape[:2]
+    return q.reshape(N, B * BLOCK).astype(np.int64)
+
+
+def dequant_format(words: np.ndarray, scales: np.ndarray, bits: int, group: int, bias=None) -> np.ndarray:
+    """fp32 weights [N][K] as decodeBlock computes them in f32 (kernels.js:28-36): one scale (and
+    bias) per `group` values; symmetric ``(q - 2^(bits-1)) * sc``, asymmetric ``fma(q, sc, bi)``
+    (one rounding: the float64 sum is exact here, then rounded to float32)."""
+    q = unpack_format(words, bits)
+    N, K = q.shape
+    s = np.repeat(np.asarray(scales, dtype=np.float16).astype(np.float64).reshape(N, K // group), group, 1)
+    if bias is None:
+        return ((q - 2 ** (bits - 1)) * s).astype(np.float32)
+    b = np.repeat(np.asarray(bias, dtype=np.float16).astype(np.float64).reshape(N, K // group), group, 1)
+    return (q * s + b).astype(np.float32)
+
+
+def transcode_sym(words: np.ndarray, scales: np.ndarray, bits: int, group: int):
+    """A symmetric 2/3/4-bit, group-32/64 weight as MatMulNBits int4 bytes with [N][K/32] fp16 scales
+    holding exactly the same weights: q4 = q - 2^(bits-1) + 8, each group scale repeated over its
+    32-blocks. Returns ``(packed [N][K/32][16] u8, scales [N][K/32] f16)``."""
+    q = unpack_format(words, bits) - 2 ** (bits - 1) + 8
+    N, K = q.shape
+    packed = pack_nibbles(q.reshape(N, K // BLOCK, BLOCK).astype(np.uint8))
+    s = np.repeat(np.asarray(scales, dtype=np.float16).reshape(N, K // group), group // BLOCK, 1)
+    return packed, s
+
+
+def fwht(a: np.ndarray, n: int) -> np.ndarray:
+    """In-place orthonormal Walsh-Hadamard transform of each contiguous n-block (wgsl.js:94-110):
+    fp32 butterflies (x + y, x - y) over pairs (i, i + h) for h = 1, 2, 4, ... < n, then times
+    f32(1/sqrt(n)) and rounded to fp16. Returns the transformed fp16 copy of ``a``."""
+    sh = np.asarray(a, dtype=np.float16).astype(np.float32).reshape(-1, n).copy()
+    h = 1
+    while h < n:
+        v = sh.reshape(sh.shape[0], n // (2 * h), 2, h)
+        x, y = v[:, :, 0, :].copy(), v[:, :, 1, :].copy()
+        v[:, :, 0, :] = x + y
+        v[:, :, 1, :] = x - y
+        h *= 2
+    c = np.float32(1.0 / np.sqrt(float(n)))
+    return (sh * c).astype(np.float16).reshape(np.shape(a))
+
+
+# --------------------------------------------------------------------------------------------
 # wire-format scale codec (web/public/engine/wire.js:1-33)
 # --------------------------------------------------------------------------------------------
+# 2^(-r/4096) for r in [0, 4096), correctly rounded: libm pow is exact to the last bit on all 4096 (a
+# test checks them against 60-digit decimal values). 2^(-i/4096) = 2^-(i >> 12) * table[i & 4095], the
+# power-of-two factor exact wherever the decoded scale is not flushed to zero anyway.
+WIRE_POW = np.array([2.0 ** (-r / 4096) for r in range(4096)], dtype=np.float64)
+
+
+def wire_from_half(h: np.ndarray) -> np.ndarray:
+    """fromHalf (wire.js:5): fp16 bits -> float64, exponent 31 read as a finite power (no inf/NaN)."""
+    h = h.astype(np.int64)
+    e, f = (h >> 10) & 31, h & 1023
+    v = np.where(e > 0, np.ldexp((1024 + f).astype(np.float64), (e - 25).astype(np.int32)),
+                 np.ldexp(f.astype(np.float64), -24))
+    return np.where(h & 0x8000, -v, v)
+
+
+def wire_to_half(x: np.ndarray) -> np.ndarray:
+    """toHalf (wire.js:8-15) bit for bit: float64 -> float32 (nearest even) -> fp16 bits by the JS
+    integer steps (magnitude exponent rebased by 112, 13 dropped bits rounded half to even, overflow
+    to 0x7c00, subnormals by floor arithmetic in units of 2^-24), stored mod 2^16 as the Uint16Array
+    it lands in does."""
+    f32 = np.asarray(x, dtype=np.float64).astype(np.float32)
+    b = f32.view(np.uint32).astype(np.int64)
+    e, rest = ((b >> 23) & 255) - 112, b & 0x1FFF
+    h = (e << 10) | ((b >> 13) & 1023)
+    normal = h + ((rest > 0x1000) | ((rest == 0x1000) & ((h & 1) == 1)))
+    u = f32.astype(np.float64) * 2.0 ** 24
+    fl = np.floor(u)
+    d = u - fl
+    fi = fl.astype(np.int64)
+    sub = fi + ((d > 0.5) | ((d == 0.5) & ((fi & 1) == 1)))
+    out = np.where((e > 0) & (e < 31), normal, np.where(e >= 31, 0x7C00, sub))
+    return (out & 0xFFFF).astype(np.uint16)
+
+
 def decode_wire_scales(wire: bytes | np.ndarray, N: int, G: int) -> np.ndarray:
     """8-bit log-coded scales -> fp16, restating ``decodeScales`` (wire.js:19-33).
 
     Layout (wire.js:1-3, 20-22): N row headers of 4 bytes (``m`` = fp16 bits of the row's largest
-    magnitude, ``j`` = u16 step), then N*G codes ``sign << 7 | k``. A code decodes to
-    ``|scale| = fp16(f32(m * 2^(-k*j/4096)))`` (the product in float64, rounded to float32, then to
-    fp16, both to nearest even, wire.js:5-15), with the sign bit copied into the fp16 sign.
+    magnitude, ``j`` = u16 step, both little-endian), then N*G codes ``sign << 7 | k``. A code
+    decodes to ``toHalf(fromHalf(m) * 2^(-k*j/4096)) | sign << 15`` (the product in float64).
     Returns fp16 ``[N, G]``."""
     b = np.frombuffer(bytes(wire), dtype=np.uint8) if not isinstance(wire, np.ndarray) else wire.view(np.uint8).ravel()
-    hdr = b[:4 * N].view(np.uint16).reshape(N, 2)
-    codes = b[4 * N:4 * N + N * G].reshape(N, G)
-    m = hdr[:, 0].view(np.float16).astype(np.float64)[:, None]             # fromHalf (wire.js:5)
-    j = hdr[:, 1].astype(np.float64)[:, None]
-    k = (codes & 127).astype(np.float64)
-    mag = (m * np.power(2.0, -(k * j) / 4096.0)).astype(np.float32).astype(np.float16)  # toHalf (wire.js:8-15)
-    bits = mag.view(np.uint16) | ((codes.astype(np.uint16) & 128) << 8)
+    hdr = b[:4 * N].reshape(N, 4).astype(np.int64)
+    codes = b[4 * N:4 * N + N * G].reshape(N, G).astype(np.int64)
+    m = wire_from_half(hdr[:, 0] | hdr[:, 1] << 8)[:, None]
+    j = (hdr[:, 2] | hdr[:, 3] << 8)[:, None]
+    i = (codes & 127) * j
+    p = np.ldexp(WIRE_POW[i & 4095], -(i >> 12).astype(np.int32))
+    bits = wire_to_half(m * p) | ((codes & 128) << 8).astype(np.uint16)
     return bits.view(np.float16)
 
 

@@ -1,0 +1,99 @@
+// Non-default weight formats and the online Hadamard rotation of `had` tensors.
+//
+// Formats (web/public/gemmbench/kernels.js:5-12, engine.js:36 fmtOf): a block of 32 consecutive K
+// values of one output row takes `bits` u32 words --
+//   4 bits: element e at bits 4(e%8) of word e/8 (MatMulNBits),
+//   2 bits: element e at bits 2(e%16) of word e/16,
+//   3 bits: words 0-1 hold the low two bits as in the 2-bit layout, bit e of word 2 is the high bit,
+// with one fp16 scale per `group` (32 or 64) values, [N][K/group]. Symmetric: w = (q - 2^(bits-1)) s.
+// A symmetric 2- or 3-bit value is an int4 one with the same scale (q4 = q - 2^(bits-1) + 8 in
+// [4, 11]) and a group-64 scale is the scale of both of its 32-blocks, so upload rewrites those
+// formats into MatMulNBits bytes and [N][K/32] scales exactly, and every kernel family runs them.
+//
+// FWHT (wgsl.js:94-110, engine.js:238): each contiguous n-block of the activations is replaced by
+// its orthonormal Walsh-Hadamard transform, in place, in fp32: stages h = 1, 2, 4, ... < n turn the
+// pair (i, i+h), i = (p / h) 2h + p % h, into (x + y, x - y); the result times 1/sqrt(n) (as a
+// float) is rounded to fp16. The same operations in the same order as the reference's shader.
+#include "common.cuh"
+
+namespace s4 {
+
+__global__ void transcode_sym_kernel(const uint32_t* __restrict__ q, const __half* __restrict__ scales, int N,
+                                     int blocks, int bits, int gper, uint32_t* __restrict__ out4,
+                                     __half* __restrict__ out_s) {
+  const int64_t total = (int64_t)N * blocks;
+  const uint32_t zero = 1u << (bits - 1);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t* w = q + i * bits;
+    uint32_t o[4] = {0, 0, 0, 0};
+    if (bits == 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = w[j];
+    } else {
+      const uint32_t lo0 = w[0], lo1 = w[1], hi = bits == 3 ? w[2] : 0u;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        uint32_t v = ((e < 16 ? lo0 : lo1) >> (2 * (e & 15))) & 3u;
+        if (bits == 3) v |= ((hi >> e) & 1u) << 2;
+        o[e >> 3] |= (v + 8u - zero) << (4 * (e & 7));
+      }
+    }
+    uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+    reinterpret_cast<uint4*>(out4)[i] = ov;
+    const int64_t n = i / blocks;
+    const int b = (int)(i - n * blocks);
+    out_s[i] = scales[n * (blocks / gper) + b / gper];
+  }
+}
+
+cudaError_t launch_transcode_sym(const uint32_t* q, const __half* scales, int N, int K, int bits, int group,
+                                 uint8_t* packed4, __half* scales32, int sm_count, cudaStream_t stream) {
+  const int blocks = K / 32;
+  const int64_t total = (int64_t)N * blocks;
+  const int64_t want = (total + 255) / 256;
+  const int grid = (int)(want < (int64_t)sm_count * 8 ? (want < 1 ? 1 : want) : (int64_t)sm_count * 8);
+  transcode_sym_kernel<<<grid, 256, 0, stream>>>(q, scales, N, blocks, bits, group / 32,
+                                                  reinterpret_cast<uint32_t*>(packed4), scales32);
+  return cudaGetLastError();
+}
+
+__global__ void fwht_kernel(__half* __restrict__ a, int n, float c) {
+  extern __shared__ float fw_sh[];
+  pdl_wait();
+  const int64_t o = (int64_t)blockIdx.x * n;
+  for (int e = threadIdx.x; e < n; e += blockDim.x) fw_sh[e] = __half2float(a[o + e]);
+  __syncthreads();
+  for (int h = 1; h < n; h <<= 1) {
+    for (int p = threadIdx.x; p < n / 2; p += blockDim.x) {
+      const int i = (p / h) * 2 * h + p % h;
+      const float x = fw_sh[i], y = fw_sh[i + h];
+      fw_sh[i] = __fadd_rn(x, y);
+      fw_sh[i + h] = __fsub_rn(x, y);
+    }
+    __syncthreads();
+  }
+  pdl_launch_dependents();
+  for (int e = threadIdx.x; e < n; e += blockDim.x) a[o + e] = __float2half_rn(__fmul_rn(fw_sh[e], c));
+}
+
+cudaError_t launch_fwht(__half* a, int64_t blocks, int n, cudaStream_t stream) {
+  const size_t smem = (size_t)n * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(fwht_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const float c = (float)(1.0 / sqrt((double)n));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+  cfg.blockDim = dim3(n / 2 < 256 ? (n / 2 < 32 ? 32 : n / 2) : 256, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fwht_kernel, a, n, c);
+}
+
+}  // namespace s4

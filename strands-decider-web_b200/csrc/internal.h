@@ -43,6 +43,7 @@ struct s4_ctx {
   void* dx = nullptr;             // staging for s4_matmul_host
   void* dy = nullptr;
   size_t dx_cap = 0, dy_cap = 0;
+  double* wire_pow = nullptr;     // 2^(-r/4096) table of the wire scale decoder (first wire call)
   std::vector<s4::Bucket> table;
   s4::Bucket forced{0, S4_FAMILY_AUTO, 0, 0};
   uint64_t launches = 0;

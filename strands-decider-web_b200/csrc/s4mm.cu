@@ -2,6 +2,7 @@
 // reference interfaces each entry point replaces are in include/s4mm.h.
 #include <algorithm>
 #include <climits>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -27,6 +28,11 @@ int gemv_max_tokens();
 cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
 cudaError_t launch_silu_mul_gather(const __half* big, int M, int Is, __half* const* dst, int ndst, int64_t ldd, int col0,
                                    int sm_count, cudaStream_t stream);
+cudaError_t launch_wire_scales(const uint8_t* wire, int N, int G, const double* pow_table, uint16_t* out, int sms,
+                               cudaStream_t stream);
+cudaError_t launch_transcode_sym(const uint32_t* q, const __half* scales, int N, int K, int bits, int group,
+                                 uint8_t* packed4, __half* scales32, int sm_count, cudaStream_t stream);
+cudaError_t launch_fwht(__half* a, int64_t blocks, int n, cudaStream_t stream);
 cudaError_t launch_add_rmsnorm(float* x, const __half* y, const float* w, int M, int D, float eps, __half* h,
                                cudaStream_t stream);
 cudaError_t launch_peer_barrier(uint32_t* const* flags, int nranks, int rank, uint32_t epoch, uint32_t* err,
@@ -327,6 +333,7 @@ int s4_destroy(s4_ctx* ctx) {
   cudaFree(ctx->err);
   cudaFree(ctx->dx);
   cudaFree(ctx->dy);
+  cudaFree(ctx->wire_pow);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return S4_OK;
@@ -371,6 +378,131 @@ int s4_weight_upload_device(s4_ctx* ctx, const void* packed_dev, const void* sca
   if (rc) return rc;
   DeviceGuard guard(ctx->device);
   return upload_common(ctx, packed_dev, scales_dev, N, K, out);
+}
+
+// 2^(-r/4096), r in [0, 4096): libm pow returns the correctly rounded double for every one of them.
+static int ensure_wire_table(s4_ctx* ctx) {
+  if (ctx->wire_pow) return S4_OK;
+  std::vector<double> t(4096);
+  for (int r = 0; r < 4096; ++r) t[r] = std::pow(2.0, -r / 4096.0);
+  double* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, t.size() * sizeof(double));
+  if (e != cudaSuccess) return fail(S4_ERR_NOMEM, "wire table allocation failed");
+  e = cudaMemcpy(d, t.data(), t.size() * sizeof(double), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "wire table upload");
+  }
+  ctx->wire_pow = d;
+  return S4_OK;
+}
+
+int s4_decode_wire_scales(s4_ctx* ctx, const void* wire_dev, int N, int G, void* scales_dev, void* stream) {
+  if (!ctx || !wire_dev || !scales_dev) return fail(S4_ERR_INVALID, "NULL argument");
+  if (N < 1 || G < 1) return fail(S4_ERR_INVALID, "bad shape N=%d G=%d", N, G);
+  if (reinterpret_cast<uintptr_t>(scales_dev) & 1) return fail(S4_ERR_INVALID, "scales must be 2-byte aligned");
+  DeviceGuard guard(ctx->device);
+  int rc = ensure_wire_table(ctx);
+  if (rc) return rc;
+  cudaError_t e = s4::launch_wire_scales(static_cast<const uint8_t*>(wire_dev), N, G, ctx->wire_pow,
+                                         static_cast<uint16_t*>(scales_dev), ctx->sm_count,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "wire scale decode launch");
+  ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_weight_upload_wire(s4_ctx* ctx, const uint8_t* packed, const uint8_t* wire_scales, int N, int K,
+                          uint32_t flags, s4_weight** out) {
+  if (!ctx || !packed || !wire_scales || !out) return fail(S4_ERR_INVALID, "NULL argument");
+  if (flags != 0) return fail(S4_ERR_INVALID, "unknown flags 0x%x", flags);
+  int rc = check_shape(N, K);
+  if (rc) return rc;
+  DeviceGuard guard(ctx->device);
+  rc = ensure_wire_table(ctx);
+  if (rc) return rc;
+  const int G = K / 32;
+  const size_t pbytes = (size_t)N * G * 16, sbytes = (size_t)N * G * 2, wbytes = 4 * (size_t)N + (size_t)N * G;
+  uint8_t* d = nullptr;  // [packed | scales | wire]
+  cudaError_t e = cudaMalloc(&d, pbytes + sbytes + wbytes);
+  if (e != cudaSuccess) return fail(S4_ERR_NOMEM, "upload staging of %zu bytes failed", pbytes + sbytes + wbytes);
+  uint8_t *dp = d, *ds = d + pbytes, *dw = d + pbytes + sbytes;
+  e = cudaMemcpyAsync(dp, packed, pbytes, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dw, wire_scales, wbytes, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) {
+    e = s4::launch_wire_scales(dw, N, G, ctx->wire_pow, reinterpret_cast<uint16_t*>(ds), ctx->sm_count, ctx->stream);
+    if (e == cudaSuccess) ++ctx->launches;
+  }
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(d);
+    return cuda_fail(e, "wire upload");
+  }
+  rc = upload_common(ctx, dp, ds, N, K, out);  // same stream: runs after the decode
+  cudaFree(d);
+  return rc;
+}
+
+int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, const void* bias, int N, int K, int bits,
+                            int group, uint32_t flags, s4_weight** out) {
+  if (!ctx || !q || !scales || !out) return fail(S4_ERR_INVALID, "NULL argument");
+  if (flags & ~S4_UPLOAD_DEVICE) return fail(S4_ERR_INVALID, "unknown flags 0x%x", flags);
+  if (bits < 2 || bits > 4) return fail(S4_ERR_INVALID, "bits must be 2, 3 or 4 (got %d)", bits);
+  if (group != 32 && group != 64) return fail(S4_ERR_INVALID, "group must be 32 or 64 (got %d)", group);
+  int rc = check_shape(N, K);
+  if (rc) return rc;
+  if (K % group) return fail(S4_ERR_INVALID, "K=%d is not a multiple of the group %d", K, group);
+  if (bias) return fail(S4_ERR_UNSUPPORTED, "asymmetric formats are not supported");
+  const bool dev = flags & S4_UPLOAD_DEVICE;
+  if (bits == 4 && group == 32)
+    return dev ? s4_weight_upload_device(ctx, q, scales, N, K, 0, out)
+               : s4_weight_upload(ctx, static_cast<const uint8_t*>(q), static_cast<const uint16_t*>(scales), N, K, 0,
+                                  out);
+  if (dev && ((reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(scales) & 1)))
+    return fail(S4_ERR_INVALID, "q must be 4-byte and scales 2-byte aligned");
+  DeviceGuard guard(ctx->device);
+  const size_t blocks = (size_t)N * (K / 32);
+  const size_t qbytes = blocks * bits * 4, sbytes = (size_t)N * (K / group) * 2;
+  const size_t p4 = blocks * 16, s4b = blocks * 2;
+  const size_t in_bytes = dev ? 0 : qbytes + sbytes;
+  uint8_t* d = nullptr;  // [packed int4 | fp16 scales per 32 | (host input: q | scales)]
+  cudaError_t e = cudaMalloc(&d, p4 + s4b + in_bytes);
+  if (e != cudaSuccess) return fail(S4_ERR_NOMEM, "format staging of %zu bytes failed", p4 + s4b + in_bytes);
+  const void *dq = q, *dsc = scales;
+  if (!dev) {
+    dq = d + p4 + s4b;
+    dsc = d + p4 + s4b + qbytes;
+    e = cudaMemcpyAsync(const_cast<void*>(dq), q, qbytes, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(const_cast<void*>(dsc), scales, sbytes, cudaMemcpyHostToDevice, ctx->stream);
+  }
+  if (e == cudaSuccess) {
+    e = s4::launch_transcode_sym(static_cast<const uint32_t*>(dq), static_cast<const __half*>(dsc), N, K, bits, group,
+                                 d, reinterpret_cast<__half*>(d + p4), ctx->sm_count, ctx->stream);
+    if (e == cudaSuccess) ++ctx->launches;
+  }
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(d);
+    return cuda_fail(e, "format upload");
+  }
+  rc = upload_common(ctx, d, d + p4, N, K, out);
+  cudaFree(d);
+  return rc;
+}
+
+int s4_fwht(s4_ctx* ctx, void* a, int M, int K, int n, void* stream) {
+  if (!ctx || !a) return fail(S4_ERR_INVALID, "NULL argument");
+  if (M < 0 || K < 1) return fail(S4_ERR_INVALID, "bad shape M=%d K=%d", M, K);
+  if (n < 2 || n > 32768 || (n & (n - 1))) return fail(S4_ERR_INVALID, "n must be a power of two in [2, 32768] (got %d)", n);
+  if (K % n) return fail(S4_ERR_INVALID, "K=%d is not a multiple of n=%d", K, n);
+  if (reinterpret_cast<uintptr_t>(a) & 1) return fail(S4_ERR_INVALID, "a must be 2-byte aligned");
+  if (M == 0) return S4_OK;
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = s4::launch_fwht(static_cast<__half*>(a), (int64_t)M * (K / n), n, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fwht launch");
+  ++ctx->launches;
+  return S4_OK;
 }
 
 int s4_weight_free(s4_weight* w) {

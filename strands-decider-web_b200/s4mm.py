@@ -28,6 +28,7 @@ LIB_PATH = os.path.join(HERE, "libs4mm.so")
 FAMILY_AUTO, FAMILY_GEMV, FAMILY_TC = 0, 1, 2
 FAMILY_NAMES = {FAMILY_AUTO: "auto", FAMILY_GEMV: "gemv", FAMILY_TC: "tc"}
 ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_DEVICE, ERR_UNSUPPORTED = 1, 2, 3, 4, 5
+UPLOAD_DEVICE = 1  # s4_weight_upload_format: pointers are device memory
 
 # Every symbol include/s4mm.h declares, with its ctypes signature.
 _P = C.c_void_p
@@ -38,6 +39,11 @@ _SIGS = {
     "s4_destroy": (C.c_int, [_P]),
     "s4_weight_upload": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.c_uint32, C.POINTER(_P)]),
     "s4_weight_upload_device": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.c_uint32, C.POINTER(_P)]),
+    "s4_decode_wire_scales": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
+    "s4_weight_upload_wire": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.c_uint32, C.POINTER(_P)]),
+    "s4_weight_upload_format": (C.c_int, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint32,
+                                          C.POINTER(_P)]),
+    "s4_fwht": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, _P]),
     "s4_weight_free": (C.c_int, [_P]),
     "s4_weight_info": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_size_t)]),
     "s4_weight_layout_bytes": (C.c_int, [_P, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
@@ -225,6 +231,59 @@ class Context:
                 raise S4Error(ERR_INVALID, f"packed/scales sizes do not match N={N} K={K}")
             _check(_lib.s4_weight_upload(self.handle, p.ctypes.data, s.ctypes.data, N, K, 0, C.byref(h)))
         return Weight(self, h.value, N, K)
+
+    def upload_wire(self, packed, wire, N: int, K: int) -> Weight:
+        """Upload int4 bytes with download-format scales (``wire``: 4*N header bytes then N*(K/32)
+        codes, as the export tooling writes them) through ``s4_weight_upload_wire``. Synchronous."""
+        p = np.ascontiguousarray(np.asarray(packed, dtype=np.uint8))
+        w = np.frombuffer(bytes(wire), dtype=np.uint8) if isinstance(wire, (bytes, bytearray)) else \
+            np.ascontiguousarray(np.asarray(wire, dtype=np.uint8))
+        G = K // 32
+        if p.size != N * G * 16 or w.size != 4 * N + N * G:
+            raise S4Error(ERR_INVALID, f"packed/wire sizes do not match N={N} K={K}")
+        h = _P()
+        _check(_lib.s4_weight_upload_wire(self.handle, p.ctypes.data, w.ctypes.data, N, K, 0, C.byref(h)))
+        return Weight(self, h.value, N, K)
+
+    def upload_format(self, q, scales, N: int, K: int, bits: int, group: int = 32, bias=None) -> Weight:
+        """Upload a weight in one of the engine's formats (``{bits, group, asym}``): ``q`` u32
+        [N][K/32][bits], ``scales`` fp16 [N][K/group], ``bias`` fp16 [N][K/group] or None. Host numpy
+        arrays, or CUDA tensors (all on the device). Synchronous."""
+        h = _P()
+        if hasattr(q, "is_cuda") and q.is_cuda:
+            _check(_lib.s4_weight_upload_format(self.handle, q.data_ptr(), scales.data_ptr(),
+                                                None if bias is None else bias.data_ptr(), N, K, bits, group,
+                                                UPLOAD_DEVICE, C.byref(h)))
+        else:
+            qa = np.ascontiguousarray(np.asarray(q, dtype=np.uint32))
+            sa = np.ascontiguousarray(np.asarray(scales, dtype=np.float16))
+            ba = None if bias is None else np.ascontiguousarray(np.asarray(bias, dtype=np.float16))
+            if qa.size != N * (K // 32) * bits or sa.size != N * (K // group if group else 0) or \
+                    (ba is not None and ba.size != sa.size):
+                raise S4Error(ERR_INVALID, f"q/scales/bias sizes do not match N={N} K={K} bits={bits} group={group}")
+            _check(_lib.s4_weight_upload_format(self.handle, qa.ctypes.data, sa.ctypes.data,
+                                                None if ba is None else ba.ctypes.data, N, K, bits, group, 0,
+                                                C.byref(h)))
+        return Weight(self, h.value, N, K)
+
+    def fwht(self, a, n: int, stream=None):
+        """In-place orthonormal Walsh-Hadamard transform of every contiguous n-block of the CUDA fp16
+        tensor ``a`` [M][K] (the engine's online rotation of ``had`` tensors). Returns ``a``."""
+        M, K = (a.shape[0], a.shape[1]) if a.dim() == 2 else (1, a.numel())
+        _check(_lib.s4_fwht(self.handle, a.data_ptr(), int(M), int(K), int(n), _stream_handle(stream)))
+        return a
+
+    def decode_wire_scales(self, wire_dev, N: int, G: int, out=None, stream=None):
+        """Decode a device-resident wire scale tensor (uint8 CUDA tensor of 4*N + N*G bytes) to fp16
+        ``[N, G]`` on the device (``decodeScales``), asynchronous on ``stream``."""
+        import torch
+        if wire_dev.numel() * wire_dev.element_size() < 4 * N + N * G:
+            raise S4Error(ERR_INVALID, f"wire buffer smaller than 4*N + N*G for N={N} G={G}")
+        if out is None:
+            out = torch.empty((N, G), dtype=torch.float16, device=wire_dev.device)
+        _check(_lib.s4_decode_wire_scales(self.handle, wire_dev.data_ptr(), int(N), int(G), out.data_ptr(),
+                                          _stream_handle(stream)))
+        return out
 
     # -- compute ---------------------------------------------------------------------------------
     def matmul(self, x, W: Weight, M: int | None = None, y=None, stream=None):

@@ -1,0 +1,105 @@
+"""The engine's non-default weight formats (kernels.js:5-12: 2/3/4 bits, group 32/64, symmetric)
+uploaded through s4_weight_upload_format: the device layout is byte-identical to an upload of the
+oracle's exact int4 rewrite, and matmuls through them (GEMV, chained and tcgen05 families) meet the
+north-star tolerance against the oracle's fp32 dequantise-then-matmul of the original format. The
+online Hadamard rotation (s4_fwht, wgsl.js:94-110) is checked bit for bit against the oracle."""
+import numpy as np
+import pytest
+
+from oracle import s4ref
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+FORMATS = [(2, 32), (3, 32), (2, 64), (3, 64), (4, 64)]
+
+
+def _format_weight(rng, K, N, bits, group):
+    words = s4ref.pack_format(rng.integers(0, 2 ** bits, (N, K)), bits)
+    sc = (np.abs(rng.standard_normal((N, K // group))) * 0.02 / 2 ** (bits - 1)).astype(np.float16)
+    sc = np.where(rng.random(sc.shape) < 0.2, -sc, sc).astype(np.float16)
+    return words, sc
+
+
+@pytest.mark.parametrize("bits,group", FORMATS)
+def test_format_upload_layout_and_matmul(ctx, bits, group):
+    K, N = 2048, 1536
+    rng = np.random.default_rng(bits * 10 + group)
+    words, sc = _format_weight(rng, K, N, bits, group)
+    W = ctx.upload_format(words, sc, N, K, bits, group)
+    packed, s32 = s4ref.transcode_sym(words, sc, bits, group)
+    Wr = ctx.upload(packed, s32, N, K)
+    for a, b in zip(W.layout(), Wr.layout()):
+        np.testing.assert_array_equal(a, b)
+    deq = s4ref.dequant_format(words, sc, bits, group)
+    for M in (1, 7, 256):
+        x = s4ref.config_x(rng, M, K)
+        y = ctx.matmul(torch.from_numpy(x).cuda(), W)
+        torch.cuda.synchronize()
+        ref = x.astype(np.float32) @ deq.T
+        ok, mr, mc = s4ref.check(y.cpu().numpy(), ref)
+        assert ok, f"bits={bits} group={group} M={M}: max_rel={mr:.2e} min_cos={mc:.7f}"
+    W.free()
+    Wr.free()
+
+
+def test_format_upload_from_device_and_chain(ctx):
+    K, N = 1024, 640
+    rng = np.random.default_rng(31)
+    words, sc = _format_weight(rng, K, N, 3, 64)
+    W = ctx.upload_format(torch.from_numpy(words.view(np.int32)).cuda(), torch.from_numpy(sc).cuda(), N, K, 3, 64)
+    deq = s4ref.dequant_format(words, sc, 3, 64)
+    x = torch.from_numpy(s4ref.config_x(rng, 4, K)).cuda()
+    y = torch.empty((4, N), dtype=torch.float16, device="cuda")
+    chain = ctx.chain([(x, W, y)])
+    chain.run()
+    torch.cuda.synchronize()
+    ok, mr, mc = s4ref.check(y.cpu().numpy(), x.cpu().numpy().astype(np.float32) @ deq.T)
+    assert ok, f"max_rel={mr:.2e} min_cos={mc:.7f}"
+    chain.free()
+    W.free()
+
+
+def test_format_errors(ctx, pkg):
+    words = np.zeros((4, 2, 2), dtype=np.uint32)
+    sc = np.zeros((4, 2), dtype=np.float16)
+    for bits, group, K in ((5, 32, 64), (2, 128, 64), (2, 64, 96)):
+        with pytest.raises(pkg.S4Error):
+            ctx.upload_format(np.zeros(4 * (K // 32) * max(bits, 2), np.uint32), np.zeros(4 * (K // group), np.float16)
+                              if K % group == 0 else np.zeros(8, np.float16), 4, K, bits, group)
+    with pytest.raises(pkg.S4Error) as e:  # asymmetric: not built yet, reported as unsupported
+        ctx.upload_format(words, sc, 4, 64, 2, 32, bias=sc)
+    assert e.value.code == pkg.s4mm.ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("n,M,K", [(2, 3, 64), (64, 5, 2048), (256, 17, 6144), (4096, 2, 8192), (32768, 1, 32768)])
+def test_fwht_bit_exact(ctx, n, M, K):
+    rng = np.random.default_rng(n + M)
+    a = rng.standard_normal((M, K)).astype(np.float16)
+    d = torch.from_numpy(a).cuda()
+    ctx.fwht(d, n)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(d.cpu().numpy().view(np.uint16), s4ref.fwht(a, n).view(np.uint16))
+
+
+def test_fwht_then_matmul(ctx):
+    """A `had` tensor: the weight was exported against rotated inputs, the engine rotates A first."""
+    K, N, n = 2048, 1024, 128
+    rng = np.random.default_rng(41)
+    packed, scales = s4ref.config_weights(rng, K, N)
+    W = ctx.upload(packed, scales, N, K)
+    x = s4ref.config_x(rng, 3, K)
+    d = torch.from_numpy(x).cuda()
+    y = ctx.matmul(ctx.fwht(d, n), W)
+    torch.cuda.synchronize()
+    _, ref = s4ref.matmul(s4ref.fwht(x, n), packed, scales)
+    ok, mr, mc = s4ref.check(y.cpu().numpy(), ref)
+    assert ok, f"max_rel={mr:.2e} min_cos={mc:.7f}"
+
+
+def test_fwht_errors(ctx, pkg):
+    d = torch.zeros((2, 96), dtype=torch.float16, device="cuda")
+    for n in (3, 1, 65536, 64):  # not a power of two, too small, too large, K % n != 0
+        with pytest.raises(pkg.S4Error):
+            ctx.fwht(d, n)
+    assert ctx.check_errors() == 0

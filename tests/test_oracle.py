@@ -200,19 +200,53 @@ def _js_decode(wire, N, G):
         for g in range(G):
             c = int(b[4 * N + r * G + g])
             k = c & 127
-            out[r * G + g] = _js_to_half(m * 2.0 ** (-(k * j) / 4096)) | ((c & 128) << 8)
+            tab = _js_to_half(m * 2.0 ** (-(k * j) / 4096)) & 0xFFFF  # a Uint16Array element
+            out[r * G + g] = (tab | ((c & 128) << 8)) & 0xFFFF
     return out.view(np.float16).reshape(N, G)
 
 
-def test_wire_scale_decode_matches_js_restatement():
-    rng = np.random.default_rng(8)
-    N, G = 24, 40
-    hdr = np.stack([rng.choice([0x2C00, 0x1E66, 0x3555, 0x0400, 0x03FF, 0x7BFF], N).astype(np.uint16),
-                    rng.integers(0, 4000, N).astype(np.uint16)], 1)
+# row headers the exporter writes (positive normal and subnormal m) and the ones it never writes but a
+# decoder still has to map like the JS does: m = 0, -0, exponent 31 (finite in fromHalf), negative m
+WIRE_EDGE_M = [0x2C00, 0x1E66, 0x3555, 0x0400, 0x03FF, 0x0001, 0x7BFF, 0x0000, 0x8000, 0x7C00, 0x7FFF,
+               0xAC00, 0x83FF, 0x8001]
+WIRE_EDGE_J = [0, 1, 37, 4096, 4097, 20000, 65535]
+
+
+def wire_case(seed, N, G):
+    """Seeded wire bytes: headers from the edge lists and random ones, codes covering all 256 values."""
+    rng = np.random.default_rng(seed)
+    m = np.where(rng.random(N) < 0.5, rng.choice(WIRE_EDGE_M, N), rng.integers(0, 65536, N))
+    j = np.where(rng.random(N) < 0.5, rng.choice(WIRE_EDGE_J, N), rng.integers(0, 4000, N))
+    hdr = np.stack([m, j], 1).astype(np.uint16)
     codes = rng.integers(0, 256, N * G).astype(np.uint8)
-    wire = hdr.astype(np.uint16).tobytes() + codes.tobytes()
-    np.testing.assert_array_equal(s4ref.decode_wire_scales(wire, N, G).view(np.uint16),
-                                  _js_decode(wire, N, G).view(np.uint16))
+    codes[:256] = np.arange(256, dtype=np.uint8)[:min(256, N * G)]
+    return hdr.tobytes() + codes.tobytes()
+
+
+def test_wire_pow_table_correctly_rounded():
+    from decimal import Decimal, getcontext
+    getcontext().prec = 60
+    ln2 = Decimal(2).ln()
+    exact = np.array([float((-(ln2 * r) / 4096).exp()) for r in range(4096)])
+    np.testing.assert_array_equal(s4ref.WIRE_POW, exact)
+
+
+def test_wire_scale_decode_matches_js_restatement():
+    for seed, N, G in ((8, 24, 40), (10, 64, 64), (11, 3, 1)):
+        wire = wire_case(seed, N, G)
+        np.testing.assert_array_equal(s4ref.decode_wire_scales(wire, N, G).view(np.uint16),
+                                      _js_decode(wire, N, G).view(np.uint16))
+
+
+def test_wire_to_half_matches_rne_for_positive_floats():
+    # on positive float32 values toHalf is IEEE round-to-nearest-even to fp16
+    rng = np.random.default_rng(12)
+    x = np.concatenate([np.abs(rng.standard_normal(20000)) * 10.0 ** rng.integers(-9, 5, 20000),
+                        np.ldexp(1.0 + np.arange(64) / 1024, -25), [65504.0, 65519.9, 65520.0, 1e-30]])
+    x32 = x.astype(np.float32)
+    with np.errstate(over="ignore"):  # values above 65520 round to inf, as intended
+        want = x32.astype(np.float16).view(np.uint16)
+    np.testing.assert_array_equal(s4ref.wire_to_half(x32.astype(np.float64)), want)
 
 
 def test_wire_scale_encoder_round_trip():
@@ -228,3 +262,77 @@ def test_wire_scale_encoder_round_trip():
     big = np.abs(ref) > 1e-4
     rel = np.abs(dec / np.where(big, ref, 1.0) - 1)
     assert np.all(rel[big] <= (half_step[:, None] + 1e-3).repeat(64, 1)[big])
+
+
+# ---- non-default weight formats and FWHT ----------------------------------------------------------
+def _wgsl_decode_block(words, bits, group, scales, bias, n, b, blocks):
+    """decodeBlock (kernels.js:23-38) for one block, element by element with the shader's shifts."""
+    w = [int(v) for v in words]
+    g = (n * blocks + b) // (group // 32)
+    sc = np.float32(scales[g])
+    out = []
+    for i in range(8):
+        e = 4 * i
+        for c in range(4):
+            if bits == 4:
+                q = ((w[e >> 3] >> (4 * (e & 7))) >> (4 * c)) & 15
+            else:
+                q = ((w[e >> 4] >> (2 * (e & 15))) >> (2 * c)) & 3
+                if bits == 3:
+                    q |= ((w[2] >> e >> c) & 1) << 2
+            if bias is None:
+                out.append(np.float32(np.float32(q) - np.float32(2 ** (bits - 1))) * sc)
+            else:  # fma: exact product and sum in float64, one rounding
+                out.append(np.float32(float(q) * float(sc) + float(np.float32(bias[g]))))
+    return np.array(out, dtype=np.float32)
+
+
+@pytest.mark.parametrize("bits,group,asym", [(2, 32, False), (3, 32, False), (4, 64, False), (3, 64, False),
+                                             (2, 64, True), (4, 32, True), (3, 32, True)])
+def test_format_dequant_matches_wgsl_decode(bits, group, asym):
+    rng = np.random.default_rng(bits * 100 + group + asym)
+    N, K = 6, 256
+    q = rng.integers(0, 2 ** bits, (N, K))
+    words = s4ref.pack_format(q, bits)
+    sc = (rng.standard_normal(N * K // group) * 0.03).astype(np.float16)
+    bi = (rng.standard_normal(N * K // group) * 0.05).astype(np.float16) if asym else None
+    deq = s4ref.dequant_format(words, sc, bits, group, bi)
+    blocks = K // 32
+    for n in range(N):
+        for b in range(blocks):
+            np.testing.assert_array_equal(deq[n, 32 * b:32 * b + 32],
+                                          _wgsl_decode_block(words[n, b], bits, group, sc, bi, n, b, blocks))
+
+
+@pytest.mark.parametrize("bits,group", [(2, 32), (3, 32), (2, 64), (3, 64), (4, 64)])
+def test_transcode_sym_is_exact(bits, group):
+    rng = np.random.default_rng(bits + group)
+    N, K = 5, 192
+    words = s4ref.pack_format(rng.integers(0, 2 ** bits, (N, K)), bits)
+    sc = (rng.standard_normal((N, K // group)) * 0.03).astype(np.float16)
+    packed, s32 = s4ref.transcode_sym(words, sc, bits, group)
+    np.testing.assert_array_equal(s4ref.dequant(packed, s32), s4ref.dequant_format(words, sc, bits, group))
+
+
+def test_fwht_matches_shader_loop():
+    rng = np.random.default_rng(13)
+    for n in (2, 8, 64):
+        a = rng.standard_normal((3, 2 * n)).astype(np.float16)
+        sh = a.astype(np.float32).reshape(-1, n).copy()
+        for blk in sh:  # wgsl.js:100-108, one workgroup per block
+            h = 1
+            while h < n:
+                for p in range(n // 2):
+                    i = (p // h) * 2 * h + p % h
+                    x, y = blk[i], blk[i + h]
+                    blk[i], blk[i + h] = x + y, x - y
+                h *= 2
+        want = (sh * np.float32(1.0 / np.sqrt(float(n)))).astype(np.float16).reshape(a.shape)
+        np.testing.assert_array_equal(s4ref.fwht(a, n).view(np.uint16), want.view(np.uint16))
+
+
+def test_fwht_is_orthonormal():
+    rng = np.random.default_rng(14)
+    a = rng.standard_normal((4, 1024)).astype(np.float16)
+    twice = s4ref.fwht(s4ref.fwht(a, 256), 256)  # H is its own inverse
+    np.testing.assert_allclose(twice.astype(np.float32), a.astype(np.float32), atol=4e-3, rtol=4e-3)
