@@ -94,7 +94,9 @@ S4_API int s4_weight_upload_wire(s4_ctx* ctx, const uint8_t* packed, const uint8
  * bit. q: [N][K/32][bits] u32; scales: fp16 [N][K/group], group 32 or 64, K % group == 0.
  * Symmetric: w = (q - 2^(bits-1)) * scale. bias: fp16 [N][K/group] for the asymmetric form
  * w = q * scale + bias, or NULL. flags: S4_UPLOAD_DEVICE when q/scales/bias are device pointers,
- * else host memory. Synchronous. 4-bit group-32 symmetric is s4_weight_upload. */
+ * else host memory. Synchronous. 4-bit group-32 symmetric is s4_weight_upload. Symmetric formats
+ * become plain int4 weights (exactly); asymmetric ones keep their biases and run through s4_matmul and
+ * s4_matmul_noalloc (the chained launch rejects them with S4_ERR_UNSUPPORTED). */
 #define S4_UPLOAD_DEVICE 1u
 S4_API int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, const void* bias, int N, int K,
                                    int bits, int group, uint32_t flags, s4_weight** out);

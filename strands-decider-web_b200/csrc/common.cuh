@@ -162,6 +162,30 @@ __device__ __forceinline__ void i4x8_to_h2x4_centered(uint32_t w, uint32_t (&h)[
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[3]) : "r"(t3), "r"(mul16), "r"(add72));
 }
 
+// Same element order, uncentered: fp16 q in [0, 15] (asymmetric formats, w = q * scale + bias).
+__device__ __forceinline__ void i4x8_to_h2x4_raw(uint32_t w, uint32_t (&h)[4]) {
+  const uint32_t kLo = 0x000f000fu, kHi = 0x00f000f0u, kMagic = 0x64006400u;
+  const uint32_t sub1024 = 0x64006400u;  // half2(1024, 1024)
+  const uint32_t mul16 = 0x2c002c00u;    // half2(1/16, 1/16)
+  const uint32_t add64 = 0xd400d400u;    // half2(-64, -64)
+  const uint32_t top = w >> 8;
+  uint32_t t0 = lop3_and_or(w, kLo, kMagic);
+  uint32_t t1 = lop3_and_or(w, kHi, kMagic);
+  uint32_t t2 = lop3_and_or(top, kLo, kMagic);
+  uint32_t t3 = lop3_and_or(top, kHi, kMagic);
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(h[0]) : "r"(t0), "r"(sub1024));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[1]) : "r"(t1), "r"(mul16), "r"(add64));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(h[2]) : "r"(t2), "r"(sub1024));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[3]) : "r"(t3), "r"(mul16), "r"(add64));
+}
+
+// h[e] = h[e] * s + b for four half2 words (one fp16 scale and bias broadcast to both halves).
+__device__ __forceinline__ void h2x4_fma(uint32_t (&h)[4], uint32_t s16, uint32_t b16) {
+  const uint32_t s2 = s16 | (s16 << 16), b2 = b16 | (b16 << 16);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[e]) : "r"(h[e]), "r"(s2), "r"(b2));
+}
+
 // Atomic add with release (orders this thread's, and by cumulativity its CTA's barrier-ordered,
 // earlier writes) and acquire (orders later reads) semantics at GPU scope.
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {

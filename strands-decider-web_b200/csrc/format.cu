@@ -9,6 +9,8 @@
 // A symmetric 2- or 3-bit value is an int4 one with the same scale (q4 = q - 2^(bits-1) + 8 in
 // [4, 11]) and a group-64 scale is the scale of both of its 32-blocks, so upload rewrites those
 // formats into MatMulNBits bytes and [N][K/32] scales exactly, and every kernel family runs them.
+// Asymmetric (w = q s + b, fp16 bias per group): q is kept uncentered as a nibble in [0, 2^bits) and
+// scales and biases are spread to [N][K/32]; the kernels dequantise fma(q, s, b) in fp16.
 //
 // FWHT (wgsl.js:94-110, engine.js:238): each contiguous n-block of the activations is replaced by
 // its orthonormal Walsh-Hadamard transform, in place, in fp32: stages h = 1, 2, 4, ... < n turn the
@@ -18,11 +20,11 @@
 
 namespace s4 {
 
-__global__ void transcode_sym_kernel(const uint32_t* __restrict__ q, const __half* __restrict__ scales, int N,
-                                     int blocks, int bits, int gper, uint32_t* __restrict__ out4,
-                                     __half* __restrict__ out_s) {
+__global__ void transcode_kernel(const uint32_t* __restrict__ q, const __half* __restrict__ scales,
+                                 const __half* __restrict__ bias, int N, int blocks, int bits, int gper,
+                                 uint32_t* __restrict__ out4, __half* __restrict__ out_s, __half* __restrict__ out_b) {
   const int64_t total = (int64_t)N * blocks;
-  const uint32_t zero = 1u << (bits - 1);
+  const uint32_t zero = bias ? 8u : 1u << (bits - 1);  // asymmetric: q stays uncentered
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const uint32_t* w = q + i * bits;
     uint32_t o[4] = {0, 0, 0, 0};
@@ -42,18 +44,21 @@ __global__ void transcode_sym_kernel(const uint32_t* __restrict__ q, const __hal
     reinterpret_cast<uint4*>(out4)[i] = ov;
     const int64_t n = i / blocks;
     const int b = (int)(i - n * blocks);
-    out_s[i] = scales[n * (blocks / gper) + b / gper];
+    const int64_t gi = n * (blocks / gper) + b / gper;
+    out_s[i] = scales[gi];
+    if (bias) out_b[i] = bias[gi];
   }
 }
 
-cudaError_t launch_transcode_sym(const uint32_t* q, const __half* scales, int N, int K, int bits, int group,
-                                 uint8_t* packed4, __half* scales32, int sm_count, cudaStream_t stream) {
+cudaError_t launch_transcode(const uint32_t* q, const __half* scales, const __half* bias, int N, int K, int bits,
+                             int group, uint8_t* packed4, __half* scales32, __half* bias32, int sm_count,
+                             cudaStream_t stream) {
   const int blocks = K / 32;
   const int64_t total = (int64_t)N * blocks;
   const int64_t want = (total + 255) / 256;
   const int grid = (int)(want < (int64_t)sm_count * 8 ? (want < 1 ? 1 : want) : (int64_t)sm_count * 8);
-  transcode_sym_kernel<<<grid, 256, 0, stream>>>(q, scales, N, blocks, bits, group / 32,
-                                                  reinterpret_cast<uint32_t*>(packed4), scales32);
+  transcode_kernel<<<grid, 256, 0, stream>>>(q, scales, bias, N, blocks, bits, group / 32,
+                                              reinterpret_cast<uint32_t*>(packed4), scales32, bias32);
   return cudaGetLastError();
 }
 

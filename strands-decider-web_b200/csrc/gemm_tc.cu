@@ -41,6 +41,9 @@ constexpr int kTcEpiWarp0 = 12;     // warps 12..15 drain TMEM (lane quarter = w
 constexpr int kTcXStageBytes = kTcMaxTn * 128;  // tn rows x 64 fp16
 constexpr int kTcAStageBytes = 128 * 128;       // 128 rows x 64 fp16
 constexpr int kTcWSlotBytes = kChunkWBytes + kChunkSBytes;
+// asymmetric formats: a slot also holds the chunk's biases; fewer slots fit the same region
+constexpr int kTcWSlotBytesAsym = kChunkWBytes + 2 * kChunkSBytes;
+constexpr int kTcSlotsWAsym = (kTcSlotsW * kTcWSlotBytes) / kTcWSlotBytesAsym;
 constexpr int kTcOffX = 0;
 constexpr int kTcOffA = kTcOffX + kTcStagesX * kTcXStageBytes;
 constexpr int kTcOffW = kTcOffA + kTcStagesA * kTcAStageBytes;
@@ -58,6 +61,7 @@ constexpr int kTcMaxDst = 8;  // output copies one launch writes (this GPU + pee
 struct TcParams {
   const uint8_t* wq;
   const uint8_t* ws;
+  const uint8_t* wb;  // asymmetric formats: biases in the layout of ws (else nullptr)
   __half* ydst[kTcMaxDst];  // output buffers: y[tok * ldy + ycol0 + n] is written to each
   int ndst;
   int64_t ldy;
@@ -173,8 +177,10 @@ __device__ __forceinline__ TcWork tc_work(int b, const TcParams& p) {
 
 // kTicketFixup: split tiles are finished inside this kernel by the last CTA to arrive (atomic
 // ticket); otherwise partials are only published and tc_fixup_kernel, launched next, sums them.
-template <bool kTicketFixup>
+template <bool kTicketFixup, bool kAsym>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p, const __grid_constant__ CUtensorMap tmap_x) {
+  constexpr int SW = kAsym ? kTcSlotsWAsym : kTcSlotsW;            // raw weight ring slots
+  constexpr int WB = kAsym ? kTcWSlotBytesAsym : kTcWSlotBytes;    // bytes per slot
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -187,7 +193,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   uint64_t* ddone = empty_x + kTcStagesX;
   uint64_t* empty_a = ddone + kTcStagesA;
   uint64_t* full_w = empty_a + kTcStagesA;
-  uint64_t* empty_w = full_w + kTcSlotsW;
+  uint64_t* empty_w = full_w + kTcSlotsW;  // barrier arrays keep the symmetric layout's size
   uint64_t* accf = empty_w + kTcSlotsW;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
@@ -208,7 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       mbar_init(ddone + s, kTcDequantWarps);
       mbar_init(empty_a + s, 1);
     }
-    for (int s = 0; s < kTcSlotsW; ++s) {
+    for (int s = 0; s < SW; ++s) {
       mbar_init(full_w + s, 1);
       mbar_init(empty_w + s, kTcDequantWarps);
     }
@@ -237,8 +243,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       int issued = 0;
       bool ok = true;
       for (int i = 0; i < n; ++i) {
-        const int slot = i % kTcSlotsW;
-        if (i >= kTcSlotsW && !mbar_wait(empty_w + slot, ((i / kTcSlotsW) - 1) & 1)) {
+        const int slot = i % SW;
+        if (i >= SW && !mbar_wait(empty_w + slot, ((i / SW) - 1) & 1)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
           break;
@@ -247,16 +253,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         const int tile = u / KT, kt = u - tile * KT;
         const int nb = tile % p.nblk;
         const int64_t chunk = (int64_t)nb * KT + kt;
-        uint8_t* dst = wraw + slot * kTcWSlotBytes;
-        mbar_arrive_expect_tx(full_w + slot, kTcWSlotBytes);
+        uint8_t* dst = wraw + slot * WB;
+        mbar_arrive_expect_tx(full_w + slot, WB);
         bulk_g2s_plain(dst, p.wq + chunk * kChunkWBytes, kChunkWBytes, full_w + slot);
         bulk_g2s_plain(dst + kChunkWBytes, p.ws + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
+        if (kAsym) bulk_g2s_plain(dst + kChunkWBytes + kChunkSBytes, p.wb + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
         ++issued;
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
-        for (int i = (issued > kTcSlotsW ? issued - kTcSlotsW : 0); i < issued; ++i)
-          if (!mbar_wait_until(full_w + (i % kTcSlotsW), (i / kTcSlotsW) & 1, deadline)) break;
+        for (int i = (issued > SW ? issued - SW : 0); i < issued; ++i)
+          if (!mbar_wait_until(full_w + (i % SW), (i / SW) & 1, deadline)) break;
       }
     }
   } else if (warp == 2) {
@@ -333,14 +340,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     const int d = threadIdx.x - 128;
     bool ok = true;
     for (int i = 0; i < n && ok; ++i) {
-      const int s = i % kTcStagesA, slot = i % kTcSlotsW;
-      if (!mbar_wait(full_w + slot, (i / kTcSlotsW) & 1) ||
+      const int s = i % kTcStagesA, slot = i % SW;
+      if (!mbar_wait(full_w + slot, (i / SW) & 1) ||
           (i >= kTcStagesA && !mbar_wait(empty_a + s, ((i / kTcStagesA) - 1) & 1))) {
         set_error(p.err, kErrWaitTimeout);
         ok = false;
         break;
       }
-      const uint8_t* src = wraw + slot * kTcWSlotBytes;
+      const uint8_t* src = wraw + slot * WB;
       const uint32_t dst = smem_u32(wa + s * kTcAStageBytes);
 #pragma unroll
       for (int rep = 0; rep < 256 / (32 * kTcDequantWarps); ++rep) {
@@ -362,10 +369,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
           const int r = sub * 16 + g + 8 * h;
           const int c = blk * 4 + t;
           uint32_t hv[4];
-          i4x8_to_h2x4_centered(w, hv);
-          const uint32_t s2 = sbits | (sbits << 16);
+          if constexpr (kAsym) {  // w = fma(q, scale, bias) in fp16 (kernels.js:36)
+            const uint2 bi = *reinterpret_cast<const uint2*>(src + kChunkWBytes + kChunkSBytes + sub * 64 + g * 8);
+            const uint32_t jb = odd ? (jj ^ 2) : jj;
+            const uint32_t bbits = ((jb >> 1) ? bi.y : bi.x) >> (16 * (jb & 1)) & 0xFFFFu;
+            i4x8_to_h2x4_raw(w, hv);
+            h2x4_fma(hv, sbits, bbits);
+          } else {
+            i4x8_to_h2x4_centered(w, hv);
+            const uint32_t s2 = sbits | (sbits << 16);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(hv[e]) : "r"(hv[e]), "r"(s2));
+            for (int e = 0; e < 4; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(hv[e]) : "r"(hv[e]), "r"(s2));
+          }
           const uint32_t addr = dst + r * 128 + ((c ^ (r & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(hv[0]), "r"(hv[1]), "r"(hv[2]),
                        "r"(hv[3])
@@ -584,7 +599,8 @@ size_t tc_partials_bytes(int max_grid) { return (size_t)max_grid * 2 * kTcMaxTn 
 // tile_n: requested tokens per tile (0 = automatic).
 // General form: x has row stride ldx (elements); the output goes to ndst buffers with row stride ldy,
 // starting at column ycol0 (a rank's slice of a gathered buffer).
-cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half* x, int64_t ldx, __half* const* ydst,
+cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, int64_t ldx,
+                              __half* const* ydst,
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
                               cudaStream_t stream, bool pdl, bool ticket_fixup) {
@@ -596,6 +612,7 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
   TcParams p;
   p.wq = wq;
   p.ws = ws;
+  p.wb = wb;
   for (int d = 0; d < kTcMaxDst; ++d) p.ydst[d] = d < ndst ? ydst[d] : nullptr;
   p.ndst = ndst;
   p.ldy = ldy;
@@ -642,9 +659,13 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    e = cudaFuncSetAttribute(tc_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+      e = cudaFuncSetAttribute(tc_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tc_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tc_gemm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
@@ -658,8 +679,11 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (ticket_fixup) return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<true>, p, tmap);
-  e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<false>, p, tmap);
+  if (ticket_fixup)
+    return wb ? cudaLaunchKernelEx(&cfg, tc_gemm_kernel<true, true>, p, tmap)
+              : cudaLaunchKernelEx(&cfg, tc_gemm_kernel<true, false>, p, tmap);
+  e = wb ? cudaLaunchKernelEx(&cfg, tc_gemm_kernel<false, true>, p, tmap)
+         : cudaLaunchKernelEx(&cfg, tc_gemm_kernel<false, false>, p, tmap);
   if (e != cudaSuccess) return e;
   // any CTA whose range starts inside a tile leaves that tile split
   bool split = false;
@@ -673,11 +697,12 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half
   return cudaLaunchKernelEx(&fcfg, tc_fixup_kernel, p);
 }
 
-cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
-                           uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
-                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl, bool ticket_fixup) {
+cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
+                           float* partials, uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K,
+                           int nblk, int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl,
+                           bool ticket_fixup) {
   __half* dst[1] = {y};
-  return launch_tc_gemm_ex(wq, ws, x, K, dst, 1, N, 0, partials, tickets, max_tickets, err, M, N, K, nblk, ktiles,
+  return launch_tc_gemm_ex(wq, ws, wb, x, K, dst, 1, N, 0, partials, tickets, max_tickets, err, M, N, K, nblk, ktiles,
                            tile_n, grid, stream, pdl, ticket_fixup);
 }
 
@@ -745,7 +770,7 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   if (e == cudaSuccess) e = cudaMemsetAsync(err, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: clearing the static scratch failed");
   const int grid = w->ctx->sm_count < kStaticMaxGrid ? w->ctx->sm_count : kStaticMaxGrid;
-  e = launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
+  e = launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
                      (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true, true);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: tcgen05 GEMM launch failed");
   return S4_OK;

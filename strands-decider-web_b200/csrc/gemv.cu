@@ -29,6 +29,7 @@ namespace s4 {
 struct GemvParams {
   const uint8_t* wq;  // repacked int4: chunk (nb, kt) at wq + (nb*KT + kt)*4096, sub-tile s at +s*512
   const uint8_t* ws;  // repacked scales: chunk at ws + (nb*KT + kt)*512, sub-tile s at +s*64
+  const uint8_t* wb;  // asymmetric formats: biases in the layout of ws (else unused)
   const __half* x;    // [M][K]
   __half* y;          // [M][N]
   uint32_t* err;      // device error word
@@ -37,7 +38,7 @@ struct GemvParams {
   int split;          // S: CTAs per cluster / k-splits per n-block
   int token0;         // first token of this launch (tokens token0 .. token0 + 8*MG - 1)
   // dynamic shared memory layout (bytes), from gemv_layout()
-  int s_off, x_off, red_off, bar_off;
+  int s_off, b_off, x_off, red_off, bar_off;
   int xrow;           // padded activation row: 128 bytes per k-tile + 64
 };
 
@@ -50,16 +51,17 @@ constexpr int kGemvGroup = 4;                 // k-tiles per bulk-copy group (on
 constexpr int kGemvMaxCopyGroups = kGemvMaxKtPerCta / kGemvGroup;
 
 // Shared memory of one CTA holding at most `nkt` k-tiles for MG token groups: weights, scales,
-// activation rows (64 bytes of padding per row: consecutive rows start 16 banks apart),
+// biases (asymmetric formats only), activation rows (64 bytes of padding per row: consecutive rows start 16 banks apart),
 // reduction partials, mbarriers.
 struct GemvLayout {
-  int s_off, x_off, red_off, bar_off, total, xrow;
+  int s_off, b_off, x_off, red_off, bar_off, total, xrow;
 };
-static GemvLayout gemv_layout(int nkt, int MG) {
+static GemvLayout gemv_layout(int nkt, int MG, bool asym) {
   GemvLayout L;
   L.xrow = nkt * 128 + 64;
   L.s_off = nkt * kChunkWBytes;
-  L.x_off = L.s_off + nkt * kChunkSBytes;
+  L.b_off = L.s_off + nkt * kChunkSBytes;
+  L.x_off = L.b_off + (asym ? nkt * kChunkSBytes : 0);
   L.red_off = L.x_off + 8 * MG * L.xrow;
   L.bar_off = L.red_off + kGemvWarps * 32 * 16 * MG;
   L.total = L.bar_off + kGemvMaxCopyGroups * 8;
@@ -82,11 +84,12 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-template <int MG>
+template <int MG, bool ASYM>
 __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* wsm = smem;
   uint8_t* ssm = smem + p.s_off;
+  uint8_t* bsm = smem + p.b_off;
   uint8_t* xs = smem + p.x_off;
   float4* red = reinterpret_cast<float4*>(smem + p.red_off);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
@@ -108,9 +111,11 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
     const int64_t chunk0 = (int64_t)nb * KT + kt0;
     for (int q = 0; q < ngroups; ++q) {
       const int t0 = q * kGemvGroup, nt = min(kGemvGroup, nkt - t0);
-      mbar_arrive_expect_tx(bars + q, (uint32_t)nt * (kChunkWBytes + kChunkSBytes));
+      mbar_arrive_expect_tx(bars + q, (uint32_t)nt * (kChunkWBytes + (ASYM ? 2 : 1) * kChunkSBytes));
       bulk_g2s(wsm + t0 * kChunkWBytes, p.wq + (chunk0 + t0) * kChunkWBytes, (uint32_t)nt * kChunkWBytes, bars + q, pol);
       bulk_g2s(ssm + t0 * kChunkSBytes, p.ws + (chunk0 + t0) * kChunkSBytes, (uint32_t)nt * kChunkSBytes, bars + q, pol);
+      if (ASYM)
+        bulk_g2s(bsm + t0 * kChunkSBytes, p.wb + (chunk0 + t0) * kChunkSBytes, (uint32_t)nt * kChunkSBytes, bars + q, pol);
     }
   }
   pdl_launch_dependents();
@@ -151,7 +156,12 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
       if (kk < nkt) {
         const uint4 w = *reinterpret_cast<const uint4*>(wl + kk * kChunkWBytes);
         const uint2 sc = *reinterpret_cast<const uint2*>(sl + kk * kChunkSBytes);
-        gemv_tile<MG>(w, sc, xl + kk * 128, xgroup, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
+        if constexpr (ASYM) {
+          const uint2 bi = *reinterpret_cast<const uint2*>(sl + (p.b_off - p.s_off) + kk * kChunkSBytes);
+          gemv_tile_asym<MG>(w, sc, bi, xl + kk * 128, xgroup, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
+        } else {
+          gemv_tile<MG>(w, sc, xl + kk * 128, xgroup, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
+        }
       }
     }
   }
@@ -204,23 +214,25 @@ static int gemv_pick_split(int nblk, int KT, int sm_count) {
   return s;
 }
 
-template <int MG>
+template <int MG, bool ASYM>
 static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t stream, bool pdl) {
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  const GemvLayout L = gemv_layout((p.ktiles + p.split - 1) / p.split, MG);
+  const GemvLayout L = gemv_layout((p.ktiles + p.split - 1) / p.split, MG, ASYM);
   p.s_off = L.s_off;
+  p.b_off = L.b_off;
   p.x_off = L.x_off;
   p.red_off = L.red_off;
   p.bar_off = L.bar_off;
   p.xrow = L.xrow;
   if (!configured[dev]) {
-    const int max_smem = gemv_layout(kGemvMaxKtPerCta, kGemvMaxGroups).total;
-    e = cudaFuncSetAttribute(gemv_cluster_kernel<MG>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_cluster_kernel<MG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    const int max_smem = gemv_layout(kGemvMaxKtPerCta, kGemvMaxGroups, ASYM).total;
+    e = cudaFuncSetAttribute(gemv_cluster_kernel<MG, ASYM>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_cluster_kernel<MG, ASYM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
@@ -240,15 +252,16 @@ static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t strea
   attr[2].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicySpread;
   cfg.attrs = attr;
   cfg.numAttrs = 3;
-  return cudaLaunchKernelEx(&cfg, gemv_cluster_kernel<MG>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_cluster_kernel<MG, ASYM>, p);
 }
 
-cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, uint32_t* err, int M, int N,
-                        int K, int nblk, int ktiles, int token0, int groups, int split, int sm_count,
-                        cudaStream_t stream, bool pdl) {
+cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
+                        uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0, int groups, int split,
+                        int sm_count, cudaStream_t stream, bool pdl) {
   GemvParams p;
   p.wq = wq;
   p.ws = ws;
+  p.wb = wb;
   p.x = x;
   p.y = y;
   p.err = err;
@@ -270,8 +283,8 @@ cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, _
   if ((ktiles + p.split - 1) / p.split > kGemvMaxKtPerCta) return cudaErrorInvalidValue;  // K > 16384
   p.token0 = token0;
   switch (groups) {
-    case 1: return launch_gemv_mg<1>(p, sm_count, stream, pdl);
-    case 2: return launch_gemv_mg<2>(p, sm_count, stream, pdl);
+    case 1: return wb ? launch_gemv_mg<1, true>(p, sm_count, stream, pdl) : launch_gemv_mg<1, false>(p, sm_count, stream, pdl);
+    case 2: return wb ? launch_gemv_mg<2, true>(p, sm_count, stream, pdl) : launch_gemv_mg<2, false>(p, sm_count, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -35,4 +35,31 @@ __device__ __forceinline__ void gemv_tile(const uint4 w, const uint2 sc, const u
   }
 }
 
+// Asymmetric formats: the lane's weights dequantised to fp16 first, w = fma(q, scale, bias) per
+// element (the f16 form of kernels.js:36), then one mma per 16 K; no per-block scaling after it.
+// bi = biases in the order of sc.
+template <int MG>
+__device__ __forceinline__ void gemv_tile_asym(const uint4 w, const uint2 sc, const uint2 bi, const uint8_t* xrow,
+                                               int xgroup, bool kin1, const bool (&xok)[MG], float (&acc)[MG][4]) {
+  const uint32_t wr[4] = {w.x, w.y, w.z, w.w};
+  const uint32_t sh[4] = {sc.x & 0xFFFFu, sc.x >> 16, sc.y & 0xFFFFu, sc.y >> 16};
+  const uint32_t bh[4] = {bi.x & 0xFFFFu, bi.x >> 16, bi.y & 0xFFFFu, bi.y >> 16};
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    uint32_t ha[4], hb[4];
+    i4x8_to_h2x4_raw(wr[2 * blk + 0], ha);  // row g
+    i4x8_to_h2x4_raw(wr[2 * blk + 1], hb);  // row g + 8
+    h2x4_fma(ha, sh[2 * blk + 0], bh[2 * blk + 0]);
+    h2x4_fma(hb, sh[2 * blk + 1], bh[2 * blk + 1]);
+#pragma unroll
+    for (int mg = 0; mg < MG; ++mg) {
+      uint4 xv = make_uint4(0, 0, 0, 0);
+      if (xok[mg] && (blk == 0 || kin1))
+        xv = *reinterpret_cast<const uint4*>(xrow + mg * xgroup + blk * 64);
+      mma_16816(acc[mg], ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
+      mma_16816(acc[mg], ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
+    }
+  }
+}
+
 }  // namespace s4

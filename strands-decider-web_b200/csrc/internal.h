@@ -55,6 +55,7 @@ struct s4_weight {
   int N = 0, K = 0, nblk = 0, ktiles = 0;
   uint8_t* wq = nullptr;
   uint8_t* ws = nullptr;
+  uint8_t* wb = nullptr;  // asymmetric formats: per-32-block fp16 biases in the layout of ws
   size_t wq_bytes = 0, ws_bytes = 0;
 };
 

@@ -10,7 +10,8 @@
 //   ws:  512 bytes = [8 sub][8 g][4 halves] = scales of (g,blk0), (g+8,blk0), (g,blk1), (g+8,blk1)
 // A warp of the decode GEMV reads one sub-tile as one coalesced 512-byte line whose 16-byte lane
 // slices are exactly its mma.sync fragments; the tcgen05 GEMM reads whole 4 KB chunks with one
-// bulk copy. Rows >= N and K >= K are padded with nibble 8 (weight 0) and scale 0.
+// bulk copy. Rows >= N and K >= K are padded with nibble 8 (weight 0) and scale 0. With wq == nullptr
+// only the scale pass runs (the biases of an asymmetric format take the layout of the scales).
 #include "common.cuh"
 
 namespace s4 {
@@ -30,7 +31,7 @@ __device__ __forceinline__ uint32_t shuffle_nibbles(uint32_t w) {
 __global__ void repack_weights_kernel(const uint8_t* __restrict__ packed, const __half* __restrict__ scales,
                                       uint32_t* __restrict__ wq, __half* __restrict__ ws, int N, int K, int nblk,
                                       int ktiles) {
-  const int64_t words = (int64_t)nblk * ktiles * 1024;  // 4096 B per chunk
+  const int64_t words = wq ? (int64_t)nblk * ktiles * 1024 : 0;  // 4096 B per chunk; none for a bias-only pass
   const int blocks_per_row = K / 32;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
     const int j = (int)(i & 3);

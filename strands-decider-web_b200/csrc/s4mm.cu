@@ -20,9 +20,9 @@ using s4::DeviceGuard;
 namespace s4 {
 cudaError_t launch_repack(const uint8_t* packed, const __half* scales, uint32_t* wq, __half* ws, int N, int K,
                           int nblk, int ktiles, int sm_count, cudaStream_t stream);
-cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, uint32_t* err, int M, int N,
-                        int K, int nblk, int ktiles, int token0, int groups, int split, int sm_count,
-                        cudaStream_t stream, bool pdl);
+cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
+                        uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0, int groups, int split,
+                        int sm_count, cudaStream_t stream, bool pdl);
 int gemv_max_split();
 int gemv_max_tokens();
 cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
@@ -30,14 +30,16 @@ cudaError_t launch_silu_mul_gather(const __half* big, int M, int Is, __half* con
                                    int sm_count, cudaStream_t stream);
 cudaError_t launch_wire_scales(const uint8_t* wire, int N, int G, const double* pow_table, uint16_t* out, int sms,
                                cudaStream_t stream);
-cudaError_t launch_transcode_sym(const uint32_t* q, const __half* scales, int N, int K, int bits, int group,
-                                 uint8_t* packed4, __half* scales32, int sm_count, cudaStream_t stream);
+cudaError_t launch_transcode(const uint32_t* q, const __half* scales, const __half* bias, int N, int K, int bits,
+                             int group, uint8_t* packed4, __half* scales32, __half* bias32, int sm_count,
+                             cudaStream_t stream);
 cudaError_t launch_fwht(__half* a, int64_t blocks, int n, cudaStream_t stream);
 cudaError_t launch_add_rmsnorm(float* x, const __half* y, const float* w, int M, int D, float eps, __half* h,
                                cudaStream_t stream);
 cudaError_t launch_peer_barrier(uint32_t* const* flags, int nranks, int rank, uint32_t epoch, uint32_t* err,
                                 cudaStream_t stream);
-cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const __half* x, int64_t ldx, __half* const* ydst,
+cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, int64_t ldx,
+                              __half* const* ydst,
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
                               cudaStream_t stream, bool pdl, bool ticket_fixup);
@@ -48,9 +50,10 @@ void chain_destroy(s4_chain* c);
 int chain_info(const s4_chain* c, int* grid, int* slots, int* smem);
 bool tc_available();
 size_t tc_partials_bytes(int max_grid);
-cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const __half* x, __half* y, float* partials,
-                           uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K, int nblk,
-                           int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl, bool ticket_fixup);
+cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
+                           float* partials, uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K,
+                           int nblk, int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl,
+                           bool ticket_fixup);
 }  // namespace s4
 
 namespace {
@@ -223,7 +226,8 @@ bool parse_table(const char* text, std::vector<Bucket>& out, std::string& why) {
   return true;
 }
 
-int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, int N, int K, s4_weight** out) {
+int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, int N, int K, s4_weight** out,
+                  const void* bias_dev = nullptr) {
   s4_weight* w = new (std::nothrow) s4_weight();
   if (!w) return fail(S4_ERR_NOMEM, "out of host memory");
   w->ctx = ctx;
@@ -235,8 +239,10 @@ int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, i
   w->ws_bytes = (size_t)w->nblk * w->ktiles * s4::kChunkSBytes;
   cudaError_t e = cudaMalloc(&w->wq, w->wq_bytes);
   if (e == cudaSuccess) e = cudaMalloc(&w->ws, w->ws_bytes);
+  if (e == cudaSuccess && bias_dev) e = cudaMalloc(&w->wb, w->ws_bytes);
   if (e != cudaSuccess) {
     cudaFree(w->wq);
+    cudaFree(w->ws);
     delete w;
     return fail(S4_ERR_NOMEM, "weight allocation of %zu bytes failed: %s", w->wq_bytes + w->ws_bytes,
                 cudaGetErrorString(e));
@@ -244,6 +250,11 @@ int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, i
   e = s4::launch_repack(static_cast<const uint8_t*>(packed_dev), static_cast<const __half*>(scales_dev),
                         reinterpret_cast<uint32_t*>(w->wq), reinterpret_cast<__half*>(w->ws), N, K, w->nblk,
                         w->ktiles, ctx->sm_count, ctx->stream);
+  if (e == cudaSuccess && bias_dev) {
+    ++ctx->launches;
+    e = s4::launch_repack(nullptr, static_cast<const __half*>(bias_dev), nullptr, reinterpret_cast<__half*>(w->wb), N,
+                          K, w->nblk, w->ktiles, ctx->sm_count, ctx->stream);
+  }
   if (e == cudaSuccess) {
     ++ctx->launches;
     e = cudaStreamSynchronize(ctx->stream);
@@ -251,6 +262,7 @@ int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, i
   if (e != cudaSuccess) {
     cudaFree(w->wq);
     cudaFree(w->ws);
+    cudaFree(w->wb);
     delete w;
     return cuda_fail(e, "repack");
   }
@@ -452,33 +464,41 @@ int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, cons
   int rc = check_shape(N, K);
   if (rc) return rc;
   if (K % group) return fail(S4_ERR_INVALID, "K=%d is not a multiple of the group %d", K, group);
-  if (bias) return fail(S4_ERR_UNSUPPORTED, "asymmetric formats are not supported");
   const bool dev = flags & S4_UPLOAD_DEVICE;
-  if (bits == 4 && group == 32)
+  if (bits == 4 && group == 32 && !bias)
     return dev ? s4_weight_upload_device(ctx, q, scales, N, K, 0, out)
                : s4_weight_upload(ctx, static_cast<const uint8_t*>(q), static_cast<const uint16_t*>(scales), N, K, 0,
                                   out);
-  if (dev && ((reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(scales) & 1)))
-    return fail(S4_ERR_INVALID, "q must be 4-byte and scales 2-byte aligned");
+  if (dev && ((reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(scales) & 1) ||
+              (reinterpret_cast<uintptr_t>(bias) & 1)))
+    return fail(S4_ERR_INVALID, "q must be 4-byte and scales / bias 2-byte aligned");
   DeviceGuard guard(ctx->device);
   const size_t blocks = (size_t)N * (K / 32);
   const size_t qbytes = blocks * bits * 4, sbytes = (size_t)N * (K / group) * 2;
-  const size_t p4 = blocks * 16, s4b = blocks * 2;
-  const size_t in_bytes = dev ? 0 : qbytes + sbytes;
-  uint8_t* d = nullptr;  // [packed int4 | fp16 scales per 32 | (host input: q | scales)]
-  cudaError_t e = cudaMalloc(&d, p4 + s4b + in_bytes);
-  if (e != cudaSuccess) return fail(S4_ERR_NOMEM, "format staging of %zu bytes failed", p4 + s4b + in_bytes);
-  const void *dq = q, *dsc = scales;
+  const size_t p4 = blocks * 16, s32 = blocks * 2, b32 = bias ? s32 : 0;
+  const size_t in_bytes = dev ? 0 : qbytes + sbytes + (bias ? sbytes : 0);
+  const size_t total = p4 + s32 + b32 + in_bytes;
+  uint8_t* d = nullptr;  // [packed int4 | scales per 32 | biases per 32 | (host input: q | scales | bias)]
+  cudaError_t e = cudaMalloc(&d, total);
+  if (e != cudaSuccess) return fail(S4_ERR_NOMEM, "format staging of %zu bytes failed", total);
+  __half* ds32 = reinterpret_cast<__half*>(d + p4);
+  __half* db32 = bias ? reinterpret_cast<__half*>(d + p4 + s32) : nullptr;
+  const void *dq = q, *dsc = scales, *dbi = bias;
   if (!dev) {
-    dq = d + p4 + s4b;
-    dsc = d + p4 + s4b + qbytes;
+    uint8_t* in = d + p4 + s32 + b32;
+    dq = in;
+    dsc = in + qbytes;
+    dbi = bias ? in + qbytes + sbytes : nullptr;
     e = cudaMemcpyAsync(const_cast<void*>(dq), q, qbytes, cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess)
       e = cudaMemcpyAsync(const_cast<void*>(dsc), scales, sbytes, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess && bias)
+      e = cudaMemcpyAsync(const_cast<void*>(dbi), bias, sbytes, cudaMemcpyHostToDevice, ctx->stream);
   }
   if (e == cudaSuccess) {
-    e = s4::launch_transcode_sym(static_cast<const uint32_t*>(dq), static_cast<const __half*>(dsc), N, K, bits, group,
-                                 d, reinterpret_cast<__half*>(d + p4), ctx->sm_count, ctx->stream);
+    e = s4::launch_transcode(static_cast<const uint32_t*>(dq), static_cast<const __half*>(dsc),
+                             static_cast<const __half*>(dbi), N, K, bits, group, d, ds32, db32, ctx->sm_count,
+                             ctx->stream);
     if (e == cudaSuccess) ++ctx->launches;
   }
   if (e != cudaSuccess) {
@@ -486,7 +506,7 @@ int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, cons
     cudaFree(d);
     return cuda_fail(e, "format upload");
   }
-  rc = upload_common(ctx, d, d + p4, N, K, out);
+  rc = upload_common(ctx, d, ds32, N, K, out, db32);
   cudaFree(d);
   return rc;
 }
@@ -510,6 +530,7 @@ int s4_weight_free(s4_weight* w) {
   DeviceGuard guard(w->ctx->device);
   cudaFree(w->wq);
   cudaFree(w->ws);
+  cudaFree(w->wb);
   delete w;
   return S4_OK;
 }
@@ -518,7 +539,7 @@ int s4_weight_info(const s4_weight* w, int* N, int* K, size_t* device_bytes) {
   if (!w) return fail(S4_ERR_INVALID, "NULL weight");
   if (N) *N = w->N;
   if (K) *K = w->K;
-  if (device_bytes) *device_bytes = w->wq_bytes + w->ws_bytes;
+  if (device_bytes) *device_bytes = w->wq_bytes + w->ws_bytes + (w->wb ? w->ws_bytes : 0);
   return S4_OK;
 }
 
@@ -571,7 +592,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
     const int grid = b.split > 0 ? std::min(b.split, ctx->sm_count) : ctx->sm_count;
     for (long long r0 = 0; r0 < M; r0 += rows_cap) {
       const int rows = (int)std::min<long long>(rows_cap, M - r0);
-      e = s4::launch_tc_gemm(w->wq, w->ws, static_cast<const __half*>(x) + r0 * w->K,
+      e = s4::launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x) + r0 * w->K,
                              static_cast<__half*>(y) + r0 * w->N, ctx->partials, ctx->tickets, kMaxTickets, ctx->err,
                              rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl, false);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
@@ -582,7 +603,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
   for (int tok0 = 0; tok0 < M; tok0 += kGemvMaxM) {
     const int rem = M - tok0;
     const int groups = rem >= kGemvMaxM ? kGemvMaxM / 8 : (rem + 7) / 8;
-    e = s4::launch_gemv(w->wq, w->ws, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->err, M, w->N,
+    e = s4::launch_gemv(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->err, M, w->N,
                         w->K, w->nblk, w->ktiles, tok0, groups, b.split, ctx->sm_count, st, ctx->pdl);
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     ++ctx->launches;
@@ -778,7 +799,7 @@ int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, in
   DeviceGuard guard(ctx->device);
   const int tn = auto_tile(M, w, ctx->sm_count);
   if ((long long)((M + tn - 1) / tn) * w->nblk > kMaxTickets) return fail(S4_ERR_INVALID, "M too large for one launch");
-  cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, static_cast<const __half*>(x), ldx,
+  cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, w->wb, static_cast<const __half*>(x), ldx,
                                         reinterpret_cast<__half* const*>(dst), ndst, ldy, col0, ctx->partials,
                                         ctx->tickets, kMaxTickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tn,
                                         ctx->sm_count, static_cast<cudaStream_t>(stream), ctx->pdl, false);

@@ -1,7 +1,8 @@
-"""The engine's non-default weight formats (kernels.js:5-12: 2/3/4 bits, group 32/64, symmetric)
-uploaded through s4_weight_upload_format: the device layout is byte-identical to an upload of the
-oracle's exact int4 rewrite, and matmuls through them (GEMV, chained and tcgen05 families) meet the
-north-star tolerance against the oracle's fp32 dequantise-then-matmul of the original format. The
+"""The engine's non-default weight formats (kernels.js:5-12: 2/3/4 bits, group 32/64, symmetric and
+asymmetric) uploaded through s4_weight_upload_format: a symmetric one's device layout is
+byte-identical to an upload of the oracle's exact int4 rewrite, and matmuls through them (GEMV,
+chained and tcgen05 families; asymmetric ones without the chain) meet the north-star tolerance
+against the oracle's fp32 dequantise-then-matmul of the original format. The
 online Hadamard rotation (s4_fwht, wgsl.js:94-110) is checked bit for bit against the oracle."""
 import numpy as np
 import pytest
@@ -61,15 +62,70 @@ def test_format_upload_from_device_and_chain(ctx):
 
 
 def test_format_errors(ctx, pkg):
-    words = np.zeros((4, 2, 2), dtype=np.uint32)
-    sc = np.zeros((4, 2), dtype=np.float16)
     for bits, group, K in ((5, 32, 64), (2, 128, 64), (2, 64, 96)):
         with pytest.raises(pkg.S4Error):
             ctx.upload_format(np.zeros(4 * (K // 32) * max(bits, 2), np.uint32), np.zeros(4 * (K // group), np.float16)
                               if K % group == 0 else np.zeros(8, np.float16), 4, K, bits, group)
-    with pytest.raises(pkg.S4Error) as e:  # asymmetric: not built yet, reported as unsupported
-        ctx.upload_format(words, sc, 4, 64, 2, 32, bias=sc)
+
+
+def _asym_weight(rng, K, N, bits, group):
+    """Min-max style asymmetric weights: scale = range / (2^bits - 1), bias near -range / 2."""
+    words = s4ref.pack_format(rng.integers(0, 2 ** bits, (N, K)), bits)
+    sc = (np.abs(rng.standard_normal((N, K // group))) * 0.04 / (2 ** bits - 1)).astype(np.float16)
+    bi = (-(2 ** bits - 1) / 2 * sc.astype(np.float32) * (1 + 0.2 * rng.standard_normal(sc.shape))).astype(np.float16)
+    return words, sc, bi
+
+
+ASYM = [(4, 32), (2, 32), (3, 64), (4, 64)]
+
+
+@pytest.mark.parametrize("bits,group", ASYM)
+def test_asym_matmul(ctx, pkg, bits, group):
+    """w = q * scale + bias (kernels.js:11, 36) through the GEMV (1 and 2 token groups) and tcgen05
+    families, and the allocation-free entry point."""
+    K, N = 2048, 1280
+    rng = np.random.default_rng(100 + bits * 10 + group)
+    words, sc, bi = _asym_weight(rng, K, N, bits, group)
+    W = ctx.upload_format(words, sc, N, K, bits, group, bias=bi)
+    deq = s4ref.dequant_format(words, sc, bits, group, bi)
+    wq, ws = W.layout()
+    packed = s4ref.pack_nibbles(s4ref.unpack_format(words, bits).reshape(N, K // 32, 32).astype(np.uint8))
+    ref_wq, ref_ws = s4ref.repack_device(packed, np.repeat(sc, group // 32, 1), N, K)
+    np.testing.assert_array_equal(wq, ref_wq.ravel())  # nibbles kept uncentered
+    np.testing.assert_array_equal(ws.view(np.uint16), ref_ws.ravel().view(np.uint16))
+    for M in (1, 9, 16, 300):
+        x = s4ref.config_x(rng, M, K)
+        xd = torch.from_numpy(x).cuda()
+        y = ctx.matmul(xd, W)
+        torch.cuda.synchronize()
+        ref = x.astype(np.float32) @ deq.T
+        ok, mr, mc = s4ref.check(y.cpu().numpy(), ref)
+        assert ok, f"bits={bits} group={group} M={M}: max_rel={mr:.2e} min_cos={mc:.7f}"
+    y2 = torch.full((300, N), float("nan"), dtype=torch.float16, device="cuda")
+    lib = pkg.load_library()
+    assert lib.s4_matmul_noalloc(W.handle, xd.data_ptr(), 300, y2.data_ptr(), None) == 0, lib.s4_last_error().decode()
+    torch.cuda.synchronize()
+    ok, mr, mc = s4ref.check(y2.cpu().numpy(), ref)
+    assert ok, f"noalloc: max_rel={mr:.2e} min_cos={mc:.7f}"
+    W.free()
+
+
+def test_asym_from_device_and_chain_rejects(ctx, pkg):
+    K, N = 1024, 384
+    rng = np.random.default_rng(7)
+    words, sc, bi = _asym_weight(rng, K, N, 2, 64)
+    W = ctx.upload_format(torch.from_numpy(words.view(np.int32)).cuda(), torch.from_numpy(sc).cuda(), N, K, 2, 64,
+                          bias=torch.from_numpy(bi).cuda())
+    x = torch.from_numpy(s4ref.config_x(rng, 3, K)).cuda()
+    y = ctx.matmul(x, W)
+    torch.cuda.synchronize()
+    ok, mr, mc = s4ref.check(y.cpu().numpy(), x.cpu().numpy().astype(np.float32)
+                             @ s4ref.dequant_format(words, sc, 2, 64, bi).T)
+    assert ok, f"max_rel={mr:.2e} min_cos={mc:.7f}"
+    with pytest.raises(pkg.S4Error) as e:
+        ctx.chain([(x, W, torch.empty((3, N), dtype=torch.float16, device="cuda"))])
     assert e.value.code == pkg.s4mm.ERR_UNSUPPORTED
+    W.free()
 
 
 @pytest.mark.parametrize("n,M,K", [(2, 3, 64), (64, 5, 2048), (256, 17, 6144), (4096, 2, 8192), (32768, 1, 32768)])
