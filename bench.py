@@ -677,6 +677,96 @@ def run_stack(args, rank, world, local_rank):
     return 0
 
 
+# formats: the non-default weight formats, the online FWHT and the wire scale decode, measured
+FORMATS = [(4, 32, False), (2, 32, False), (3, 32, False), (4, 64, False), (2, 64, True), (4, 32, True),
+           (3, 64, True)]
+
+
+def format_bytes(K, N, bits, group, asym):
+    """Bytes of one weight in its own format (q words + fp16 scales [+ fp16 biases])."""
+    return N * K * bits // 8 + (N * K // group) * 2 * (2 if asym else 1)
+
+
+def run_formats(args, rank, world, local_rank):
+    """Decode (M = 1, GEMV) and prefill (M = 2048, tcgen05) matmuls of the gate|up shape for every
+    weight format, the FWHT of a 2048 x 2048 activation in 256-blocks, and the device decode of
+    wire-format scales for that weight. Weights rotate over 16 copies (> L2) for the decode calls."""
+    import numpy as np
+    import torch
+    from oracle import s4ref
+
+    if world > 1:
+        print(json.dumps({"workload": "formats", "skipped": "single-GPU measurement"}) if rank == 0 else "")
+        return 0
+    torch.cuda.set_device(local_rank)
+    pkg = load_pkg()
+    ctx = pkg.Context(local_rank)
+    hbm, tc_peak, peak_kind = peaks()
+    stream = torch.cuda.current_stream()
+    K, N = 2048, 12288
+    rng = np.random.default_rng(5)
+    copies = 16
+
+    def timed(fn, reps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps  # us per call
+
+    rows = []
+    x1 = torch.from_numpy(s4ref.config_x(rng, 1, K)).cuda()
+    xp = torch.from_numpy(s4ref.config_x(rng, 2048, K)).cuda()
+    y1 = torch.empty((1, N), dtype=torch.float16, device="cuda")
+    yp = torch.empty((2048, N), dtype=torch.float16, device="cuda")
+    with ClockSampler(local_rank) as clk:
+        for bits, group, asym in FORMATS:
+            words = s4ref.pack_format(rng.integers(0, 2 ** bits, (N, K)), bits)
+            sc = (np.abs(rng.standard_normal((N, K // group))) * 0.02 / 2 ** (bits - 1)).astype(np.float16)
+            bi = (-(2 ** bits - 1) / 2 * sc).astype(np.float16) if asym else None
+            Ws = [ctx.upload_format(words, sc, N, K, bits, group, bias=bi) for _ in range(copies)]
+            it = {"i": 0}
+
+            def dec():
+                ctx.matmul(x1, Ws[it["i"] % copies], y=y1, stream=stream)
+                it["i"] += 1
+
+            us_dec = timed(dec, 20 * copies)
+            us_pre = timed(lambda: ctx.matmul(xp, Ws[0], y=yp, stream=stream), 20)
+            fb = format_bytes(K, N, bits, group, asym)
+            rows.append({"format": f"{bits}b g{group} {'asym' if asym else 'sym'}",
+                         "decode_us": round(us_dec, 2),
+                         "decode_format_GBps": round((fb + 2 * K + 2 * N) / us_dec / 1e3, 1),
+                         "decode_device_GBps": round((Ws[0].device_bytes + 2 * K + 2 * N) / us_dec / 1e3, 1),
+                         "prefill_us": round(us_pre, 1),
+                         "prefill_TFLOPs": round(2.0 * 2048 * K * N / us_pre / 1e6, 1)})
+            for W in Ws:
+                W.free()
+        a = torch.from_numpy(s4ref.config_x(rng, 2048, 2048)).cuda()
+        us_fwht = timed(lambda: ctx.fwht(a, 256, stream=stream), 50)
+        G = K // 32
+        wire = torch.frombuffer(bytearray(s4ref.encode_wire_scales(
+            (rng.standard_normal((N, G)) * 0.01).astype(np.float16))), dtype=torch.uint8).cuda()
+        out = torch.empty((N, G), dtype=torch.float16, device="cuda")
+        us_wire = timed(lambda: ctx.decode_wire_scales(wire, N, G, out=out, stream=stream), 50)
+    line = {"workload": "formats", "shape": {"K": K, "N": N, "decode_M": 1, "prefill_M": 2048},
+            "weight_copies": copies, "rows": rows,
+            "fwht": {"M": 2048, "K": 2048, "n": 256, "us": round(us_fwht, 2),
+                     "GBps": round(2 * 2 * 2048 * 2048 / us_fwht / 1e3, 1)},
+            "wire_decode": {"N": N, "G": G, "us": round(us_wire, 2),
+                            "GBps": round((4 * N + 3 * N * G) / us_wire / 1e3, 1)},
+            "peaks": {"hbm_GBps": hbm, "bf16_TFLOPs": tc_peak, "kind": peak_kind},
+            "clocks": clk.summary()}
+    print(json.dumps(line))
+    ctx.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -688,10 +778,11 @@ def main():
     ap.add_argument("--quick", action="store_true", help="skip the per-call breakdown")
     ap.add_argument("--family", choices=["auto", "gemv", "tc"], default="auto",
                     help="pin the kernel family instead of the dispatch table")
-    ap.add_argument("--workload", choices=["decode", "stack", "serve"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "stack", "serve", "formats"], default="decode",
                     help="decode: configs[1] GEMV sweep (default); stack: config 4, one 2048-token prompt "
                          "through the 24-layer linear stack, column-sharded over the ranks; serve: config 5, "
-                         "requests sharded over the ranks (weights replicated)")
+                         "requests sharded over the ranks (weights replicated); formats: the non-default weight "
+                         "formats, FWHT and wire scale decode (one GPU)")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="stack: fuse the all-gathers into the producing kernels (peer stores over NVLink) or "
                          "call NCCL all-gather after every projection")
@@ -711,6 +802,8 @@ def main():
         return run_reference(args, rank, world)
     if args.workload in ("stack", "serve"):
         return run_stack(args, rank, world, local_rank)
+    if args.workload == "formats":
+        return run_formats(args, rank, world, local_rank)
     return run_ours(args, rank, world, local_rank)
 
 

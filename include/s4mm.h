@@ -37,6 +37,7 @@ extern "C" {
 #define S4_ERR_NOMEM 3        /* device or pinned memory allocation failed */
 #define S4_ERR_DEVICE 4       /* a kernel reported an error (bounded wait expired) */
 #define S4_ERR_UNSUPPORTED 5  /* no sm_100 device, or shape outside what a kernel handles */
+#define S4_ERR_IO 6           /* a cache file is missing, unreadable, or not a weight of this layout */
 
 /* Kernel families of the dispatcher (s4_force / s4_plan). */
 #define S4_FAMILY_AUTO 0
@@ -102,6 +103,16 @@ S4_API int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scale
                                    int bits, int group, uint32_t flags, s4_weight** out);
 
 S4_API int s4_weight_free(s4_weight* w);
+
+/* On-disk cache of repacked weights (the role of the worker's OPFS asset cache, worker.js:27-44,
+ * 82-100, here holding the device layout so a later load skips decode and repack). A file is a
+ * 64-byte header (magic "S4WL", layout version, N, K, asymmetric flag, section sizes, a 64-bit
+ * checksum of the payload) followed by the device layout. Entries are keyed by the caller's file
+ * name (the host side builds names with the worker's fingerprint prefix). Synchronous.
+ * s4_weight_load returns S4_ERR_IO for a missing, truncated or corrupt file, or one written by a
+ * different layout version; the caller then uploads from the shard and saves again. */
+S4_API int s4_weight_save(const s4_weight* w, const char* path);
+S4_API int s4_weight_load(s4_ctx* ctx, const char* path, s4_weight** out);
 
 /* Shape and device footprint of an uploaded weight. */
 S4_API int s4_weight_info(const s4_weight* w, int* N, int* K, size_t* device_bytes);

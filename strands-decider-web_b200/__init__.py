@@ -9,7 +9,7 @@ Public API: :class:`Context`, :class:`Weight`, :class:`Chain`, :class:`Gemm`, :c
 (:mod:`.stack`) and the multi-GPU drivers (:mod:`.serve`).
 """
 from .s4mm import (FAMILY_AUTO, FAMILY_GEMV, FAMILY_TC, LIB_PATH, Chain, Context, Gemm, S4Error, Weight,  # noqa: F401
-                   load_library)
+                   WeightCache, cache_prefix, fnv1a32, load_library)
 
 
 def build(verbose: bool = False) -> str:

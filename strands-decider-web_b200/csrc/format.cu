@@ -15,7 +15,8 @@
 // FWHT (wgsl.js:94-110, engine.js:238): each contiguous n-block of the activations is replaced by
 // its orthonormal Walsh-Hadamard transform, in place, in fp32: stages h = 1, 2, 4, ... < n turn the
 // pair (i, i+h), i = (p / h) 2h + p % h, into (x + y, x - y); the result times 1/sqrt(n) (as a
-// float) is rounded to fp16. The same operations in the same order as the reference's shader.
+// float) is rounded to fp16. The same operations in the same order as the reference's shader. Blocks
+// of 32..1024 elements take one warp each (registers and shuffles); others one CTA (shared memory).
 #include "common.cuh"
 
 namespace s4 {
@@ -81,13 +82,102 @@ __global__ void fwht_kernel(__half* __restrict__ a, int n, float c) {
   for (int e = threadIdx.x; e < n; e += blockDim.x) a[o + e] = __float2half_rn(__fmul_rn(fw_sh[e], c));
 }
 
+// n = 32 E (E = 1 .. 32): one warp per block, lane l holding elements [l E, l E + E) in registers.
+// Stages h < E pair registers of one lane; stages h >= E pair lane l with lane l ^ (h / E), the
+// lower lane keeping x + y and the upper x - y (its own value is y): the same operations on the
+// same operands as the shared-memory form, so the same bits.
+template <int E>
+__global__ void fwht_warp_kernel(__half* __restrict__ a, int64_t blocks, float c) {
+  const int lane = threadIdx.x & 31;
+  const int64_t blk = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_wait();
+  if (blk >= blocks) return;
+  __half* p = a + blk * (32 * E) + lane * E;
+  float v[E];
+  if constexpr (E >= 8) {
+#pragma unroll
+    for (int q = 0; q < E / 8; ++q) {
+      const uint4 u = reinterpret_cast<const uint4*>(p)[q];
+      const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h2[j]);
+        v[8 * q + 2 * j] = f.x;
+        v[8 * q + 2 * j + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = __half2float(p[e]);
+  }
+#pragma unroll
+  for (int h = 1; h < E; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < E; ++i)
+      if ((i & h) == 0) {
+        const float x = v[i], y = v[i + h];
+        v[i] = __fadd_rn(x, y);
+        v[i + h] = __fsub_rn(x, y);
+      }
+  }
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const bool upper = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
+      v[i] = upper ? __fsub_rn(o, v[i]) : __fadd_rn(v[i], o);
+    }
+  }
+  pdl_launch_dependents();
+  if constexpr (E >= 8) {
+#pragma unroll
+    for (int q = 0; q < E / 8; ++q) {
+      uint4 u;
+      __half2* h2 = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        h2[j] = __floats2half2_rn(__fmul_rn(v[8 * q + 2 * j], c), __fmul_rn(v[8 * q + 2 * j + 1], c));
+      reinterpret_cast<uint4*>(p)[q] = u;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) p[e] = __float2half_rn(__fmul_rn(v[e], c));
+  }
+}
+
+template <int E>
+static cudaError_t launch_fwht_warp(__half* a, int64_t blocks, float c, cudaStream_t stream) {
+  const int warps = 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((blocks + warps - 1) / warps), 1, 1);
+  cfg.blockDim = dim3(32 * warps, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fwht_warp_kernel<E>, a, blocks, c);
+}
+
 cudaError_t launch_fwht(__half* a, int64_t blocks, int n, cudaStream_t stream) {
+  const float c = (float)(1.0 / sqrt((double)n));
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(a) & 15) == 0;
+  switch (n) {
+    case 32: return launch_fwht_warp<1>(a, blocks, c, stream);
+    case 64: return launch_fwht_warp<2>(a, blocks, c, stream);
+    case 128: return launch_fwht_warp<4>(a, blocks, c, stream);
+    case 256: if (aligned16) return launch_fwht_warp<8>(a, blocks, c, stream); break;
+    case 512: if (aligned16) return launch_fwht_warp<16>(a, blocks, c, stream); break;
+    case 1024: if (aligned16) return launch_fwht_warp<32>(a, blocks, c, stream); break;
+    default: break;
+  }
   const size_t smem = (size_t)n * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(fwht_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  const float c = (float)(1.0 / sqrt((double)n));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)blocks, 1, 1);
   cfg.blockDim = dim3(n / 2 < 256 ? (n / 2 < 32 ? 32 : n / 2) : 256, 1, 1);

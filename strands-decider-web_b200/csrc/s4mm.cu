@@ -560,6 +560,133 @@ int s4_weight_download_layout(const s4_weight* w, void* wq_host, size_t wq_bytes
   return S4_OK;
 }
 
+// ---- on-disk cache of repacked weights ----
+namespace {
+constexpr uint32_t kCacheMagic = 0x4c573453u;  // "S4WL"
+constexpr uint32_t kCacheLayoutVersion = 1;    // the device layout of repack.cu; bump when it changes
+struct CacheHeader {
+  uint32_t magic, version;
+  int32_t N, K;
+  uint32_t flags;  // bit 0: asymmetric (a bias section follows the scales)
+  uint32_t reserved0;
+  uint64_t wq_bytes, ws_bytes, wb_bytes;
+  uint64_t checksum;  // of the payload, cache_checksum()
+  uint64_t reserved1;
+};
+static_assert(sizeof(CacheHeader) == 64, "cache header is 64 bytes");
+
+// FNV-1a style over 8-byte little-endian words with an extra xor-shift per word (multi-byte words
+// need the high bits folded back); detects truncation and corruption, not tampering.
+uint64_t cache_checksum(const uint8_t* p, size_t n, uint64_t h) {
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8) {
+    uint64_t w;
+    memcpy(&w, p + i, 8);
+    h = (h ^ w) * 0x100000001b3ull;
+    h ^= h >> 29;
+  }
+  uint64_t w = 0;
+  memcpy(&w, p + i, n - i);
+  h = (h ^ w ^ (uint64_t)n) * 0x100000001b3ull;
+  return h ^ (h >> 29);
+}
+}  // namespace
+
+int s4_weight_save(const s4_weight* w, const char* path) {
+  if (!w || !path) return fail(S4_ERR_INVALID, "NULL argument");
+  const size_t wb_bytes = w->wb ? w->ws_bytes : 0;
+  std::vector<uint8_t> buf(w->wq_bytes + w->ws_bytes + wb_bytes);
+  {
+    DeviceGuard guard(w->ctx->device);
+    cudaError_t e = cudaMemcpy(buf.data(), w->wq, w->wq_bytes, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(buf.data() + w->wq_bytes, w->ws, w->ws_bytes, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && w->wb)
+      e = cudaMemcpy(buf.data() + w->wq_bytes + w->ws_bytes, w->wb, wb_bytes, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "weight download for the cache");
+  }
+  CacheHeader h = {};
+  h.magic = kCacheMagic;
+  h.version = kCacheLayoutVersion;
+  h.N = w->N;
+  h.K = w->K;
+  h.flags = w->wb ? 1u : 0u;
+  h.wq_bytes = w->wq_bytes;
+  h.ws_bytes = w->ws_bytes;
+  h.wb_bytes = wb_bytes;
+  h.checksum = cache_checksum(buf.data(), buf.size(), 0xcbf29ce484222325ull);
+  const std::string tmp = std::string(path) + ".tmp";  // written whole, then renamed over the entry
+  FILE* f = fopen(tmp.c_str(), "wb");
+  if (!f) return fail(S4_ERR_IO, "cannot create %s", tmp.c_str());
+  const bool ok = fwrite(&h, sizeof h, 1, f) == 1 && fwrite(buf.data(), 1, buf.size(), f) == buf.size();
+  const bool closed = fclose(f) == 0;
+  if (!ok || !closed || rename(tmp.c_str(), path) != 0) {
+    remove(tmp.c_str());
+    return fail(S4_ERR_IO, "writing %s failed", path);
+  }
+  return S4_OK;
+}
+
+int s4_weight_load(s4_ctx* ctx, const char* path, s4_weight** out) {
+  if (!ctx || !path || !out) return fail(S4_ERR_INVALID, "NULL argument");
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(S4_ERR_IO, "no cache entry %s", path);
+  CacheHeader h;
+  if (fread(&h, sizeof h, 1, f) != 1) {
+    fclose(f);
+    return fail(S4_ERR_IO, "%s: truncated header", path);
+  }
+  if (h.magic != kCacheMagic || h.version != kCacheLayoutVersion || (h.flags & ~1u)) {
+    fclose(f);
+    return fail(S4_ERR_IO, "%s: not a weight of layout version %u", path, kCacheLayoutVersion);
+  }
+  if (check_shape(h.N, h.K) != S4_OK) {
+    fclose(f);
+    return fail(S4_ERR_IO, "%s: bad shape N=%d K=%d", path, h.N, h.K);
+  }
+  s4_weight* w = new (std::nothrow) s4_weight();
+  if (!w) {
+    fclose(f);
+    return fail(S4_ERR_NOMEM, "out of host memory");
+  }
+  w->ctx = ctx;
+  w->N = h.N;
+  w->K = h.K;
+  w->nblk = (h.N + s4::kRowsPerBlock - 1) / s4::kRowsPerBlock;
+  w->ktiles = (h.K + s4::kKPerTile - 1) / s4::kKPerTile;
+  w->wq_bytes = (size_t)w->nblk * w->ktiles * s4::kChunkWBytes;
+  w->ws_bytes = (size_t)w->nblk * w->ktiles * s4::kChunkSBytes;
+  const size_t wb_bytes = (h.flags & 1u) ? w->ws_bytes : 0;
+  if (h.wq_bytes != w->wq_bytes || h.ws_bytes != w->ws_bytes || h.wb_bytes != wb_bytes) {
+    fclose(f);
+    delete w;
+    return fail(S4_ERR_IO, "%s: section sizes do not match N=%d K=%d", path, h.N, h.K);
+  }
+  std::vector<uint8_t> buf(w->wq_bytes + w->ws_bytes + wb_bytes);
+  const bool read_ok = fread(buf.data(), 1, buf.size(), f) == buf.size() && fgetc(f) == EOF;
+  fclose(f);
+  if (!read_ok || cache_checksum(buf.data(), buf.size(), 0xcbf29ce484222325ull) != h.checksum) {
+    delete w;
+    return fail(S4_ERR_IO, "%s: truncated or corrupt payload", path);
+  }
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaMalloc(&w->wq, w->wq_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&w->ws, w->ws_bytes);
+  if (e == cudaSuccess && wb_bytes) e = cudaMalloc(&w->wb, wb_bytes);
+  if (e == cudaSuccess) e = cudaMemcpy(w->wq, buf.data(), w->wq_bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(w->ws, buf.data() + w->wq_bytes, w->ws_bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && wb_bytes)
+    e = cudaMemcpy(w->wb, buf.data() + w->wq_bytes + w->ws_bytes, wb_bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(w->wq);
+    cudaFree(w->ws);
+    cudaFree(w->wb);
+    delete w;
+    return cuda_fail(e, "cache load");
+  }
+  *out = w;
+  return S4_OK;
+}
+
 // Tokens per tcgen05 tile when the table does not fix it: 256 (M rounded up to 16 below that);
 // 128 when K is short (<= 4096) and 256-token tiles would fill under 3/4 of the SMs while 128-token
 // tiles still fit in one wave (measured: out_proj M = 256..1024, in_proj M = 256 faster by 20-25%;

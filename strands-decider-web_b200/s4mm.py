@@ -27,7 +27,7 @@ LIB_PATH = os.path.join(HERE, "libs4mm.so")
 
 FAMILY_AUTO, FAMILY_GEMV, FAMILY_TC = 0, 1, 2
 FAMILY_NAMES = {FAMILY_AUTO: "auto", FAMILY_GEMV: "gemv", FAMILY_TC: "tc"}
-ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_DEVICE, ERR_UNSUPPORTED = 1, 2, 3, 4, 5
+ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_DEVICE, ERR_UNSUPPORTED, ERR_IO = 1, 2, 3, 4, 5, 6
 UPLOAD_DEVICE = 1  # s4_weight_upload_format: pointers are device memory
 
 # Every symbol include/s4mm.h declares, with its ctypes signature.
@@ -45,6 +45,8 @@ _SIGS = {
                                           C.POINTER(_P)]),
     "s4_fwht": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, _P]),
     "s4_weight_free": (C.c_int, [_P]),
+    "s4_weight_save": (C.c_int, [_P, C.c_char_p]),
+    "s4_weight_load": (C.c_int, [_P, C.c_char_p, C.POINTER(_P)]),
     "s4_weight_info": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_size_t)]),
     "s4_weight_layout_bytes": (C.c_int, [_P, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "s4_weight_download_layout": (C.c_int, [_P, _P, C.c_size_t, _P, C.c_size_t]),
@@ -181,6 +183,10 @@ class Weight:
         _check(_lib.s4_weight_info(self.handle, C.byref(n), C.byref(k), C.byref(b)))
         return b.value
 
+    def save(self, path: str):
+        """Write the repacked device layout to a cache file (``s4_weight_save``)."""
+        _check(_lib.s4_weight_save(self.handle, os.fsencode(path)))
+
     def layout(self):
         """Download the device layout: ``(wq uint32, ws float16)`` flat arrays."""
         qb, sb = C.c_size_t(), C.c_size_t()
@@ -272,6 +278,15 @@ class Context:
         M, K = (a.shape[0], a.shape[1]) if a.dim() == 2 else (1, a.numel())
         _check(_lib.s4_fwht(self.handle, a.data_ptr(), int(M), int(K), int(n), _stream_handle(stream)))
         return a
+
+    def load_weight(self, path: str) -> Weight:
+        """A weight from a cache file written by :meth:`Weight.save` (``s4_weight_load``); raises
+        S4Error with code ERR_IO when the entry is missing, corrupt or of another layout version."""
+        h = _P()
+        _check(_lib.s4_weight_load(self.handle, os.fsencode(path), C.byref(h)))
+        n, k = C.c_int(), C.c_int()
+        _check(_lib.s4_weight_info(h.value, C.byref(n), C.byref(k), None))
+        return Weight(self, h.value, n.value, k.value)
 
     def decode_wire_scales(self, wire_dev, N: int, G: int, out=None, stream=None):
         """Decode a device-resident wire scale tensor (uint8 CUDA tensor of 4*N + N*G bytes) to fp16
@@ -482,3 +497,61 @@ class Gemm:
         import torch
         torch.cuda.synchronize(self._dev)
         return self.Y.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+
+
+# ------------------------------------------------------------------------------------------------
+# On-disk weight cache keyed like the reference worker's asset cache (web/public/js/worker.js:27-44,
+# 82-88, 100): entry names carry the prefix ``<rev>__<fnv(base + config + manifest)>__`` so new
+# weights get fresh entries even at the same location, and entries under any other prefix are
+# removed after a load. Entries hold the repacked device layout (``s4_weight_save``).
+# ------------------------------------------------------------------------------------------------
+def fnv1a32(text: str) -> str:
+    """The worker's ``fnv`` (worker.js:31): FNV-1a 32, one step per code point on its first UTF-16
+    unit (``for (const c of s) ... c.charCodeAt(0)``: the high surrogate of a non-BMP character), 8 hex
+    digits."""
+    h = 0x811C9DC5
+    for ch in text:
+        cp = ord(ch)
+        unit = cp if cp < 0x10000 else 0xD800 + ((cp - 0x10000) >> 10)
+        h = ((h ^ unit) * 0x01000193) & 0xFFFFFFFF
+    return f"{h:08x}"
+
+
+def cache_prefix(rev: str, base: str, config_text: str, manifest_text: str) -> str:
+    """``cachePrefix`` of worker.js:100."""
+    return f"{rev}__{fnv1a32(base + config_text + manifest_text)}__"
+
+
+class WeightCache:
+    """Repacked weights on disk under one fingerprint prefix."""
+
+    SUFFIX = ".s4w"
+
+    def __init__(self, directory: str, prefix: str):
+        self.dir = directory
+        self.prefix = prefix
+        os.makedirs(directory, exist_ok=True)
+
+    def path(self, name: str) -> str:
+        return os.path.join(self.dir, self.prefix + name.replace("/", "_") + self.SUFFIX)
+
+    def get(self, ctx: "Context", name: str, upload):
+        """The cached weight ``name``, or ``upload()``'s result saved for the next load.
+        Returns ``(weight, hit)``."""
+        try:
+            return ctx.load_weight(self.path(name)), True
+        except S4Error as e:
+            if e.code != ERR_IO:
+                raise
+        w = upload()
+        w.save(self.path(name))
+        return w, False
+
+    def prune(self) -> int:
+        """Remove entries under any other prefix (``pruneCache``, worker.js:82-88). Returns the count."""
+        n = 0
+        for f in os.listdir(self.dir):
+            if f.endswith(self.SUFFIX) and not f.startswith(self.prefix):
+                os.remove(os.path.join(self.dir, f))
+                n += 1
+        return n

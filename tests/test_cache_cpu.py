@@ -1,0 +1,42 @@
+"""Host side of the on-disk weight cache: the fingerprint prefix is the worker's (FNV-1a 32 over
+UTF-16 code units, worker.js:31, 100) and pruning keeps only the current prefix (worker.js:82-88)."""
+import os
+
+from conftest import load_package
+
+
+def _js_fnv(s):
+    """worker.js:31 as written: for (const c of s) iterates code points, c.charCodeAt(0) is the first
+    UTF-16 unit of each; Math.imul keeps the low 32 bits."""
+    h = 0x811C9DC5
+    for ch in s:
+        unit = ord(ch) if ord(ch) < 0x10000 else 0xD800 + ((ord(ch) - 0x10000) >> 10)
+        h = ((h ^ unit) * 0x01000193) & 0xFFFFFFFF
+    return f"{h:08x}"
+
+
+def test_fnv_known_values():
+    pkg = load_package()
+    assert pkg.fnv1a32("") == "811c9dc5"
+    assert pkg.fnv1a32("a") == "e40c292c"          # FNV-1a 32 test vector
+    assert pkg.fnv1a32("foobar") == "bf9cf968"     # FNV-1a 32 test vector
+
+
+def test_fnv_matches_worker_loop():
+    pkg = load_package()
+    for s in ("https://cdn.example/assets/", '{"layer_types": ["linear_attention"]}', "héllo wörld", "emoji \U0001F600!"):
+        assert pkg.fnv1a32(s) == _js_fnv(s)
+
+
+def test_prefix_and_prune(tmp_path):
+    pkg = load_package()
+    pre = pkg.cache_prefix("v19-test", "https://a/", "{}", '{"shards": []}')
+    assert pre.startswith("v19-test__") and pre.endswith("__") and len(pre) == len("v19-test__") + 8 + 2
+    old = pkg.cache_prefix("v19-test", "https://a/", "{}", '{"shards": [1]}')
+    assert old != pre
+    cache = pkg.WeightCache(str(tmp_path), pre)
+    for name in (pre + "a.s4w", old + "a.s4w", old + "b.s4w", "other.txt"):
+        (tmp_path / name).write_bytes(b"x")
+    assert cache.prune() == 2
+    assert sorted(os.listdir(tmp_path)) == sorted([pre + "a.s4w", "other.txt"])
+    assert cache.path("layers.0/mlp.q") == os.path.join(str(tmp_path), pre + "layers.0_mlp.q.s4w")

@@ -128,7 +128,9 @@ def test_asym_from_device_and_chain_rejects(ctx, pkg):
     W.free()
 
 
-@pytest.mark.parametrize("n,M,K", [(2, 3, 64), (64, 5, 2048), (256, 17, 6144), (4096, 2, 8192), (32768, 1, 32768)])
+# warp-per-block sizes (32..1024) and shared-memory sizes (2, 4096, 32768)
+@pytest.mark.parametrize("n,M,K", [(2, 3, 64), (32, 4, 96), (64, 5, 2048), (128, 3, 384), (256, 17, 6144),
+                                   (512, 2, 1024), (1024, 3, 2048), (4096, 2, 8192), (32768, 1, 32768)])
 def test_fwht_bit_exact(ctx, n, M, K):
     rng = np.random.default_rng(n + M)
     a = rng.standard_normal((M, K)).astype(np.float16)
@@ -136,6 +138,18 @@ def test_fwht_bit_exact(ctx, n, M, K):
     ctx.fwht(d, n)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(d.cpu().numpy().view(np.uint16), s4ref.fwht(a, n).view(np.uint16))
+
+
+def test_fwht_unaligned_rows(ctx):
+    """A 2-byte aligned (not 16-byte) tensor takes the shared-memory form: same bits."""
+    rng = np.random.default_rng(2)
+    a = rng.standard_normal((3, 512)).astype(np.float16)
+    buf = torch.zeros(3 * 512 + 1, dtype=torch.float16, device="cuda")
+    d = buf[1:].view(3, 512)
+    d.copy_(torch.from_numpy(a))
+    ctx.fwht(d, 256)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(d.cpu().numpy().view(np.uint16), s4ref.fwht(a, 256).view(np.uint16))
 
 
 def test_fwht_then_matmul(ctx):
