@@ -251,8 +251,9 @@ def run_ours(args, rank, world, local_rank):
     # The engine submits a decode step's recorded matmul steps at once (engine.js:236-282); the
     # chained GEMV runs the 16 matmuls of one sweep step (on the step's weight copies) as ONE
     # persistent launch. One chain per weight rotation; consecutive steps alternate between two
-    # bound buffer sets (inputs and outputs) and two streams, so a step's launch can begin while the
-    # previous one drains and the steps never share a buffer.
+    # bound buffer sets (inputs and outputs). The device-timed steps follow one another on one
+    # stream as programmatic dependent launches: a step's CTAs start, and stream their first
+    # weights, as the previous step's CTAs exit.
     xbuf2 = torch.empty_like(xbuf)
     ybuf2 = torch.empty_like(ybuf)
     xbuf2.copy_(xbuf)
@@ -275,9 +276,10 @@ def run_ours(args, rank, world, local_rank):
             for name, K, N in SHAPES:
                 ctx.matmul(xs[(M, name)], weight_for(name, rot, mi), M, ys[(M, name)], st)
 
-    # Each step is replayed from a CUDA graph (one per weight rotation) so the host does not pace
-    # the GPU: the chained launch for the headline, the 16 per-call launches for comparison.
-    graphs, call_graphs = [], []
+    # Steps are replayed from CUDA graphs so the host does not pace the GPU: graphs[n] holds the
+    # chained launches of rotations 0 .. n-1 back to back (graphs[COPIES] is a full rotation), and
+    # the 16 per-call launches of each rotation for comparison.
+    graphs, call_graphs = {}, []
     cap_stream = torch.cuda.Stream(dev)
     cap_stream.wait_stream(stream)
     with torch.cuda.stream(cap_stream):
@@ -285,14 +287,17 @@ def run_ours(args, rank, world, local_rank):
             chains[rot].run(cap_stream)      # eager warm-up
             sweep(rot, cap_stream)
         cap_stream.synchronize()
-        launches_per_step = None
-        for rot in range(COPIES):
+        n0 = ctx.launch_count
+        chains[0].run(cap_stream)
+        launches_per_step = ctx.launch_count - n0
+        cap_stream.synchronize()
+        for n in range(1, COPIES + 1):
             g = torch.cuda.CUDAGraph()
-            n0 = ctx.launch_count
             with torch.cuda.graph(g, stream=cap_stream):
-                chains[rot].run(cap_stream)
-            launches_per_step = ctx.launch_count - n0
-            graphs.append(g)
+                for rot in range(n):
+                    chains[rot].run(cap_stream)
+            graphs[n] = g
+        for rot in range(COPIES):
             g2 = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g2, stream=cap_stream):
                 sweep(rot, cap_stream)
@@ -300,11 +305,13 @@ def run_ours(args, rank, world, local_rank):
     stream.wait_stream(cap_stream)
     torch.cuda.synchronize(dev)
 
-    def step():
-        r = counter[0]
-        with torch.cuda.stream(step_streams[r % 2]):
-            graphs[r % COPIES].replay()
-        counter[0] += 1
+    def steps_on_stream(k: int):
+        # k steps: whole rotations, then the first k % COPIES chains of one, all on `stream`
+        with torch.cuda.stream(stream):
+            for _ in range(k // COPIES):
+                graphs[COPIES].replay()
+            if k % COPIES:
+                graphs[k % COPIES].replay()
 
     def barrier():
         if world > 1:
@@ -318,18 +325,13 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        step()
+    steps_on_stream(args.warmup)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         barrier()
-        counter[0] = 0
         e0.record(stream)
-        step_streams[1].wait_event(e0)
-        for _ in range(args.steps):
-            step()
-        stream.wait_stream(step_streams[1])
+        steps_on_stream(args.steps)
         e1.record(stream)
         barrier()
     launches = launches_per_step * args.steps   # kernels inside the replayed graphs
@@ -485,7 +487,8 @@ def run_ours(args, rank, world, local_rank):
             "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "decode_gemv_sweep_config2", "launch": "the 16 matmuls of a step as one chained launch", "M": MS,
+            "config": {"workload": "decode_gemv_sweep_config2", "launch": "the 16 matmuls of a step as one chained launch; steps back to back on one stream "
+                                 "(programmatic dependent launch)", "M": MS,
                        "shapes_KN": [[K, N] for _, K, N in SHAPES], "weight_copies": COPIES,
                        "l2": "inputs larger than L2: 8 rotating weight copies (272 MB) per step sequence",
                        "parallelism": f"dp{world} (weights replicated, no collective)"},

@@ -160,7 +160,12 @@ S4_API int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, 
  * Buffers are bound at creation (DEVICE pointers, x 16-byte aligned) and must stay valid while the
  * chain is used; results equal s4_matmul's within fp32 summation order. s4_chain_run is asynchronous
  * on `stream`; runs of one chain must not overlap. Creation is synchronous and allocates the chain's
- * split-K scratch. S4_ERR_UNSUPPORTED if an op's activation window does not fit in shared memory. */
+ * split-K scratch. S4_ERR_UNSUPPORTED if an op's activation window does not fit in shared memory.
+ * s4_chain_run launches as a programmatic dependent launch: a run that follows another kernel on the
+ * same stream streams its weights while that kernel drains (it reads activations and scratch only
+ * after that kernel completes). Its CTAs wait on one another, so chained runs issued on DIFFERENT
+ * streams must not execute concurrently with it (environment S4_PDL=0 gives a cooperative launch,
+ * safe on any streams). s4_chain_run_host always launches cooperatively. */
 S4_API int s4_chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y,
                            const int* M, const int* dep, s4_chain** out);
 S4_API int s4_chain_run(s4_ctx* ctx, s4_chain* chain, void* stream);

@@ -447,6 +447,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     s_fail = 0;
   }
   __syncthreads();
+  // Launched with programmatic stream serialization, the next grid in the stream may start its
+  // CTAs as ours exit. Only the producer runs before the previous grid has completed: it reads
+  // nothing but the weights (immutable after upload) and fills this CTA's ring. Every other role
+  // reads activations, completion counters or scratch the previous grid may write, so it waits.
+  // (Both instructions are no-ops in a cooperative launch.)
+  pdl_launch_dependents();
+  if (warp != kChainProducerWarp) pdl_wait();
 
   bool ok = true;
   if (warp == kChainProducerWarp) {
@@ -734,7 +741,7 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
   return S4_OK;
 }
 
-cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream) {
+cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream, bool cooperative) {
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -764,9 +771,19 @@ cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream) {
   cfg.blockDim = dim3(kChainThreads, 1, 1);
   cfg.dynamicSmemBytes = c->smem;
   cfg.stream = stream;
+  // Every CTA must be resident at once (CTAs wait on one another's counters). A cooperative launch
+  // guarantees that on any stream. A programmatic-dependent launch does too when runs follow one
+  // another on ONE stream: it begins only after every CTA of the previous grid has started (each
+  // triggers at entry), and that grid finishes without ours, freeing every SM. Chained runs on other
+  // streams must not overlap a programmatic one.
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  if (cooperative) {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return c->mg == 2 ? cudaLaunchKernelEx(&cfg, chain_kernel<2>, p) : cudaLaunchKernelEx(&cfg, chain_kernel<1>, p);

@@ -45,7 +45,7 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
                               cudaStream_t stream, bool pdl, bool ticket_fixup);
 int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y, const int* M,
                  const int* dep, s4_chain** out, const char** why);
-cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream);
+cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream, bool cooperative);
 void chain_destroy(s4_chain* c);
 int chain_info(const s4_chain* c, int* grid, int* slots, int* smem);
 bool tc_available();
@@ -818,7 +818,7 @@ int s4_chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void
 int s4_chain_run(s4_ctx* ctx, s4_chain* chain, void* stream) {
   if (!ctx || !chain) return fail(S4_ERR_INVALID, "NULL argument");
   DeviceGuard guard(ctx->device);
-  cudaError_t e = s4::chain_launch(chain, ctx->err, static_cast<cudaStream_t>(stream));
+  cudaError_t e = s4::chain_launch(chain, ctx->err, static_cast<cudaStream_t>(stream), !ctx->pdl);
   if (e != cudaSuccess) return cuda_fail(e, "chain launch");
   ++ctx->launches;
   return S4_OK;
@@ -833,7 +833,7 @@ int s4_chain_run_host(s4_ctx* ctx, s4_chain* chain, const void* x_host, void* x_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = x_bytes ? cudaMemcpyAsync(x_dev, x_host, x_bytes, cudaMemcpyHostToDevice, st) : cudaSuccess;
   if (e != cudaSuccess) return cuda_fail(e, "chain input upload");
-  e = s4::chain_launch(chain, ctx->err, st);
+  e = s4::chain_launch(chain, ctx->err, st, true);  // callers alternate streams between host-buffer runs
   if (e != cudaSuccess) return cuda_fail(e, "chain launch");
   ++ctx->launches;
   e = y_bytes ? cudaMemcpyAsync(y_host, y_dev, y_bytes, cudaMemcpyDeviceToHost, st) : cudaSuccess;
