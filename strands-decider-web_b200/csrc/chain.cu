@@ -75,7 +75,7 @@ struct ChainOp {
   int maxparts;
   int xrow;           // padded activation window row (bytes)
   int phase_base;     // first chunk of this op in its phase's concatenated chunk sequence
-  int phase_U;        // chunks of the whole phase
+  int phase_U;        // chunks of the whole phase; -1 for the dynamic op (no static ranges)
 };
 
 __device__ __forceinline__ uint32_t* chain_tickets(const ChainOp& op) {
@@ -94,6 +94,8 @@ struct ChainParams {
                        // evempty[kChainEv], pubfull[2], pubempty[2]
   uint32_t* op_done;   // [nops] finished sub-tiles
   uint32_t* exit_count;
+  uint32_t* dyn_next;  // next unclaimed n-block of the dynamic op
+  int dyn_op;          // index of the op whose n-blocks CTAs claim at run time, or -1
   uint32_t* err;
 };
 
@@ -154,6 +156,8 @@ __device__ __forceinline__ void cp_async_cg16(void* dst_smem, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 struct ChainSmem {
+  int* slot_unit;  // [kChainMaxSlots] n-block of the dynamic op a ring slot holds (-1: no more)
+  int* pub_nb;     // [2] n-block of a dynamic segment in a publish buffer (-1: no more)
   uint8_t* ring;
   uint8_t* xbuf;
   float4* ev;   // [2] part-0 sums for the reducer
@@ -395,14 +399,152 @@ __device__ bool chain_reduce(const ChainOp& op, const ChainRange& r, const Chain
   return true;
 }
 
+// ---- the dynamic op -------------------------------------------------------------------------------
+// When no op depends on another, the chain's last op is not cut into static ranges: each CTA's
+// producer, once its static share is streamed, claims whole n-blocks of it (atomic counter) until
+// none is left. A whole n-block needs no split-K partials, and the claims even out the CTAs' random
+// speed differences, which otherwise leave every launch waiting for its slowest CTA.
+
+// Producer: stream claimed n-blocks (all K, in groups of kChainGroup chunks) into the ring after
+// `seq` slots; a slot whose unit is -1 ends the op.
+__device__ bool chain_dyn_produce(const ChainOp& op, const ChainParams& p, const ChainSmem& sm, int& seq,
+                                  uint64_t pol) {
+  const int KT = op.ktiles;
+  for (;;) {
+    const int u = (int)atomicAdd(p.dyn_next, 1u);
+    const bool last = u >= op.nblk;
+    for (int k0 = 0; k0 < (last ? 1 : KT); k0 += kChainGroup, ++seq) {
+      const int slot = seq % p.slots;
+      if ((seq >= p.slots && !mbar_wait(sm.empty + slot, (uint32_t)((seq / p.slots) - 1) & 1u)) || *(volatile int*)sm.fail)
+        return false;
+      if (last) {
+        sm.slot_unit[slot] = -1;
+        mbar_arrive(sm.full + slot);  // no bytes: the sentinel completes the slot's phase by itself
+        break;
+      }
+      sm.slot_unit[slot] = u;
+      const int n = min(kChainGroup, KT - k0);
+      const int64_t g0 = (int64_t)u * KT + k0;
+      uint8_t* dst = sm.ring + slot * kChainSlotBytes;
+      mbar_arrive_expect_tx(sm.full + slot, (uint32_t)n * (kChunkWBytes + kChunkSBytes));
+      bulk_g2s(dst, op.wq + g0 * kChunkWBytes, (uint32_t)n * kChunkWBytes, sm.full + slot, pol);
+      bulk_g2s(dst + kChainSlotScales, op.ws + g0 * kChunkSBytes, (uint32_t)n * kChunkSBytes, sm.full + slot, pol);
+    }
+    if (last) return true;
+  }
+}
+
+// Consumers: whole n-blocks from the ring (window = all of K), each flushed as a direct segment
+// tagged with its n-block; a publish buffer tagged -1 ends the op.
+template <int MG>
+__device__ bool chain_dyn_consume(const ChainOp& op, const ChainParams& p, const ChainSmem& sm, int& slot,
+                                  uint32_t& phase, int xk, int& pubk) {
+  const int KT = op.ktiles;
+  const int sub = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int xb = xk % p.nx;
+  if (!mbar_wait(sm.xfull + xb, (uint32_t)(xk / p.nx) & 1u) || *(volatile int*)sm.fail) return false;
+  const uint8_t* xl = sm.xbuf + xb * p.x_bytes + g * op.xrow + 16 * t;
+  const int xgroup = 8 * op.xrow;
+  bool xok[MG];
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg) xok[mg] = (mg * 8 + g) < op.M;
+  float acc[MG][4];
+  int kt = 0;
+  for (;;) {
+    if (!mbar_wait(sm.full + slot, phase)) return false;
+    const int u = sm.slot_unit[slot];
+    const uint8_t* ch = sm.ring + slot * kChainSlotBytes;
+    if (u >= 0) {
+      if (kt == 0) {
+#pragma unroll
+        for (int mg = 0; mg < MG; ++mg)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[mg][e] = 0.f;
+      }
+      const int n = min(kChainGroup, KT - kt);
+      uint4 wv[kChainGroup];
+      uint2 sc[kChainGroup];
+#pragma unroll
+      for (int j = 0; j < kChainGroup; ++j)
+        if (j < n) {
+          wv[j] = *reinterpret_cast<const uint4*>(ch + j * kChunkWBytes + sub * 512 + lane * 16);
+          sc[j] = *reinterpret_cast<const uint2*>(ch + kChainSlotScales + j * kChunkSBytes + sub * 64 + g * 8);
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.empty + slot);
+#pragma unroll
+      for (int j = 0; j < kChainGroup; ++j)
+        if (j < n) gemv_tile<MG>(wv[j], sc[j], xl + (kt + j) * 128, xgroup, (kt + j) * 64 + 32 < op.K, xok, acc);
+      kt += n;
+    }
+    if (++slot == p.slots) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    if (u >= 0 && kt < KT) continue;
+    // an n-block is complete (or the op ended): hand it to the publisher
+    const int e = pubk & 1;
+    if (pubk >= 2 && !mbar_wait(sm.pubempty + e, (uint32_t)((pubk >> 1) - 1) & 1u)) return false;
+    ++pubk;
+    if (u >= 0) {
+      float4* dst = sm.pub + (size_t)e * (kChainSegBytes / 16) + (sub * MG) * 32 + lane;
+#pragma unroll
+      for (int mg = 0; mg < MG; ++mg) dst[mg * 32] = make_float4(acc[mg][0], acc[mg][1], acc[mg][2], acc[mg][3]);
+    }
+    if (threadIdx.x == 0) sm.pub_nb[e] = u;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.pubfull + e);
+    if (u < 0) break;
+    kt = 0;
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(sm.xempty + xb);
+  return true;
+}
+
+// Publisher: the dynamic op's segments, in the consumers' order.
+template <int MG>
+__device__ bool chain_dyn_publish(const ChainOp& op, const ChainParams& p, const ChainSmem& sm, int& pubk) {
+  const int lane = threadIdx.x & 31;
+  for (;;) {
+    const int e = pubk & 1;
+    if (!mbar_wait(sm.pubfull + e, (uint32_t)(pubk >> 1) & 1u)) return false;
+    ++pubk;
+    const int nb = sm.pub_nb[e];
+    if (nb < 0) return true;
+    const float4* src = sm.pub + (size_t)e * (kChainSegBytes / 16) + lane;
+    for (int sub = 0; sub < 8; ++sub) {
+      float v[MG][4];
+#pragma unroll
+      for (int mg = 0; mg < MG; ++mg) {
+        const float4 f = src[(sub * MG + mg) * 32];
+        v[mg][0] = f.x;
+        v[mg][1] = f.y;
+        v[mg][2] = f.z;
+        v[mg][3] = f.w;
+      }
+      chain_store_y<MG>(op, nb, sub, v);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.pubempty + e);
+    fence_acq_rel_gpu();
+    if (lane == 0) red_relaxed_gpu(p.op_done + p.dyn_op, 8u);
+  }
+}
+
 // MG: 8-token groups of every op of the launch (1 if all ops have M <= 8, else 2). One MG per
 // kernel keeps the code small enough for the instruction cache (five warp roles share it).
 template <int MG>
 __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_fail;
+  __shared__ int s_slot_unit[kChainMaxSlots];
+  __shared__ int s_pub_nb[2];
   __shared__ __align__(16) ChainOp s_ops[kChainCachedOps];
   ChainSmem sm;
+  sm.slot_unit = s_slot_unit;
+  sm.pub_nb = s_pub_nb;
   sm.ring = smem;
   sm.xbuf = smem + p.x_off;
   sm.ev = reinterpret_cast<float4*>(smem + p.ev_off);
@@ -479,6 +621,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
                    pol);
         }
       }
+      if (ok && p.dyn_op >= 0) {
+        pdl_wait();  // the claim counter is reset by the previous run's last CTA
+        ok = chain_dyn_produce(chain_op_at(p, sm, p.dyn_op), p, sm, seq, pol);
+      }
       if (!ok) {
         // copies still in flight land before the CTA exits (bounded)
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
@@ -494,7 +640,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       const uint64_t pol = policy_evict_last();  // every CTA reads the same activations
       for (int i = 0; i < p.nops && ok; ++i) {
         const ChainOp op = chain_op_at(p, sm, i);
-        const ChainRange r = chain_range(op, b, G);
+        ChainRange r = chain_range(op, b, G);
+        if (i == p.dyn_op) {  // the whole of K: any n-block may be claimed
+          r.c0 = 0;
+          r.c1 = op.ktiles;
+        }
         if (r.c0 >= r.c1) continue;
         const int xb = xk % p.nx;
         ok = !(xk >= p.nx && !mbar_wait(sm.xempty + xb, (uint32_t)((xk / p.nx) - 1) & 1u));
@@ -541,6 +691,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       if (r.c0 >= r.c1) continue;
       ok = chain_publish_op<MG>(op, r, p, sm, i, pubk);
     }
+    if (ok && p.dyn_op >= 0) ok = chain_dyn_publish<MG>(chain_op_at(p, sm, p.dyn_op), p, sm, pubk);
   } else if (warp == kChainReducerWarp) {
     // ---------------- reducer ----------------
     int evk = 0;
@@ -565,6 +716,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       ok = chain_consume<MG>(op, r, p, sm, slot, phase, xk, evk, pubk);
       ++xk;
     }
+    if (ok && p.dyn_op >= 0) ok = chain_dyn_consume<MG>(chain_op_at(p, sm, p.dyn_op), p, sm, slot, phase, xk, pubk);
   }
   if (!ok && lane == 0) {
     set_error(p.err, kErrWaitTimeout);
@@ -577,6 +729,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     if (prev == (uint32_t)(G - 1)) {  // last CTA of the run: completion counters back to zero
       __threadfence();
       for (int i = 0; i < p.nops; ++i) p.op_done[i] = 0u;
+      *p.dyn_next = 0u;
       *p.exit_count = 0u;
       __threadfence();
     }
@@ -599,6 +752,8 @@ struct s4_chain {
   uint8_t* d_scratch;  // partials, tickets, op_done, exit_count
   uint32_t* op_done;
   uint32_t* exit_count;
+  uint32_t* dyn_next;
+  int dyn_op;  // index of the dynamic op (the last), or -1
   std::vector<ChainOp> ops;
 };
 
@@ -633,6 +788,9 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
   // With no dependencies at all the ops may run in any order: the ops that need a phase of their own
   // (whole-K activation window above kChainPhaseWindow) go first, so their split-K reductions overlap
   // the streaming of the merged phase and the launch ends on a phase split at most twice per CTA.
+  // The small op with the most n-blocks then becomes the dynamic op (claimed n-block by n-block at
+  // run time, after every static range): it goes last and is left out of the phases.
+  int dyn_op = -1;
   {
     bool any_dep = false;
     for (int i = 0; i < nops; ++i) any_dep |= ops[i].dep >= 0;
@@ -640,17 +798,30 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
       std::vector<ChainOp> big, small;
       for (int i = 0; i < nops; ++i)
         (ops[i].M * (ops[i].ktiles * 128 + 64) > kChainPhaseWindow ? big : small).push_back(ops[i]);
+      long long total = 0;
+      for (int i = 0; i < nops; ++i) total += (long long)ops[i].nblk * ops[i].ktiles;
+      int pick = -1;
+      for (int i = 0; i < (int)small.size(); ++i)
+        if (pick < 0 || small[i].nblk > small[pick].nblk) pick = i;
+      if (nops >= 2 && pick >= 0 && small[pick].nblk >= 16 &&
+          (long long)small[pick].nblk * small[pick].ktiles * 100 <= total * 35) {
+        const ChainOp d = small[pick];
+        small.erase(small.begin() + pick);
+        small.push_back(d);
+        dyn_op = nops - 1;
+      }
       ops = big;
       ops.insert(ops.end(), small.begin(), small.end());
     }
   }
+  const int nstatic = dyn_op >= 0 ? nops - 1 : nops;
   // phases: runs of consecutive ops none of which reads another op of the run; an op whose whole-K
   // activation window would exceed kChainPhaseWindow stays alone (its range within a shared phase
   // could span whole n-blocks, i.e. all of K)
   std::vector<int> phase_start(nops);
   {
     int start = 0;
-    for (int i = 0; i < nops; ++i) {
+    for (int i = 0; i < nstatic; ++i) {
       const ChainOp& o = ops[i];
       const int wfull = o.M * (o.ktiles * 128 + 64);
       const bool big = wfull > kChainPhaseWindow;
@@ -659,9 +830,9 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
       phase_start[i] = start;
     }
   }
-  for (int i = 0; i < nops;) {
+  for (int i = 0; i < nstatic;) {
     int j = i, U = 0;
-    while (j < nops && phase_start[j] == i) {
+    while (j < nstatic && phase_start[j] == i) {
       ops[j].phase_base = U;
       U += ops[j].nblk * ops[j].ktiles;
       ++j;
@@ -669,17 +840,26 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     for (int q = i; q < j; ++q) ops[q].phase_U = U;
     i = j;
   }
+  if (dyn_op >= 0) {
+    ops[dyn_op].phase_base = 0;
+    ops[dyn_op].phase_U = -1;
+  }
   for (int i = 0; i < nops; ++i) {
     ChainOp& o = ops[i];
-    const int U = o.nblk * o.ktiles;
-    const int Gp = o.phase_U < G ? o.phase_U : G;
-    const int per_cta = (o.phase_U + Gp - 1) / Gp;
-    const int min_cta = o.phase_U / Gp;  // >= 1
-    o.maxparts = (o.ktiles + min_cta - 1) / min_cta + 1;  // CTAs one n-block can span
-    if (o.maxparts > Gp) o.maxparts = Gp;
-    int n_win = per_cta < U ? per_cta : U;
-    if (n_win > o.ktiles) n_win = o.ktiles;
-    o.xrow = n_win * 128 + 64;
+    if (i == dyn_op) {  // whole n-blocks only: no partials, a window of all of K
+      o.maxparts = 1;
+      o.xrow = o.ktiles * 128 + 64;
+    } else {
+      const int U = o.nblk * o.ktiles;
+      const int Gp = o.phase_U < G ? o.phase_U : G;
+      const int per_cta = (o.phase_U + Gp - 1) / Gp;
+      const int min_cta = o.phase_U / Gp;  // >= 1
+      o.maxparts = (o.ktiles + min_cta - 1) / min_cta + 1;  // CTAs one n-block can span
+      if (o.maxparts > Gp) o.maxparts = Gp;
+      int n_win = per_cta < U ? per_cta : U;
+      if (n_win > o.ktiles) n_win = o.ktiles;
+      o.xrow = n_win * 128 + 64;
+    }
     const int xb = o.M * o.xrow;
     if (xb > xmax) xmax = xb;
     part_off[i] = scratch;  // partials sized for MG = 2, the tickets right after (chain_tickets)
@@ -717,7 +897,7 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
   c->bar_off = c->ev_off + (kChainEv + 2) * kChainSegBytes;
   c->smem = c->bar_off + (2 * slots + 2 * nx + 2 * kChainEv + 4) * 8;
   const size_t ctr_off = scratch;
-  scratch += (size_t)(nops + 1) * 4;
+  scratch += (size_t)(nops + 2) * 4;  // op_done[nops], exit_count, dyn_next
   cudaError_t e = cudaMalloc(&c->d_scratch, scratch);
   if (e == cudaSuccess) e = cudaMemset(c->d_scratch, 0, scratch);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_ops, sizeof(ChainOp) * nops);
@@ -729,6 +909,8 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
   for (int i = 0; i < nops; ++i) ops[i].partials = reinterpret_cast<float*>(c->d_scratch + part_off[i]);
   c->op_done = reinterpret_cast<uint32_t*>(c->d_scratch + ctr_off);
   c->exit_count = c->op_done + nops;
+  c->dyn_next = c->exit_count + 1;
+  c->dyn_op = dyn_op;
   e = cudaMemcpy(c->d_ops, ops.data(), sizeof(ChainOp) * nops, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     cudaFree(c->d_ops);
@@ -765,6 +947,8 @@ cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream, bool c
   p.bar_off = c->bar_off;
   p.op_done = c->op_done;
   p.exit_count = c->exit_count;
+  p.dyn_next = c->dyn_next;
+  p.dyn_op = c->dyn_op;
   p.err = err;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(c->grid, 1, 1);

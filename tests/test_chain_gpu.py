@@ -232,3 +232,36 @@ def test_chain_runs_back_to_back_on_one_stream(ctx):
     assert ctx.check_errors() == 0
     for ch in chains:
         ch.free()
+
+
+@pytest.mark.parametrize("big_m", [7, 16])
+def test_dynamic_op_ragged_and_deterministic(ctx, big_m):
+    """A dependency-free chain whose op with the most n-blocks (17, the last one ragged: N = 2125,
+    K = 1024) is claimed n-block by n-block at run time, next to static ops; 1 and 2 token groups.
+    Every run matches the oracle and repeated runs are bitwise identical (a claimed n-block is summed
+    by one CTA in k order, whichever CTA claims it)."""
+    rng = np.random.default_rng(300 + big_m)
+    specs = [(1024, 2125, big_m), (2048, 2048, 3), (2048, 384, 2), (96, 200, 5), (2048, 1000, 9)]
+    ops, refs = [], []
+    for K, N, M in specs:
+        W, packed, scales = _weights(ctx, rng, K, N)
+        x = _x(rng, M, K)
+        y = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        ops.append((x, W, y))
+        refs.append(s4ref.matmul(x.cpu().numpy(), packed, scales)[1])
+    chain = ctx.chain(ops)
+    outs = []
+    for _ in range(4):
+        for o in ops:
+            o[2].fill_(float("nan"))
+        chain.run()
+        torch.cuda.synchronize()
+        assert ctx.check_errors() == 0
+        for (x, W, y), ref in zip(ops, refs):
+            ok, mr, mc = s4ref.check(y.cpu().numpy(), ref)
+            assert ok, (x.shape[0], W.K, W.N, mr, mc)
+        outs.append([o[2].clone() for o in ops])
+    for later in outs[1:]:
+        for a, b in zip(outs[0], later):
+            assert torch.equal(a, b)
+    chain.free()
