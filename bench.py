@@ -36,6 +36,7 @@ if ROOT not in sys.path:
 SHAPES = [("qkvz_ab", 2048, 8224), ("attn_qkv", 2048, 3072), ("gate_up", 2048, 12288), ("down", 6144, 2048)]
 MS = [1, 2, 4, 8]
 COPIES = 8
+BLOCK = 8 * COPIES  # chained launches per replayed graph in the device-timed loop
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
@@ -277,8 +278,9 @@ def run_ours(args, rank, world, local_rank):
                 ctx.matmul(xs[(M, name)], weight_for(name, rot, mi), M, ys[(M, name)], st)
 
     # Steps are replayed from CUDA graphs so the host does not pace the GPU: graphs[n] holds the
-    # chained launches of rotations 0 .. n-1 back to back (graphs[COPIES] is a full rotation), and
-    # the 16 per-call launches of each rotation for comparison.
+    # chained launches of rotations 0 .. n-1 back to back (graphs[COPIES] is a full rotation) and
+    # graphs[BLOCK] eight full rotations (consecutive launches overlap inside a graph, not across
+    # graph launches); call_graphs hold the 16 per-call launches of each rotation for comparison.
     graphs, call_graphs = {}, []
     cap_stream = torch.cuda.Stream(dev)
     cap_stream.wait_stream(stream)
@@ -291,11 +293,11 @@ def run_ours(args, rank, world, local_rank):
         chains[0].run(cap_stream)
         launches_per_step = ctx.launch_count - n0
         cap_stream.synchronize()
-        for n in range(1, COPIES + 1):
+        for n in list(range(1, COPIES + 1)) + [BLOCK]:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=cap_stream):
-                for rot in range(n):
-                    chains[rot].run(cap_stream)
+                for i in range(n):
+                    chains[i % COPIES].run(cap_stream)
             graphs[n] = g
         for rot in range(COPIES):
             g2 = torch.cuda.CUDAGraph()
@@ -306,9 +308,11 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
 
     def steps_on_stream(k: int):
-        # k steps: whole rotations, then the first k % COPIES chains of one, all on `stream`
+        # k steps on `stream`: blocks of eight rotations, whole rotations, then part of one
         with torch.cuda.stream(stream):
-            for _ in range(k // COPIES):
+            for _ in range(k // BLOCK):
+                graphs[BLOCK].replay()
+            for _ in range((k % BLOCK) // COPIES):
                 graphs[COPIES].replay()
             if k % COPIES:
                 graphs[k % COPIES].replay()
