@@ -237,6 +237,9 @@ __device__ bool chain_consume(const ChainOp& op, const ChainRange& r, const Chai
   for (int mg = 0; mg < MG; ++mg) xok[mg] = (mg * 8 + g) < op.M;
   const int xgroup = 8 * op.xrow;
   const uint8_t* xl = xs + g * op.xrow + 16 * t;
+  const uint8_t* xr[MG];  // per token group; a token past M reads row M - 1 (never stored)
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg) xr[mg] = xs + min(mg * 8 + g, op.M - 1) * op.xrow + 16 * t;
 
   float acc[MG][4];
 #pragma unroll
@@ -266,9 +269,13 @@ __device__ bool chain_consume(const ChainOp& op, const ChainRange& r, const Chai
     if (n == kChainGroup && kt + n <= KT && wpos + n <= KT && (kt + n) * 64 <= op.K) {
       // fast path: four chunks in one n-block and one stretch of the window, all of K in range;
       // the tiles are independent, so the compiler can overlap their latencies
-      const uint8_t* xg = xl + wpos * 128;
 #pragma unroll
-      for (int j = 0; j < kChainGroup; ++j) gemv_tile<MG>(wv[j], sc[j], xg + j * 128, xgroup, true, xok, acc);
+      for (int j = 0; j < kChainGroup; ++j) {
+        const uint8_t* xj[MG];
+#pragma unroll
+        for (int mg = 0; mg < MG; ++mg) xj[mg] = xr[mg] + (wpos + j) * 128;
+        gemv_tile_rows<MG>(wv[j], sc[j], xj, acc);
+      }
       kt += n;
       wpos += n;
       if (wpos == KT) wpos = 0;
@@ -444,11 +451,17 @@ __device__ bool chain_dyn_consume(const ChainOp& op, const ChainParams& p, const
   const int g = lane >> 2, t = lane & 3;
   const int xb = xk % p.nx;
   if (!mbar_wait(sm.xfull + xb, (uint32_t)(xk / p.nx) & 1u) || *(volatile int*)sm.fail) return false;
-  const uint8_t* xl = sm.xbuf + xb * p.x_bytes + g * op.xrow + 16 * t;
+  const uint8_t* xs = sm.xbuf + xb * p.x_bytes;
+  const uint8_t* xl = xs + g * op.xrow + 16 * t;
   const int xgroup = 8 * op.xrow;
   bool xok[MG];
+  const uint8_t* xr[MG];  // a token past M reads row M - 1 (never stored)
 #pragma unroll
-  for (int mg = 0; mg < MG; ++mg) xok[mg] = (mg * 8 + g) < op.M;
+  for (int mg = 0; mg < MG; ++mg) {
+    xok[mg] = (mg * 8 + g) < op.M;
+    xr[mg] = xs + min(mg * 8 + g, op.M - 1) * op.xrow + 16 * t;
+  }
+  const bool kfull = (op.K % 64) == 0;
   float acc[MG][4];
   int kt = 0;
   for (;;) {
@@ -473,9 +486,19 @@ __device__ bool chain_dyn_consume(const ChainOp& op, const ChainParams& p, const
         }
       __syncwarp();
       if (lane == 0) mbar_arrive(sm.empty + slot);
+      if (n == kChainGroup && kfull) {
 #pragma unroll
-      for (int j = 0; j < kChainGroup; ++j)
-        if (j < n) gemv_tile<MG>(wv[j], sc[j], xl + (kt + j) * 128, xgroup, (kt + j) * 64 + 32 < op.K, xok, acc);
+        for (int j = 0; j < kChainGroup; ++j) {
+          const uint8_t* xj[MG];
+#pragma unroll
+          for (int mg = 0; mg < MG; ++mg) xj[mg] = xr[mg] + (kt + j) * 128;
+          gemv_tile_rows<MG>(wv[j], sc[j], xj, acc);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kChainGroup; ++j)
+          if (j < n) gemv_tile<MG>(wv[j], sc[j], xl + (kt + j) * 128, xgroup, (kt + j) * 64 + 32 < op.K, xok, acc);
+      }
       kt += n;
     }
     if (++slot == p.slots) {

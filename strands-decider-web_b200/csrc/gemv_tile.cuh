@@ -35,6 +35,39 @@ __device__ __forceinline__ void gemv_tile(const uint4 w, const uint2 sc, const u
   }
 }
 
+// The same tile with one activation row pointer per token group, already at this k-tile, and both
+// 32-blocks inside K: no predicates. A lane whose token is past M reads a valid row instead
+// (min(token, M - 1)): token columns of the MMA are independent and those outputs are never stored.
+template <int MG>
+__device__ __forceinline__ void gemv_tile_rows(const uint4 w, const uint2 sc, const uint8_t* const (&xr)[MG],
+                                               float (&acc)[MG][4]) {
+  const uint32_t wr[4] = {w.x, w.y, w.z, w.w};
+  const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&sc.x));
+  const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&sc.y));
+  uint4 xv[MG][2];
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg)
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) xv[mg][blk] = *reinterpret_cast<const uint4*>(xr[mg] + blk * 64);
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    uint32_t ha[4], hb[4];
+    i4x8_to_h2x4_centered(wr[2 * blk + 0], ha);
+    i4x8_to_h2x4_centered(wr[2 * blk + 1], hb);
+    const float sg = blk ? s1.x : s0.x, sg8 = blk ? s1.y : s0.y;
+#pragma unroll
+    for (int mg = 0; mg < MG; ++mg) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_16816(d, ha[0], hb[0], ha[1], hb[1], xv[mg][blk].x, xv[mg][blk].y);
+      mma_16816(d, ha[2], hb[2], ha[3], hb[3], xv[mg][blk].z, xv[mg][blk].w);
+      acc[mg][0] = fmaf(sg, d[0], acc[mg][0]);
+      acc[mg][1] = fmaf(sg, d[1], acc[mg][1]);
+      acc[mg][2] = fmaf(sg8, d[2], acc[mg][2]);
+      acc[mg][3] = fmaf(sg8, d[3], acc[mg][3]);
+    }
+  }
+}
+
 // Asymmetric formats: the lane's weights dequantised to fp16 first, w = fma(q, scale, bias) per
 // element (the f16 form of kernels.js:36), then one mma per 16 K; no per-block scaling after it.
 // bi = biases in the order of sc.
