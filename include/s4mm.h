@@ -102,6 +102,17 @@ S4_API int s4_weight_upload_wire(s4_ctx* ctx, const uint8_t* packed, const uint8
 S4_API int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, const void* bias, int N, int K,
                                    int bits, int group, uint32_t flags, s4_weight** out);
 
+/* A fused gate|up projection whose matmul writes the SiLU*mul of its two halves: packed / scales are
+ * the MatMulNBits bytes of the [2I][K] weight (rows 0..I-1 gate, I..2I-1 up, the engine's fused
+ * layout), and s4_matmul / s4_matmul_gather on it write y[M][I] = silu(x W_gate^T) * (x W_up^T)
+ * (the SILU_MUL step, wgsl.js:81-90, engine.js:279-280, done in the GEMM epilogue; gate and up are
+ * rounded to fp16 first, as when they pass through memory). I % 64 == 0. Upload permutes rows so a
+ * 128-row tile holds 64 gate rows and their 64 up rows. s4_weight_info reports N = I. Not usable by a
+ * chain or s4_matmul_noalloc (S4_ERR_UNSUPPORTED). flags: S4_UPLOAD_DEVICE for device pointers.
+ * Synchronous. */
+S4_API int s4_weight_upload_glu(s4_ctx* ctx, const void* packed, const void* scales, int I, int K, uint32_t flags,
+                                s4_weight** out);
+
 S4_API int s4_weight_free(s4_weight* w);
 
 /* On-disk cache of repacked weights (the role of the worker's OPFS asset cache, worker.js:27-44,

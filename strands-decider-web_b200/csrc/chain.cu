@@ -804,6 +804,7 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     o.ktiles = wi->ktiles;
     o.dep = dep ? dep[i] : -1;
     if (wi->wb) return *why = "asymmetric-format weights run through s4_matmul, not a chain", S4_ERR_UNSUPPORTED;
+    if (wi->glu) return *why = "fused gate|up (SiLU*mul) weights run through s4_matmul, not a chain", S4_ERR_UNSUPPORTED;
     if (o.M < 1 || o.M > 16) return *why = "every op needs 1 <= M <= 16", S4_ERR_INVALID;
     if (o.dep >= i || o.dep < -1) return *why = "dep must name an earlier op or be -1", S4_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(x[i]) & 15) || (o.K * 2) % 16) return *why = "x must be 16-byte aligned", S4_ERR_INVALID;

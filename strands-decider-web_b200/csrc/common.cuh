@@ -162,6 +162,9 @@ __device__ __forceinline__ void i4x8_to_h2x4_centered(uint32_t w, uint32_t (&h)[
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[3]) : "r"(t3), "r"(mul16), "r"(add72));
 }
 
+// silu(g) * u in fp32 (wgsl.js:81-90); every kernel that produces SiLU*mul outputs uses this one.
+__device__ __forceinline__ float silu_mul_f32(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
 // Same element order, uncentered: fp16 q in [0, 15] (asymmetric formats, w = q * scale + bias).
 __device__ __forceinline__ void i4x8_to_h2x4_raw(uint32_t w, uint32_t (&h)[4]) {
   const uint32_t kLo = 0x000f000fu, kHi = 0x00f000f0u, kMagic = 0x64006400u;

@@ -62,6 +62,7 @@ struct TcParams {
   const uint8_t* wq;
   const uint8_t* ws;
   const uint8_t* wb;  // asymmetric formats: biases in the layout of ws (else nullptr)
+  int glu;            // fused gate|up weight: write silu(gate) * up, N / 2 columns (see repack.cu)
   __half* ydst[kTcMaxDst];  // output buffers: y[tok * ldy + ycol0 + n] is written to each
   int ndst;
   int64_t ldy;
@@ -419,7 +420,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       }
       const int sel = (u0 == wk.sk0) ? 0 : 1;  // partial slot: first or last stream-K segment
       float* mine = p.partials + (((int64_t)blockIdx.x * 2 + sel) * kTcMaxTn) * 128 + nl;
-      if (!failed) {
+      if (p.glu && full) {
+        // SiLU*mul: lane quarters q and q + 2 hold the gate and up rows of the same 32 features; each
+        // stages its fp16 values, then the pair computes the outputs, 8 tokens each. The pair's two
+        // barriers run on every slab even after a failed wait (the partner still arrives).
+        const int pq = q & 1;
+        const __half* gs = reinterpret_cast<const __half*>(smem + kTcOffEpi + pq * kTcEpiStageBytes);
+        const __half* us = reinterpret_cast<const __half*>(smem + kTcOffEpi + (pq + 2) * kTcEpiStageBytes);
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
+        if (!failed) tc_fence_after();
+        for (int cb = 0; cb < p.tn; cb += 16) {
+          if (!failed) {
+            float v[16];
+            tmem_ld16(taddr + cb, v);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) epi_stage[e * 32 + lane] = __float2half_rn(v[e]);
+          }
+          named_bar_sync(3 + pq, 64);
+          if (!failed) {
+            const int t = (q >> 1) * 8 + (lane >> 2), c = lane & 3;
+            const uint4 gv = *reinterpret_cast<const uint4*>(gs + t * 32 + c * 8);
+            const uint4 uv = *reinterpret_cast<const uint4*>(us + t * 32 + c * 8);
+            const __half2* g2 = reinterpret_cast<const __half2*>(&gv);
+            const __half2* u2 = reinterpret_cast<const __half2*>(&uv);
+            uint4 ov;
+            __half2* o2 = reinterpret_cast<__half2*>(&ov);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 g = __half22float2(g2[e]), u = __half22float2(u2[e]);
+              o2[e] = __floats2half2_rn(silu_mul_f32(g.x, u.x), silu_mul_f32(g.y, u.y));
+            }
+            const int tok = tok0 + cb + t;
+            if (tok < p.M) {
+              const int64_t off = tc_out_off(p, tok, nb * 64 + pq * 32 + c * 8);
+              for (int d = 0; d < p.ndst; ++d) *reinterpret_cast<uint4*>(p.ydst[d] + off) = ov;
+            }
+          }
+          named_bar_sync(3 + pq, 64);
+        }
+        if (!failed) {
+          tc_fence_before();
+          mbar_arrive(acce + buf);
+        }
+      } else if (!failed) {
         tc_fence_after();
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
         for (int cb = 0; cb < p.tn; cb += 16) {
@@ -524,6 +567,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
 // kernels.js:269-282, fp32 throughout). CTA (b, row group) handles the tile that GEMM CTA b's range
 // starts inside of, when b is that tile's second CTA, so every split tile is done exactly once.
 __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcParams p) {
+  __shared__ float up_s[64][8];  // fused gate|up weight: the up rows' sums
   pdl_wait();  // the partials come from the GEMM launched just before
   const int b = blockIdx.x, KT = p.ktiles;
   const int cb = tc_begin(b, p);
@@ -558,6 +602,22 @@ __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcParams p) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] += v[j][e];
       }
+  }
+  if (p.glu) {  // rows 64.. are the up rows of rows 0..63 (see repack.cu): SiLU*mul, fp16 in between
+    if (nl >= 64)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) up_s[nl - 64][e] = acc[e];
+    __syncthreads();
+    if (nl < 64) {
+      const int64_t off0 = tc_out_off(p, tok0 + r0, nb * 64 + nl);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (r0 + e < rows) {
+          const float g = __half2float(__float2half_rn(acc[e])), u = __half2float(__float2half_rn(up_s[nl][e]));
+          tc_store_all(p, off0 + e * p.ldy, __float2half_rn(silu_mul_f32(g, u)));
+        }
+    }
+    return;
   }
   if (ncol < p.N) {
     const int64_t off0 = tc_out_off(p, tok0 + r0, ncol);
@@ -603,7 +663,7 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
                               __half* const* ydst,
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
-                              cudaStream_t stream, bool pdl, bool ticket_fixup) {
+                              cudaStream_t stream, bool pdl, bool ticket_fixup, int glu) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   int tn = tile_n > 0 ? tile_n : (M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16);
@@ -613,6 +673,7 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
   p.wq = wq;
   p.ws = ws;
   p.wb = wb;
+  p.glu = glu;
   for (int d = 0; d < kTcMaxDst; ++d) p.ydst[d] = d < ndst ? ydst[d] : nullptr;
   p.ndst = ndst;
   p.ldy = ldy;
@@ -639,6 +700,8 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
   // a little fewer tiles than CTAs: one whole tile per CTA (a few idle SMs cost less than splitting
   // nearly every tile and fixing it up)
   if (tiles < p.grid && tiles * 4 >= p.grid * 3) p.grid = tiles;
+  // the fused SiLU*mul epilogue stores 8 outputs at a time and has no in-kernel ticket fix-up
+  if (glu && (!p.vec || ticket_fixup || N % 128)) return cudaErrorInvalidValue;
   p.dpq = tiles / p.grid;
   p.sk_base = p.dpq * p.grid * ktiles;
   p.sk_total = p.total - p.sk_base;
@@ -700,10 +763,10 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
 cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
                            float* partials, uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K,
                            int nblk, int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl,
-                           bool ticket_fixup) {
+                           bool ticket_fixup, int glu) {
   __half* dst[1] = {y};
-  return launch_tc_gemm_ex(wq, ws, wb, x, K, dst, 1, N, 0, partials, tickets, max_tickets, err, M, N, K, nblk, ktiles,
-                           tile_n, grid, stream, pdl, ticket_fixup);
+  return launch_tc_gemm_ex(wq, ws, wb, x, K, dst, 1, glu ? N / 2 : N, 0, partials, tickets, max_tickets, err, M, N, K,
+                           nblk, ktiles, tile_n, grid, stream, pdl, ticket_fixup, glu);
 }
 
 }  // namespace s4
@@ -736,6 +799,7 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   if (M < 0) return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: M must be >= 0");
   if (M == 0) return S4_OK;
   if (!x || !y) return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: NULL x or y");
+  if (w->glu) return record_error(S4_ERR_UNSUPPORTED, "s4_matmul_noalloc: fused gate|up weights run through s4_matmul");
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
     return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: x and y must be 16-byte aligned");
   const int dev = w->ctx->device;
@@ -771,7 +835,7 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: clearing the static scratch failed");
   const int grid = w->ctx->sm_count < kStaticMaxGrid ? w->ctx->sm_count : kStaticMaxGrid;
   e = launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
-                     (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true, true);
+                     (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true, true, 0);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: tcgen05 GEMM launch failed");
   return S4_OK;
 }

@@ -30,6 +30,7 @@ struct GemvParams {
   const uint8_t* wq;  // repacked int4: chunk (nb, kt) at wq + (nb*KT + kt)*4096, sub-tile s at +s*512
   const uint8_t* ws;  // repacked scales: chunk at ws + (nb*KT + kt)*512, sub-tile s at +s*64
   const uint8_t* wb;  // asymmetric formats: biases in the layout of ws (else unused)
+  int glu;            // fused gate|up weight: y[M][N/2] = silu(gate) * up (see repack.cu)
   const __half* x;    // [M][K]
   __half* y;          // [M][N]
   uint32_t* err;      // device error word
@@ -172,6 +173,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
   for (int mg = 0; mg < MG; ++mg) mine[mg * kGemvWarps * 32] = make_float4(acc[mg][0], acc[mg][1], acc[mg][2], acc[mg][3]);
   if (S > 1) cluster_sync_all();
   if (rank == 0) {
+    float sums[MG][4];
 #pragma unroll
     for (int mg = 0; mg < MG; ++mg) {
       // every peer's partial requested at once (one round trip), then summed in rank order
@@ -189,6 +191,11 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
           sum.w += v[q].w;
         }
       const float out[4] = {sum.x, sum.y, sum.z, sum.w};
+      sums[mg][0] = sum.x;
+      sums[mg][1] = sum.y;
+      sums[mg][2] = sum.z;
+      sums[mg][3] = sum.w;
+      if (p.glu) continue;
       const int n0 = nb * 128 + sub * 16 + g;
       const int tok = p.token0 + mg * 8 + 2 * t;
 #pragma unroll
@@ -196,6 +203,31 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
         const int m = tok + (e & 1);
         const int n = n0 + ((e >> 1) << 3);
         if (m < p.M && n < p.N) p.y[(int64_t)m * p.N + n] = __float2half_rn(out[e]);
+      }
+    }
+    if (p.glu) {
+      // sub-tiles 4..7 hold the up rows of sub-tiles 0..3 (see repack.cu): each up warp leaves its
+      // sums in its own reduction slot (already consumed), the gate warps combine
+      if (sub >= 4)
+#pragma unroll
+        for (int mg = 0; mg < MG; ++mg)
+          mine[mg * kGemvWarps * 32] = make_float4(sums[mg][0], sums[mg][1], sums[mg][2], sums[mg][3]);
+      __syncthreads();
+      if (sub < 4) {
+        const int I = p.N / 2;
+#pragma unroll
+        for (int mg = 0; mg < MG; ++mg) {
+          const float4 uv = mine[4 * 32 + mg * kGemvWarps * 32];
+          const float up[4] = {uv.x, uv.y, uv.z, uv.w};
+          const int j0 = nb * 64 + sub * 16 + g;
+          const int tok = p.token0 + mg * 8 + 2 * t;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int m = tok + (e & 1);
+            const float gf = __half2float(__float2half_rn(sums[mg][e])), uf = __half2float(__float2half_rn(up[e]));
+            if (m < p.M) p.y[(int64_t)m * I + j0 + ((e >> 1) << 3)] = __float2half_rn(silu_mul_f32(gf, uf));
+          }
+        }
       }
     }
   }
@@ -257,11 +289,12 @@ static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t strea
 
 cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
                         uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0, int groups, int split,
-                        int sm_count, cudaStream_t stream, bool pdl) {
+                        int sm_count, cudaStream_t stream, bool pdl, int glu) {
   GemvParams p;
   p.wq = wq;
   p.ws = ws;
   p.wb = wb;
+  p.glu = glu;
   p.x = x;
   p.y = y;
   p.err = err;

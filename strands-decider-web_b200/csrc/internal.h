@@ -56,6 +56,7 @@ struct s4_weight {
   uint8_t* wq = nullptr;
   uint8_t* ws = nullptr;
   uint8_t* wb = nullptr;  // asymmetric formats: per-32-block fp16 biases in the layout of ws
+  int glu = 0;            // fused gate|up weight (rows permuted, see repack.cu): matmuls write SiLU*mul, N / 2 wide
   size_t wq_bytes = 0, ws_bytes = 0;
 };
 

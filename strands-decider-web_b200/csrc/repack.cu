@@ -12,6 +12,14 @@
 // slices are exactly its mma.sync fragments; the tcgen05 GEMM reads whole 4 KB chunks with one
 // bulk copy. Rows >= N and K >= K are padded with nibble 8 (weight 0) and scale 0. With wq == nullptr
 // only the scale pass runs (the biases of an asymmetric format take the layout of the scales).
+// glu_I > 0: the input is a fused gate|up weight of 2 * glu_I rows (gate rows, then up rows) and
+// n-block b takes gate rows 64b .. 64b+63 followed by the up rows of the same features, so one
+// 128-row tile holds both halves of 64 SiLU*mul outputs.
+__device__ __forceinline__ int repack_src_row(int r, int glu_I) {
+  if (glu_I <= 0) return r;
+  const int b = r >> 7, i = r & 127;
+  return i < 64 ? 64 * b + i : glu_I + 64 * b + (i - 64);
+}
 #include "common.cuh"
 
 namespace s4 {
@@ -30,7 +38,7 @@ __device__ __forceinline__ uint32_t shuffle_nibbles(uint32_t w) {
 
 __global__ void repack_weights_kernel(const uint8_t* __restrict__ packed, const __half* __restrict__ scales,
                                       uint32_t* __restrict__ wq, __half* __restrict__ ws, int N, int K, int nblk,
-                                      int ktiles) {
+                                      int ktiles, int glu_I) {
   const int64_t words = wq ? (int64_t)nblk * ktiles * 1024 : 0;  // 4096 B per chunk; none for a bias-only pass
   const int blocks_per_row = K / 32;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
@@ -45,7 +53,7 @@ __global__ void repack_weights_kernel(const uint8_t* __restrict__ packed, const 
     const int k0 = kt * 64 + blk * 32 + 8 * t;
     uint32_t v = 0x88888888u;
     if (r < N && k0 < K) {
-      const uint8_t* row = packed + (int64_t)r * blocks_per_row * 16;
+      const uint8_t* row = packed + (int64_t)repack_src_row(r, glu_I) * blocks_per_row * 16;
       v = *reinterpret_cast<const uint32_t*>(row + k0 / 2);
       v = shuffle_nibbles(v);
     }
@@ -63,18 +71,18 @@ __global__ void repack_weights_kernel(const uint8_t* __restrict__ packed, const 
     const int r = nb * 128 + sub * 16 + g + 8 * h;
     const int b = kt * 2 + blk;
     __half s = __ushort_as_half((unsigned short)0);
-    if (r < N && b < blocks_per_row) s = scales[(int64_t)r * blocks_per_row + b];
+    if (r < N && b < blocks_per_row) s = scales[(int64_t)repack_src_row(r, glu_I) * blocks_per_row + b];
     ws[i] = s;
   }
 }
 
 cudaError_t launch_repack(const uint8_t* packed, const __half* scales, uint32_t* wq, __half* ws, int N, int K,
-                          int nblk, int ktiles, int sm_count, cudaStream_t stream) {
+                          int nblk, int ktiles, int sm_count, cudaStream_t stream, int glu_I) {
   const int64_t words = (int64_t)nblk * ktiles * 1024;
   int64_t want = (words + 255) / 256;
   int grid = (int)(want < (int64_t)sm_count * 16 ? want : (int64_t)sm_count * 16);
   if (grid < 1) grid = 1;
-  repack_weights_kernel<<<grid, 256, 0, stream>>>(packed, scales, wq, ws, N, K, nblk, ktiles);
+  repack_weights_kernel<<<grid, 256, 0, stream>>>(packed, scales, wq, ws, N, K, nblk, ktiles, glu_I);
   return cudaGetLastError();
 }
 

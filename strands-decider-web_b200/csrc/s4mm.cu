@@ -19,10 +19,10 @@ using s4::DeviceGuard;
 
 namespace s4 {
 cudaError_t launch_repack(const uint8_t* packed, const __half* scales, uint32_t* wq, __half* ws, int N, int K,
-                          int nblk, int ktiles, int sm_count, cudaStream_t stream);
+                          int nblk, int ktiles, int sm_count, cudaStream_t stream, int glu_I);
 cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
                         uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0, int groups, int split,
-                        int sm_count, cudaStream_t stream, bool pdl);
+                        int sm_count, cudaStream_t stream, bool pdl, int glu);
 int gemv_max_split();
 int gemv_max_tokens();
 cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
@@ -42,7 +42,7 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
                               __half* const* ydst,
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
-                              cudaStream_t stream, bool pdl, bool ticket_fixup);
+                              cudaStream_t stream, bool pdl, bool ticket_fixup, int glu);
 int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y, const int* M,
                  const int* dep, s4_chain** out, const char** why);
 cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream, bool cooperative);
@@ -53,7 +53,7 @@ size_t tc_partials_bytes(int max_grid);
 cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
                            float* partials, uint32_t* tickets, int max_tickets, uint32_t* err, int M, int N, int K,
                            int nblk, int ktiles, int tile_n, int grid, cudaStream_t stream, bool pdl,
-                           bool ticket_fixup);
+                           bool ticket_fixup, int glu);
 }  // namespace s4
 
 namespace {
@@ -227,12 +227,13 @@ bool parse_table(const char* text, std::vector<Bucket>& out, std::string& why) {
 }
 
 int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, int N, int K, s4_weight** out,
-                  const void* bias_dev = nullptr) {
+                  const void* bias_dev = nullptr, int glu_I = 0) {
   s4_weight* w = new (std::nothrow) s4_weight();
   if (!w) return fail(S4_ERR_NOMEM, "out of host memory");
   w->ctx = ctx;
   w->N = N;
   w->K = K;
+  w->glu = glu_I > 0;
   w->nblk = (N + s4::kRowsPerBlock - 1) / s4::kRowsPerBlock;
   w->ktiles = (K + s4::kKPerTile - 1) / s4::kKPerTile;
   w->wq_bytes = (size_t)w->nblk * w->ktiles * s4::kChunkWBytes;
@@ -249,11 +250,11 @@ int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, i
   }
   e = s4::launch_repack(static_cast<const uint8_t*>(packed_dev), static_cast<const __half*>(scales_dev),
                         reinterpret_cast<uint32_t*>(w->wq), reinterpret_cast<__half*>(w->ws), N, K, w->nblk,
-                        w->ktiles, ctx->sm_count, ctx->stream);
+                        w->ktiles, ctx->sm_count, ctx->stream, glu_I);
   if (e == cudaSuccess && bias_dev) {
     ++ctx->launches;
     e = s4::launch_repack(nullptr, static_cast<const __half*>(bias_dev), nullptr, reinterpret_cast<__half*>(w->wb), N,
-                          K, w->nblk, w->ktiles, ctx->sm_count, ctx->stream);
+                          K, w->nblk, w->ktiles, ctx->sm_count, ctx->stream, 0);
   }
   if (e == cudaSuccess) {
     ++ctx->launches;
@@ -525,6 +526,35 @@ int s4_fwht(s4_ctx* ctx, void* a, int M, int K, int n, void* stream) {
   return S4_OK;
 }
 
+int s4_weight_upload_glu(s4_ctx* ctx, const void* packed, const void* scales, int I, int K, uint32_t flags,
+                         s4_weight** out) {
+  if (!ctx || !packed || !scales || !out) return fail(S4_ERR_INVALID, "NULL argument");
+  if (flags & ~S4_UPLOAD_DEVICE) return fail(S4_ERR_INVALID, "unknown flags 0x%x", flags);
+  if (I < 64 || I % 64) return fail(S4_ERR_INVALID, "I must be a positive multiple of 64 (got %d)", I);
+  int rc = check_shape(2 * I, K);
+  if (rc) return rc;
+  DeviceGuard guard(ctx->device);
+  if (flags & S4_UPLOAD_DEVICE) {
+    if ((reinterpret_cast<uintptr_t>(packed) & 3) || (reinterpret_cast<uintptr_t>(scales) & 1))
+      return fail(S4_ERR_INVALID, "packed must be 4-byte and scales 2-byte aligned");
+    return upload_common(ctx, packed, scales, 2 * I, K, out, nullptr, I);
+  }
+  const size_t pbytes = (size_t)2 * I * (K / 32) * 16, sbytes = (size_t)2 * I * (K / 32) * 2;
+  uint8_t* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, pbytes + sbytes);
+  if (e != cudaSuccess) return fail(S4_ERR_NOMEM, "upload staging of %zu bytes failed", pbytes + sbytes);
+  e = cudaMemcpyAsync(d, packed, pbytes, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d + pbytes, scales, sbytes, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(d);
+    return cuda_fail(e, "upload copy");
+  }
+  rc = upload_common(ctx, d, d + pbytes, 2 * I, K, out, nullptr, I);
+  cudaFree(d);
+  return rc;
+}
+
 int s4_weight_free(s4_weight* w) {
   if (!w) return S4_OK;
   DeviceGuard guard(w->ctx->device);
@@ -540,6 +570,7 @@ int s4_weight_info(const s4_weight* w, int* N, int* K, size_t* device_bytes) {
   if (N) *N = w->N;
   if (K) *K = w->K;
   if (device_bytes) *device_bytes = w->wq_bytes + w->ws_bytes + (w->wb ? w->ws_bytes : 0);
+  if (N && w->glu) *N = w->N / 2;  // a fused gate|up weight's matmul writes N / 2 columns
   return S4_OK;
 }
 
@@ -567,7 +598,7 @@ constexpr uint32_t kCacheLayoutVersion = 1;    // the device layout of repack.cu
 struct CacheHeader {
   uint32_t magic, version;
   int32_t N, K;
-  uint32_t flags;  // bit 0: asymmetric (a bias section follows the scales)
+  uint32_t flags;  // bit 0: asymmetric (a bias section follows the scales); bit 1: fused gate|up (SiLU*mul)
   uint32_t reserved0;
   uint64_t wq_bytes, ws_bytes, wb_bytes;
   uint64_t checksum;  // of the payload, cache_checksum()
@@ -609,7 +640,7 @@ int s4_weight_save(const s4_weight* w, const char* path) {
   h.version = kCacheLayoutVersion;
   h.N = w->N;
   h.K = w->K;
-  h.flags = w->wb ? 1u : 0u;
+  h.flags = (w->wb ? 1u : 0u) | (w->glu ? 2u : 0u);
   h.wq_bytes = w->wq_bytes;
   h.ws_bytes = w->ws_bytes;
   h.wb_bytes = wb_bytes;
@@ -635,7 +666,7 @@ int s4_weight_load(s4_ctx* ctx, const char* path, s4_weight** out) {
     fclose(f);
     return fail(S4_ERR_IO, "%s: truncated header", path);
   }
-  if (h.magic != kCacheMagic || h.version != kCacheLayoutVersion || (h.flags & ~1u)) {
+  if (h.magic != kCacheMagic || h.version != kCacheLayoutVersion || (h.flags & ~3u)) {
     fclose(f);
     return fail(S4_ERR_IO, "%s: not a weight of layout version %u", path, kCacheLayoutVersion);
   }
@@ -651,6 +682,7 @@ int s4_weight_load(s4_ctx* ctx, const char* path, s4_weight** out) {
   w->ctx = ctx;
   w->N = h.N;
   w->K = h.K;
+  w->glu = (h.flags & 2u) ? 1 : 0;
   w->nblk = (h.N + s4::kRowsPerBlock - 1) / s4::kRowsPerBlock;
   w->ktiles = (h.K + s4::kKPerTile - 1) / s4::kKPerTile;
   w->wq_bytes = (size_t)w->nblk * w->ktiles * s4::kChunkWBytes;
@@ -720,8 +752,9 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
     for (long long r0 = 0; r0 < M; r0 += rows_cap) {
       const int rows = (int)std::min<long long>(rows_cap, M - r0);
       e = s4::launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x) + r0 * w->K,
-                             static_cast<__half*>(y) + r0 * w->N, ctx->partials, ctx->tickets, kMaxTickets, ctx->err,
-                             rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl, false);
+                             static_cast<__half*>(y) + r0 * (w->glu ? w->N / 2 : w->N), ctx->partials, ctx->tickets,
+                             kMaxTickets, ctx->err, rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl, false,
+                             w->glu);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
       ++ctx->launches;
     }
@@ -731,7 +764,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
     const int rem = M - tok0;
     const int groups = rem >= kGemvMaxM ? kGemvMaxM / 8 : (rem + 7) / 8;
     e = s4::launch_gemv(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->err, M, w->N,
-                        w->K, w->nblk, w->ktiles, tok0, groups, b.split, ctx->sm_count, st, ctx->pdl);
+                        w->K, w->nblk, w->ktiles, tok0, groups, b.split, ctx->sm_count, st, ctx->pdl, w->glu);
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     ++ctx->launches;
   }
@@ -744,7 +777,7 @@ int s4_matmul_host(s4_ctx* ctx, const s4_weight* w, const uint16_t* x, int M, ui
   if (M == 0) return S4_OK;
   if (!x || !y) return fail(S4_ERR_INVALID, "NULL x or y");
   DeviceGuard guard(ctx->device);
-  const size_t xb = (size_t)M * w->K * 2, yb = (size_t)M * w->N * 2;
+  const size_t xb = (size_t)M * w->K * 2, yb = (size_t)M * (w->glu ? w->N / 2 : w->N) * 2;
   if (xb > ctx->dx_cap || yb > ctx->dy_cap) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(e, "staging resize");
@@ -769,7 +802,7 @@ int s4_matmul_host_async(s4_ctx* ctx, const s4_weight* w, const uint16_t* x, int
   if (!x || !y) return fail(S4_ERR_INVALID, "NULL x or y");
   DeviceGuard guard(ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const size_t xb = (size_t)M * w->K * 2, yb = (size_t)M * w->N * 2;
+  const size_t xb = (size_t)M * w->K * 2, yb = (size_t)M * (w->glu ? w->N / 2 : w->N) * 2;
   if (xb > ctx->dx_cap || yb > ctx->dy_cap) {
     // growing frees the old staging buffers: wait for work that may still use them
     cudaError_t e = cudaDeviceSynchronize();
@@ -920,7 +953,8 @@ int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, in
   if (M == 0) return S4_OK;
   if (!x || ldx < w->K || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(x) & 15))
     return fail(S4_ERR_INVALID, "x must be 16-byte aligned with ldx >= K and ldx*2 a multiple of 16");
-  if (ldy < 1 || col0 < 0 || (long long)col0 + w->N > ldy) return fail(S4_ERR_INVALID, "output slice outside the row");
+  const int ycols = w->glu ? w->N / 2 : w->N;
+  if (ldy < 1 || col0 < 0 || (long long)col0 + ycols > ldy) return fail(S4_ERR_INVALID, "output slice outside the row");
   for (int d = 0; d < ndst; ++d)
     if (!dst[d]) return fail(S4_ERR_INVALID, "NULL destination %d", d);
   DeviceGuard guard(ctx->device);
@@ -929,7 +963,7 @@ int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, in
   cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, w->wb, static_cast<const __half*>(x), ldx,
                                         reinterpret_cast<__half* const*>(dst), ndst, ldy, col0, ctx->partials,
                                         ctx->tickets, kMaxTickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tn,
-                                        ctx->sm_count, static_cast<cudaStream_t>(stream), ctx->pdl, false);
+                                        ctx->sm_count, static_cast<cudaStream_t>(stream), ctx->pdl, false, w->glu);
   if (e != cudaSuccess) return cuda_fail(e, "gathered tc gemm launch");
   ++ctx->launches;
   return S4_OK;

@@ -5,7 +5,6 @@
 
 namespace s4 {
 
-__device__ __forceinline__ float silu_mul_f32(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
 // Vector path: I % 8 == 0, one thread per 8 outputs (16-byte loads and stores).
 __global__ void silu_mul_vec8_kernel(const __half* __restrict__ big, __half* __restrict__ mid, int M, int I) {

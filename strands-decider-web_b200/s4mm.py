@@ -44,6 +44,7 @@ _SIGS = {
     "s4_weight_upload_format": (C.c_int, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint32,
                                           C.POINTER(_P)]),
     "s4_fwht": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, _P]),
+    "s4_weight_upload_glu": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.c_uint32, C.POINTER(_P)]),
     "s4_weight_free": (C.c_int, [_P]),
     "s4_weight_save": (C.c_int, [_P, C.c_char_p]),
     "s4_weight_load": (C.c_int, [_P, C.c_char_p, C.POINTER(_P)]),
@@ -237,6 +238,21 @@ class Context:
                 raise S4Error(ERR_INVALID, f"packed/scales sizes do not match N={N} K={K}")
             _check(_lib.s4_weight_upload(self.handle, p.ctypes.data, s.ctypes.data, N, K, 0, C.byref(h)))
         return Weight(self, h.value, N, K)
+
+    def upload_glu(self, packed, scales, I: int, K: int) -> Weight:
+        """Upload a fused gate|up weight ([2I][K] MatMulNBits bytes, gate rows first) whose matmul
+        writes silu(gate) * up, [M][I] (``s4_weight_upload_glu``). Host arrays or CUDA tensors."""
+        h = _P()
+        if hasattr(packed, "is_cuda") and packed.is_cuda:
+            _check(_lib.s4_weight_upload_glu(self.handle, packed.data_ptr(), scales.data_ptr(), I, K, UPLOAD_DEVICE,
+                                             C.byref(h)))
+        else:
+            p = np.ascontiguousarray(np.asarray(packed, dtype=np.uint8))
+            s = np.ascontiguousarray(np.asarray(scales, dtype=np.float16))
+            if p.size != 2 * I * (K // 32) * 16 or s.size != 2 * I * (K // 32):
+                raise S4Error(ERR_INVALID, f"packed/scales sizes do not match 2I={2 * I} K={K}")
+            _check(_lib.s4_weight_upload_glu(self.handle, p.ctypes.data, s.ctypes.data, I, K, 0, C.byref(h)))
+        return Weight(self, h.value, I, K)
 
     def upload_wire(self, packed, wire, N: int, K: int) -> Weight:
         """Upload int4 bytes with download-format scales (``wire``: 4*N header bytes then N*(K/32)
