@@ -558,10 +558,10 @@ def run_stack(args, rank, world, local_rank):
     fused = None
     if args.workload == "stack":
         if args.gather == "fused":
-            fused = serve.FusedColshardStack(ctx, None, rank, world)
+            fused = serve.FusedColshardStack(ctx, None, rank, world, fuse_silu=bool(args.fuse_silu))
             stack = fused.stack
         else:
-            stack = serve.CudaStack(ctx, rank=rank, world=world)
+            stack = serve.CudaStack(ctx, rank=rank, world=world, fuse_silu=bool(args.fuse_silu))
         x = torch.from_numpy(np.random.default_rng(0).standard_normal((2048, serve.HIDDEN)).astype(np.float16)).to(dev)
         timing = {"on": False}
 
@@ -583,7 +583,7 @@ def run_stack(args, rank, world, local_rank):
         tokens_per_step = 2048 * 1  # the prompt, whatever the number of ranks (strong scaling)
         label = f"config4_stack_2048_prompt_colshard_{args.gather}"
     else:
-        stack = serve.CudaStack(ctx)  # weights replicated on every rank
+        stack = serve.CudaStack(ctx, fuse_silu=bool(args.fuse_silu))  # weights replicated on every rank
         lengths = serve.request_lengths(4096)[: args.requests]
         mine = serve.lpt_shard(lengths, world)[rank]
         chunks = serve.pack_chunks(lengths[mine], 8192)
@@ -667,6 +667,7 @@ def run_stack(args, rank, world, local_rank):
                          "note": "whole-stack FLOP rate (2 x weight parameters per token), all kernels included"},
             "gather_share": comm_share,
             "cuda_graph": bool(args.workload == "stack" and args.graph),
+            "silu_mul": "in the gate|up GEMM epilogue" if args.fuse_silu else "separate kernel",
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
@@ -795,6 +796,8 @@ def main():
                          "call NCCL all-gather after every projection")
     ap.add_argument("--graph", type=int, default=1,
                     help="stack: replay the whole forward as one CUDA graph (1, default) or launch eagerly (0)")
+    ap.add_argument("--fuse-silu", type=int, default=1,
+                    help="stack/serve: SiLU*mul in the gate|up GEMM epilogue (1, default) or as its own kernel (0)")
     ap.add_argument("--requests", type=int, default=512,
                     help="serve: number of config-5 requests timed per step (the first n of the seeded 4096)")
     args = ap.parse_args()

@@ -123,7 +123,7 @@ def gathered_to_rows(g, M: int, world: int, ns: int):
 class Ops:
     """The operators a stack forward needs; CUDA kernels + NCCL, or the CPU oracle + gloo."""
     matmul: object      # (x [M,K] f16, weight handle) -> y [M,N] f16
-    silu_mul: object    # (big [M, 2I] f16, I) -> mid [M, I] f16
+    silu_mul: object    # (big [M, 2I] f16, I) -> mid [M, I] f16; None: the gate_up matmul already wrote mid
     all_gather: object  # (local [M, ns]) -> [world][M][ns] stacked (None when world == 1)
     add_norm: object    # (x f32 [M, D], y f16 or None) -> (x + y f32, rmsnorm(x + y) f16)
     cols: object        # (x, c0, c1) -> contiguous x[:, c0:c1]
@@ -154,7 +154,7 @@ def stack_forward(x, layers, ops: Ops, world: int = 1, timers=None):
         y = gather(ops.matmul(ops.cols(a, 0, HIDDEN), w["out_proj"]))
         x, h = ops.add_norm(x, y)                                   # post_norm (engine.js:277)
         gu = ops.matmul(h, w["gate_up"])
-        mid = gather(ops.silu_mul(gu, gu.shape[1] // 2))
+        mid = gather(gu if ops.silu_mul is None else ops.silu_mul(gu, gu.shape[1] // 2))
         y = gather(ops.matmul(mid, w["down"]))
     x, h = ops.add_norm(x, y)                                       # final norm (engine.js:284)
     return h
@@ -187,11 +187,15 @@ def projection_seed(layer: int, name: str) -> int:
 
 
 class CudaStack:
-    """The stack's weights uploaded through the C ABI, optionally as this rank's column shard."""
+    """The stack's weights uploaded through the C ABI, optionally as this rank's column shard.
+    With ``fuse_silu`` (default) every gate|up projection is uploaded as a fused weight whose matmul
+    writes SiLU*mul directly (``s4_weight_upload_glu``), so no separate SiLU*mul pass runs."""
 
-    def __init__(self, ctx, n_layers: int = N_LAYERS, rank: int = 0, world: int = 1, device=None, host_gen=False):
+    def __init__(self, ctx, n_layers: int = N_LAYERS, rank: int = 0, world: int = 1, device=None, host_gen=False,
+                 fuse_silu: bool = True):
         import torch
         self.ctx, self.rank, self.world = ctx, rank, world
+        self.fuse_silu = fuse_silu
         self.device = device or torch.device("cuda", ctx.device)
         self.layers = []
         self.n_layers = n_layers
@@ -207,7 +211,10 @@ class CudaStack:
                 if world > 1:
                     rows = torch.from_numpy(shard_rows(name, N, rank, world)).to(self.device)
                     packed, scales = packed.index_select(0, rows).contiguous(), scales.index_select(0, rows).contiguous()
-                ws[name] = ctx.upload(packed, scales, packed.shape[0], K)
+                if name == "gate_up" and fuse_silu:  # rows: the rank's gate slice, then its up slice
+                    ws[name] = ctx.upload_glu(packed, scales, packed.shape[0] // 2, K)
+                else:
+                    ws[name] = ctx.upload(packed, scales, packed.shape[0], K)
                 del packed, scales
             self.layers.append(ws)
 
@@ -225,7 +232,7 @@ class CudaStack:
             return x, ctx.add_rmsnorm(x, y)
 
         return Ops(matmul=lambda x, w: ctx.matmul(x, w),
-                   silu_mul=lambda big, I: ctx.silu_mul(big, I),
+                   silu_mul=None if self.fuse_silu else (lambda big, I: ctx.silu_mul(big, I)),
                    all_gather=all_gather,
                    add_norm=add_norm,
                    cols=lambda x, c0, c1: x[:, c0:c1].contiguous(),
@@ -256,12 +263,13 @@ class FusedColshardStack:
     its column slice into all ranks' buffers over NVLink while it computes. A bounded flag barrier
     between projections orders the writes before the next projection reads them."""
 
-    def __init__(self, ctx, group, rank: int, world: int, max_tokens: int = 2048, n_layers: int = N_LAYERS):
+    def __init__(self, ctx, group, rank: int, world: int, max_tokens: int = 2048, n_layers: int = N_LAYERS,
+                 fuse_silu: bool = True):
         import torch
         import torch.distributed as dist
         self.ctx, self.group, self.rank, self.world = ctx, group, rank, world
         self.device = torch.device("cuda", ctx.device)
-        self.stack = CudaStack(ctx, n_layers, rank, world, self.device)
+        self.stack = CudaStack(ctx, n_layers, rank, world, self.device, fuse_silu=fuse_silu)
         self.max_tokens = max_tokens
         self.widths = {"a": N_LINEAR_IN, "b": HIDDEN, "mid": INTER, "d": HIDDEN}
         sizes = {k: max_tokens * w * 2 for k, w in self.widths.items()}
@@ -308,8 +316,11 @@ class FusedColshardStack:
             ctx.matmul_gather(self.local["a"], nin, M, w["out_proj"], self.ptrs["b"], HIDDEN, r * (HIDDEN // g))
             self.barrier()
             ctx.add_rmsnorm(xs, self._view("b", M, HIDDEN), h=h)        # post_norm
-            gu = ctx.matmul(h, w["gate_up"], M, self.gu[:M])
-            ctx.silu_mul_gather(gu, INTER // g, self.ptrs["mid"], INTER, r * (INTER // g))
+            if self.stack.fuse_silu:  # SiLU*mul in the GEMM epilogue, stored into every rank's buffer
+                ctx.matmul_gather(h.data_ptr(), HIDDEN, M, w["gate_up"], self.ptrs["mid"], INTER, r * (INTER // g))
+            else:
+                gu = ctx.matmul(h, w["gate_up"], M, self.gu[:M])
+                ctx.silu_mul_gather(gu, INTER // g, self.ptrs["mid"], INTER, r * (INTER // g))
             self.barrier()
             ctx.matmul_gather(self.local["mid"], INTER, M, w["down"], self.ptrs["d"], HIDDEN, r * (HIDDEN // g))
             self.barrier()
