@@ -50,12 +50,13 @@ constexpr int kChainStagerWarp = 9;
 constexpr int kChainPublisherWarp = 10;
 constexpr int kChainReducerWarp = 11;
 constexpr int kChainThreads = 12 * 32;
-constexpr int kChainGroup = 4;  // chunks per ring slot (and per consumer batch)
+constexpr int kChainGroup = 8;  // chunks per ring slot (and per consumer batch: 8 independent tiles in
+                                // flight per consumer warp; 4 left the warps waiting on dependencies)
 constexpr int kChainSlotBytes = kChainGroup * (kChunkWBytes + kChunkSBytes);
 constexpr int kChainSlotScales = kChainGroup * kChunkWBytes;  // scales follow the nibbles in a slot
 constexpr int kChainMaxSlots = 16;
-constexpr int kChainMinSlots = 3;
-constexpr int kChainPreferSlots = 7;   // 126 KB of weights in flight per SM before more windows
+constexpr int kChainMinSlots = 2;
+constexpr int kChainPreferSlots = 3;   // 110 KB of weights in flight per SM before more windows
 constexpr int kChainMaxWindows = 8;
 constexpr int kChainPhaseWindow = 36 * 1024;  // largest whole-K activation window of an op sharing a phase
 constexpr int kChainCachedOps = 64;  // op descriptors kept in shared memory
@@ -253,12 +254,21 @@ __device__ bool chain_consume(const ChainOp& op, const ChainRange& r, const Chai
     const uint8_t* ch = sm.ring + slot * kChainSlotBytes;
     uint4 wv[kChainGroup];
     uint2 sc[kChainGroup];
+    const uint8_t* wl = ch + sub * 512 + lane * 16;
+    const uint8_t* sl = ch + kChainSlotScales + sub * 64 + g * 8;
+    if (n == kChainGroup) {
 #pragma unroll
-    for (int j = 0; j < kChainGroup; ++j) {
-      if (j < n) {
-        wv[j] = *reinterpret_cast<const uint4*>(ch + j * kChunkWBytes + sub * 512 + lane * 16);
-        sc[j] = *reinterpret_cast<const uint2*>(ch + kChainSlotScales + j * kChunkSBytes + sub * 64 + g * 8);
+      for (int j = 0; j < kChainGroup; ++j) {
+        wv[j] = *reinterpret_cast<const uint4*>(wl + j * kChunkWBytes);
+        sc[j] = *reinterpret_cast<const uint2*>(sl + j * kChunkSBytes);
       }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kChainGroup; ++j)
+        if (j < n) {
+          wv[j] = *reinterpret_cast<const uint4*>(wl + j * kChunkWBytes);
+          sc[j] = *reinterpret_cast<const uint2*>(sl + j * kChunkSBytes);
+        }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(sm.empty + slot);

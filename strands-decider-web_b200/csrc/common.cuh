@@ -136,6 +136,15 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Same with C = 0: d = A * B (no registers to clear first).
+__device__ __forceinline__ void mma_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
 // ---- int4 -> fp16 ---------------------------------------------------------------------------------
 // Device word layout: nibbles 0-3 hold k0,k2,k4,k6 and nibbles 4-7 hold k1,k3,k5,k7 of eight
 // consecutive K values of one row. Output h[i] = half2(k_{2i} - 8, k_{2i+1} - 8), exact.

@@ -24,8 +24,8 @@ __device__ __forceinline__ void gemv_tile(const uint4 w, const uint2 sc, const u
       uint4 xv = make_uint4(0, 0, 0, 0);
       if (xok[mg] && (blk == 0 || kin1))
         xv = *reinterpret_cast<const uint4*>(xrow + mg * xgroup + blk * 64);
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma_16816(d, ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
+      float d[4];
+      mma_16816_zero(d, ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
       mma_16816(d, ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
       acc[mg][0] = fmaf(sg, d[0], acc[mg][0]);
       acc[mg][1] = fmaf(sg, d[1], acc[mg][1]);
@@ -57,8 +57,8 @@ __device__ __forceinline__ void gemv_tile_rows(const uint4 w, const uint2 sc, co
     const float sg = blk ? s1.x : s0.x, sg8 = blk ? s1.y : s0.y;
 #pragma unroll
     for (int mg = 0; mg < MG; ++mg) {
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma_16816(d, ha[0], hb[0], ha[1], hb[1], xv[mg][blk].x, xv[mg][blk].y);
+      float d[4];
+      mma_16816_zero(d, ha[0], hb[0], ha[1], hb[1], xv[mg][blk].x, xv[mg][blk].y);
       mma_16816(d, ha[2], hb[2], ha[3], hb[3], xv[mg][blk].z, xv[mg][blk].w);
       acc[mg][0] = fmaf(sg, d[0], acc[mg][0]);
       acc[mg][1] = fmaf(sg, d[1], acc[mg][1]);
