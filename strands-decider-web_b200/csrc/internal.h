@@ -48,6 +48,7 @@ struct s4_ctx {
   s4::Bucket forced{0, S4_FAMILY_AUTO, 0, 0};
   uint64_t launches = 0;
   bool pdl = true;    // launch with programmatic dependent launch (env S4_PDL=0 turns it off)
+  bool ticket_fixup = false;  // split tcgen05 tiles summed by their last CTA in-kernel (env S4_TICKET_FIXUP=1)
 };
 
 struct s4_weight {

@@ -320,6 +320,7 @@ int s4_init(int device, s4_ctx** out) {
   ctx->sm_count = prop.multiProcessorCount;
   ctx->table = default_table();
   if (const char* v = getenv("S4_PDL")) ctx->pdl = (v[0] != '0');
+  if (const char* v = getenv("S4_TICKET_FIXUP")) ctx->ticket_fixup = (v[0] == '1');
   e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
   const size_t part_bytes = s4::tc_partials_bytes(ctx->sm_count);
   if (e == cudaSuccess) e = cudaMalloc(&ctx->partials, part_bytes);
@@ -753,7 +754,8 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
       const int rows = (int)std::min<long long>(rows_cap, M - r0);
       e = s4::launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x) + r0 * w->K,
                              static_cast<__half*>(y) + r0 * (w->glu ? w->N / 2 : w->N), ctx->partials, ctx->tickets,
-                             kMaxTickets, ctx->err, rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl, false,
+                             kMaxTickets, ctx->err, rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl,
+                             ctx->ticket_fixup && !w->glu,
                              w->glu);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
       ++ctx->launches;
