@@ -63,3 +63,19 @@ def test_missing_library_is_loud(pkg, tmp_path):
             pkg.s4mm.load_library(str(tmp_path / "missing.so"))
     finally:
         pkg.s4mm._lib = saved
+
+
+def test_new_entry_points_reject_null_arguments(pkg, tmp_path):
+    """The format, wire, FWHT, fused gate|up and cache entry points fail with a status on NULL handles
+    before touching a device."""
+    lib = pkg.load_library()
+    h = C.c_void_p()
+    INV = pkg.s4mm.ERR_INVALID
+    assert lib.s4_weight_upload_format(None, None, None, None, 16, 64, 2, 32, 0, C.byref(h)) == INV
+    assert lib.s4_weight_upload_glu(None, None, None, 64, 64, 0, C.byref(h)) == INV
+    assert lib.s4_weight_upload_wire(None, None, None, 16, 64, 0, C.byref(h)) == INV
+    assert lib.s4_decode_wire_scales(None, None, 4, 4, None, None) == INV
+    assert lib.s4_fwht(None, None, 1, 64, 64, None) == INV
+    assert lib.s4_weight_save(None, str(tmp_path / "w").encode()) == INV
+    assert lib.s4_weight_load(None, str(tmp_path / "w").encode(), C.byref(h)) == INV
+    assert b"NULL" in lib.s4_last_error()
