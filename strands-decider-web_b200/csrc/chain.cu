@@ -621,6 +621,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     fence_mbar_init();
     s_fail = 0;
   }
+  __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole after its role code
   __syncthreads();
   // Launched with programmatic stream serialization, the next grid in the stream may start its
   // CTAs as ours exit. Only the producer runs before the previous grid has completed: it reads
@@ -755,6 +756,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     set_error(p.err, kErrWaitTimeout);
     s_fail = 1;
   }
+  __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole after its role code
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();

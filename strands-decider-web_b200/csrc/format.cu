@@ -68,6 +68,7 @@ __global__ void fwht_kernel(__half* __restrict__ a, int n, float c) {
   pdl_wait();
   const int64_t o = (int64_t)blockIdx.x * n;
   for (int e = threadIdx.x; e < n; e += blockDim.x) fw_sh[e] = __half2float(a[o + e]);
+  __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole
   __syncthreads();
   for (int h = 1; h < n; h <<= 1) {
     for (int p = threadIdx.x; p < n / 2; p += blockDim.x) {
@@ -76,6 +77,7 @@ __global__ void fwht_kernel(__half* __restrict__ a, int n, float c) {
       fw_sh[i] = __fadd_rn(x, y);
       fw_sh[i + h] = __fsub_rn(x, y);
     }
+    __syncwarp();
     __syncthreads();
   }
   pdl_launch_dependents();

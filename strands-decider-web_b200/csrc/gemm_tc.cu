@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole after its role code
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -553,6 +554,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     }
   }
 
+  __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole after its role code
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

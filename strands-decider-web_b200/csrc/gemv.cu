@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
       *reinterpret_cast<uint4*>(xs + r * p.xrow + c * 16) = v;
     }
   }
+  __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole after its role code
   __syncthreads();  // also orders the mbarrier initialisation before the waits below
 
   bool xok[MG];

@@ -27,6 +27,7 @@ __global__ void peer_barrier_kernel(FlagList flags, int nranks, int rank, uint32
     s_epoch = epoch;
   }
   __threadfence_system();  // this GPU's earlier peer stores (previous kernels) before the signal
+  __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole after its role code
   __syncthreads();
   epoch = s_epoch;
   if (q < nranks)
@@ -45,6 +46,7 @@ __global__ void peer_barrier_kernel(FlagList flags, int nranks, int rank, uint32
       __nanosleep(64);
     }
   }
+  __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole after its role code
   __syncthreads();
 }
 
