@@ -571,6 +571,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
 __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcParams p) {
   __shared__ float up_s[64][8];  // fused gate|up weight: the up rows' sums
   pdl_wait();  // the partials come from the GEMM launched just before
+  // the next kernel may start its prologue and weight prefetch now; it reads this kernel's output
+  // only after its own grid-dependency wait, which waits for this grid to complete
+  pdl_launch_dependents();
   const int b = blockIdx.x, KT = p.ktiles;
   const int cb = tc_begin(b, p);
   if (b == 0 || cb % KT == 0) return;
