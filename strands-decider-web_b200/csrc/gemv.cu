@@ -142,6 +142,11 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
   for (int mg = 0; mg < MG; ++mg) xok[mg] = (mg * 8 + g) < rows;
   const int xgroup = 8 * p.xrow;
   const uint8_t* xl = xs + g * p.xrow + 16 * t;  // lane's row, k offset 8t (blk adds 64 bytes)
+  // symmetric path: one row pointer per token group; a token past the staged rows reads the last
+  // staged row (its outputs are never stored) and K past the end is staged as zeros, so no predicates
+  const uint8_t* xr[MG];
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg) xr[mg] = xs + min(mg * 8 + g, rows - 1) * p.xrow + 16 * t;
   const uint8_t* wl = wsm + sub * 512 + lane * 16;
   const uint8_t* sl = ssm + sub * 64 + g * 8;
   float acc[MG][4];
@@ -162,7 +167,10 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
           const uint2 bi = *reinterpret_cast<const uint2*>(sl + (p.b_off - p.s_off) + kk * kChunkSBytes);
           gemv_tile_asym<MG>(w, sc, bi, xl + kk * 128, xgroup, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
         } else {
-          gemv_tile<MG>(w, sc, xl + kk * 128, xgroup, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
+          const uint8_t* xj[MG];
+#pragma unroll
+          for (int mg = 0; mg < MG; ++mg) xj[mg] = xr[mg] + kk * 128;
+          gemv_tile_rows<MG>(w, sc, xj, acc);
         }
       }
     }
