@@ -37,6 +37,7 @@ SHAPES = [("qkvz_ab", 2048, 8224), ("attn_qkv", 2048, 3072), ("gate_up", 2048, 1
 MS = [1, 2, 4, 8]
 COPIES = 8
 BLOCK = 8 * COPIES  # chained launches per replayed graph in the device-timed loop
+NSETS = 4           # bound input/output buffer sets (and end-to-end streams), used round robin
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
@@ -255,13 +256,12 @@ def run_ours(args, rank, world, local_rank):
     # bound buffer sets (inputs and outputs). The device-timed steps follow one another on one
     # stream as programmatic dependent launches: a step's CTAs start, and stream their first
     # weights, as the previous step's CTAs exit.
-    xbuf2 = torch.empty_like(xbuf)
-    ybuf2 = torch.empty_like(ybuf)
-    xbuf2.copy_(xbuf)
-    sets = [(xbuf, ybuf), (xbuf2, ybuf2)]
+    sets = [(xbuf, ybuf)]
+    for _ in range(NSETS - 1):
+        sets.append((xbuf.clone(), torch.empty_like(ybuf)))
     chains = []
     for rot in range(COPIES):
-        xb_, yb_ = sets[rot % 2]
+        xb_, yb_ = sets[rot % NSETS]
         ops, xo, yo = [], 0, 0
         for mi, M in enumerate(MS):   # the slice order of xbuf / ybuf (M-major, then shape)
             for name, K, N in SHAPES:
@@ -269,7 +269,7 @@ def run_ours(args, rank, world, local_rank):
                 xo += M * K
                 yo += M * N
         chains.append(ctx.chain(ops))
-    step_streams = [stream, torch.cuda.Stream(dev)]
+    step_streams = [stream] + [torch.cuda.Stream(dev) for _ in range(NSETS - 1)]
 
     def sweep(rot: int, st):
         # the same 16 matmuls as one launch each (the per-call path, s4_matmul)
@@ -360,16 +360,17 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- e2e: the same sweep through the host-buffer C-ABI entry point ------------------------------
     # Every step: its inputs from pinned host memory, one chained launch, its outputs back to pinned
-    # host memory (s4_chain_run_host), on the step's stream and buffer set as above, so one step's
-    # copies overlap the other step's launch. Each rotation's call is captured once in a CUDA graph
-    # (copies included) and replayed, so the host's call rate does not pace the steps.
-    hx = [xbuf.cpu().pin_memory(), xbuf.cpu().pin_memory()]
-    hy = [torch.empty(ybuf.shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+    # host memory (s4_chain_run_host), on the stream of its buffer set (NSETS round robin), so a step's
+    # copies overlap the following steps' launches and have NSETS - 1 steps to finish before their
+    # buffers are reused. Each rotation's call is captured once in a CUDA graph (copies included) and
+    # replayed, so the host's call rate does not pace the steps.
+    hx = [xbuf.cpu().pin_memory() for _ in range(NSETS)]
+    hy = [torch.empty(ybuf.shape, dtype=torch.float16).pin_memory() for _ in range(NSETS)]
     e2e_streams = step_streams
     e2e_graphs = []
     with torch.cuda.stream(cap_stream):
         for rot in range(COPIES):
-            k = rot % 2
+            k = rot % NSETS
             chains[rot].run_host(hx[k], sets[k][0], hy[k], sets[k][1], cap_stream)  # eager once
             cap_stream.synchronize()
             g = torch.cuda.CUDAGraph()
@@ -380,7 +381,7 @@ def run_ours(args, rank, world, local_rank):
 
     def e2e_step():
         r = counter[0]
-        with torch.cuda.stream(e2e_streams[r % 2]):
+        with torch.cuda.stream(e2e_streams[r % NSETS]):
             e2e_graphs[r % COPIES].replay()
         counter[0] += 1
 
@@ -390,10 +391,12 @@ def run_ours(args, rank, world, local_rank):
     counter[0] = 0
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
-    e2e_streams[1].wait_event(e2)
+    for st_ in e2e_streams[1:]:
+        st_.wait_event(e2)
     for _ in range(args.steps):
         e2e_step()
-    stream.wait_stream(e2e_streams[1])
+    for st_ in e2e_streams[1:]:
+        stream.wait_stream(st_)
     e3.record(stream)
     barrier()
     ms_e2e = max_over_ranks(e2.elapsed_time(e3))
@@ -512,8 +515,8 @@ def run_ours(args, rank, world, local_rank):
                          "kernel": "chain_kernel", "launch_us_avg": avg_launch_us},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "s4_chain_run_host every step (pinned host x -> device, one chained launch, device -> "
-                           "pinned host y), each rotation's call replayed from a CUDA graph; consecutive steps on "
-                           "two streams with two bound buffer sets"},
+                           "pinned host y), each rotation's call replayed from a CUDA graph; steps round robin over "
+                           "four streams with four bound buffer sets"},
             "per_launch_sweep": {"value": per_launch_value, "unit": "GB/s",
                                  "note": "the same 16 matmuls as 16 s4_matmul launches (decode GEMV kernel)"},
             "cpu_baseline": cpu,
