@@ -24,7 +24,7 @@ def test_glu_matches_oracle_and_unfused(ctx, I, K):
     Wp = ctx.upload(packed, scales, 2 * I, K)
     assert W.N == I
     deq = s4ref.dequant(packed, scales)
-    for M in (1, 5, 16, 17, 300, 2048):
+    for M in (1, 5, 16, 17, 300, 512, 2048):  # 512: two whole waves of 176-token tiles (I = 6144)
         x = s4ref.config_x(rng, M, K)
         xd = torch.from_numpy(x).cuda()
         y = ctx.matmul(xd, W)

@@ -85,3 +85,16 @@ def test_tc_and_gemv_agree(ctx, shapes):
     ctx.force("auto")
     _check(b, a.astype(np.float32), "tc vs gemv")
     assert ctx.check_errors() == 0
+
+
+@pytest.mark.parametrize("K,N,M", [(6144, 2048, 2048), (2048, 2048, 2048), (2048, 12288, 512), (2048, 12288, 768)])
+def test_whole_wave_tile_shapes(ctx, K, N, M):
+    """Automatic shapes that pack whole tiles into whole waves: one wave of 240-token tiles (16 n-blocks
+    at M = 2048) and two exact waves of 176- / 256-token tiles (96 n-blocks at M = 512 / 768)."""
+    rng = np.random.default_rng(K + N + M)
+    packed, scales = s4ref.config_weights(rng, K, N)
+    W = ctx.upload(packed, scales, N, K)
+    x = s4ref.config_x(rng, M, K)
+    _, ref = s4ref.matmul(x, packed, scales)
+    _check(_run(ctx, W, x), ref, f"K={K} N={N} M={M}")
+    W.free()
