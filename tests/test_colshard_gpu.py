@@ -81,11 +81,12 @@ def _rank_main(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_fused_and_nccl_colshard_match_single_gpu():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4])
+def test_fused_and_nccl_colshard_match_single_gpu(world):
+    """Two and four ranks (narrower slices per rank: 24 gate|up n-blocks at four)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from oracle import s4ref
-    world = 2
     mp = torch.multiprocessing.get_context("spawn")
     q = mp.Queue()
     port = _free_port()
@@ -103,7 +104,8 @@ def test_fused_and_nccl_colshard_match_single_gpu():
         np.testing.assert_array_equal(res[r]["fused"], res[r]["graph"])
         ok, mr, mc = s4ref.check(res[r]["fused"], ref)
         assert ok, (r, mr, mc)
-    np.testing.assert_array_equal(res[0]["fused"], res[1]["fused"])
+    for r in range(1, world):
+        np.testing.assert_array_equal(res[0]["fused"], res[r]["fused"])
     for key in ("b", "d"):
         got, want = res[0][key]
         ok, mr, mc = s4ref.check(got, want.astype(np.float32))
