@@ -851,19 +851,36 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     }
   }
   const int nstatic = dyn_op >= 0 ? nops - 1 : nops;
-  // phases: runs of consecutive ops none of which reads another op of the run; an op whose whole-K
-  // activation window would exceed kChainPhaseWindow stays alone (its range within a shared phase
-  // could span whole n-blocks, i.e. all of K)
+  // phases: runs of consecutive ops none of which reads another op of the run. An op whose whole-K
+  // activation window would exceed kChainPhaseWindow ("big") never shares a phase with the others
+  // (its range within a merged phase could span whole n-blocks, i.e. all of K); consecutive big ops
+  // share one while every op's window for the phase's per-CTA range still fits: a CTA then streams
+  // one longer range instead of one short range per op (fewer part-filled ring slots, windows and
+  // split-K parts per n-block).
   std::vector<int> phase_start(nops);
   {
+    auto is_big = [&](const ChainOp& o) { return o.M * (o.ktiles * 128 + 64) > kChainPhaseWindow; };
     int start = 0;
+    long long U = 0;  // chunks of the current phase so far
     for (int i = 0; i < nstatic; ++i) {
       const ChainOp& o = ops[i];
-      const int wfull = o.M * (o.ktiles * 128 + 64);
-      const bool big = wfull > kChainPhaseWindow;
-      const bool prev_big = i > 0 && ops[i - 1].M * (ops[i - 1].ktiles * 128 + 64) > kChainPhaseWindow;
-      if (i == 0 || o.dep >= start || big || prev_big) start = i;
+      const long long Uo = (long long)o.nblk * o.ktiles;
+      bool join = i > 0 && o.dep < start && is_big(o) == is_big(ops[i - 1]);
+      if (join && is_big(o)) {
+        const long long U2 = U + Uo;
+        const long long Gp = U2 < G ? U2 : G;
+        const long long per_cta = (U2 + Gp - 1) / Gp;
+        for (int q = start; q <= i && join; ++q) {
+          const long long n_win = per_cta < ops[q].ktiles ? per_cta : ops[q].ktiles;
+          join = (long long)ops[q].M * (n_win * 128 + 64) <= kChainPhaseWindow;
+        }
+      }
+      if (!join) {
+        start = i;
+        U = 0;
+      }
       phase_start[i] = start;
+      U += Uo;
     }
   }
   for (int i = 0; i < nstatic;) {
