@@ -8,15 +8,15 @@
 //
 //  * producer (warp 8, one lane): streams the CTA's weight chunks (128 rows x 64 K: 4096 bytes of
 //    nibbles + 512 bytes of scales, contiguous in the repacked layout) into a ring of shared-memory
-//    slots, four consecutive chunks per slot with two 1-D bulk copies (16 KB of nibbles, 2 KB of
+//    slots, eight consecutive chunks per slot with two 1-D bulk copies (32 KB of nibbles, 4 KB of
 //    scales; TMA engine, no multicast), op after op without a pause. Copy size matters: the bytes
 //    an SM keeps in flight grow with it (4.6 KB copies streamed at under half the rate);
 //  * stager (warp 9, one lane): per op, waits until the op it depends on is complete (if any), then
 //    fetches the op's activation window into one of two shared-memory buffers with at most two bulk
 //    copies per activation row, one op ahead of the consumers (16-byte pieces from every CTA at
 //    once made the window of an 8-row op take ~4 us);
-//  * consumers (warps 0-7, one 16-row sub-tile each): only the tile math of gemv_tile.cuh, four
-//    chunks per batch. At the end of an n-block segment they leave their fp32 sums in shared memory
+//  * consumers (warps 0-7, one 16-row sub-tile each): only the tile math of gemv_tile.cuh, one
+//    ring slot (eight chunks) per batch. At the end of an n-block segment they leave their fp32 sums in shared memory
 //    and move on: they never touch global memory, so they never wait for it;
 //  * publisher (warp 10): writes the consumers' finished segments to global memory (fp16 outputs,
 //    or fp32 partials of split n-blocks), then issues one gpu-scope fence for its own stores and
@@ -277,7 +277,7 @@ __device__ bool chain_consume(const ChainOp& op, const ChainRange& r, const Chai
       phase ^= 1u;
     }
     if (n == kChainGroup && kt + n <= KT && wpos + n <= KT && (kt + n) * 64 <= op.K) {
-      // fast path: four chunks in one n-block and one stretch of the window, all of K in range;
+      // fast path: a full slot in one n-block and one stretch of the window, all of K in range;
       // the tiles are independent, so the compiler can overlap their latencies
 #pragma unroll
       for (int j = 0; j < kChainGroup; ++j) {
