@@ -151,14 +151,15 @@ def cpu_setup():
     from oracle import s4ref
     torch.set_num_threads(os.cpu_count() or 1)
     rng = np.random.default_rng(0)
-    deqs, xs = {}, {}
+    deqs, packs, xs = {}, {}, {}
     for name, K, N in SHAPES:
         packed, scales = s4ref.config_weights(rng, K, N)
         deqs[name] = torch.from_numpy(s4ref.dequant(packed, scales))   # dequantised once (fake-quant)
+        packs[name] = (torch.from_numpy(packed), torch.from_numpy(scales))
     for M in MS:
         for name, K, N in SHAPES:
             xs[(M, name)] = torch.from_numpy(s4ref.config_x(rng, M, K).astype(np.float32))
-    return deqs, xs
+    return deqs, packs, xs
 
 
 def cpu_sweep_once(deqs, xs):
@@ -169,11 +170,21 @@ def cpu_sweep_once(deqs, xs):
                 (xs[(M, name)] @ deqs[name].T).to(torch.float16)
 
 
-def cpu_time(deqs, xs, seconds: float):
-    cpu_sweep_once(deqs, xs)  # warm
+def cpu_sweep_dequant_once(packs, xs):
+    """The same sweep dequantising every weight inside each call (int4 bytes in, fp32 math)."""
+    import torch
+    from oracle import s4ref
+    with torch.inference_mode():
+        for M in MS:
+            for name, K, N in SHAPES:
+                (xs[(M, name)] @ s4ref.dequant_torch(*packs[name]).T).to(torch.float16)
+
+
+def cpu_time(deqs, xs, seconds: float, sweep=cpu_sweep_once):
+    sweep(deqs, xs)  # warm
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu_sweep_once(deqs, xs)
+        sweep(deqs, xs)
         n += 1
         dt = time.perf_counter() - t0
         if dt >= seconds:
@@ -183,7 +194,7 @@ def cpu_time(deqs, xs, seconds: float):
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    deqs, xs = cpu_setup()
+    deqs, _, xs = cpu_setup()
     for _ in range(args.warmup):
         cpu_sweep_once(deqs, xs)
     t0 = time.perf_counter()
@@ -490,11 +501,15 @@ def run_ours(args, rank, world, local_rank):
     hbm, bf16, peak_kind = peaks()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        deqs, cxs = cpu_setup()
+        deqs, packs, cxs = cpu_setup()
         n, dt = cpu_time(deqs, cxs, args.cpu_seconds)
+        n2, dt2 = cpu_time(packs, cxs, args.cpu_seconds / 2, cpu_sweep_dequant_once)
         cpu = {"value": sweep_bytes() * n / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
                "sample": f"{n} full sweeps (16 matmuls each) in {dt:.1f} s, torch fp32 on weights dequantised once "
-                         f"(fake-quant route, export_engine.py:88-103)"}
+                         f"(fake-quant route, export_engine.py:88-103)",
+               "dequant_per_call": {"value": sweep_bytes() * n2 / dt2 / 1e9, "unit": "GB/s",
+                                    "sample": f"{n2} full sweeps in {dt2:.1f} s, every weight dequantised from its "
+                                              f"int4 bytes inside each call, then the same fp32 matmul"}}
 
     if rank == 0:
         per_launch_bytes = sweep_bytes()  # one chained launch moves the whole sweep

@@ -71,6 +71,18 @@ def dequant(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
     return (q * s).reshape(N, B * BLOCK)
 
 
+def dequant_torch(packed, scales):
+    """``dequant`` in torch (CPU tensors in, fp32 ``[N, K]`` out), for timing the dequantise-per-call
+    variant of the CPU baseline: the reference's own quantiser is torch code (export_engine.py:17-26),
+    byte i of a block holding elements 2i (low nibble) and 2i + 1 (high nibble)."""
+    import torch
+    p = torch.as_tensor(packed)
+    N, B, _ = p.shape
+    q = torch.stack((p & 0xF, p >> 4), dim=-1).reshape(N, B, BLOCK).to(torch.float32) - 8.0
+    s = torch.as_tensor(scales).to(torch.float32).unsqueeze(-1)
+    return (q * s).reshape(N, B * BLOCK)
+
+
 def matmul(x: np.ndarray, packed: np.ndarray, scales: np.ndarray, deq: np.ndarray | None = None):
     """The reference CPU path: fp32 dequantise-then-matmul, one fp16 rounding at the end.
 

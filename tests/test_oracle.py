@@ -49,6 +49,13 @@ def test_dequant_of_packed_equals_reference_deq(name):
     np.testing.assert_array_equal(deq, QZ[f"{name}/deq"])
 
 
+@pytest.mark.parametrize("name", QNAMES)
+def test_torch_dequant_equals_reference_deq(name):
+    """The torch restatement timed by the dequantise-per-call CPU baseline gives the reference's deq."""
+    deq = s4ref.dequant_torch(QZ[f"{name}/packed"], QZ[f"{name}/scales"]).numpy()
+    np.testing.assert_array_equal(deq, QZ[f"{name}/deq"])
+
+
 @pytest.mark.parametrize("name", MNAMES)
 def test_matmul_matches_reference_fake_quant(name):
     x = MZ[f"{name}/x"]
