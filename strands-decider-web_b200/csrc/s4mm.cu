@@ -7,8 +7,11 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <new>
 #include <string>
 #include <vector>
+
+#include <sys/types.h>
 
 #include "../../include/s4mm.h"
 #include "common.cuh"
@@ -627,7 +630,12 @@ uint64_t cache_checksum(const uint8_t* p, size_t n, uint64_t h) {
 int s4_weight_save(const s4_weight* w, const char* path) {
   if (!w || !path) return fail(S4_ERR_INVALID, "NULL argument");
   const size_t wb_bytes = w->wb ? w->ws_bytes : 0;
-  std::vector<uint8_t> buf(w->wq_bytes + w->ws_bytes + wb_bytes);
+  std::vector<uint8_t> buf;
+  try {
+    buf.resize(w->wq_bytes + w->ws_bytes + wb_bytes);
+  } catch (const std::bad_alloc&) {
+    return fail(S4_ERR_NOMEM, "out of host memory for the cache copy");
+  }
   {
     DeviceGuard guard(w->ctx->device);
     cudaError_t e = cudaMemcpy(buf.data(), w->wq, w->wq_bytes, cudaMemcpyDeviceToHost);
@@ -694,7 +702,25 @@ int s4_weight_load(s4_ctx* ctx, const char* path, s4_weight** out) {
     delete w;
     return fail(S4_ERR_IO, "%s: section sizes do not match N=%d K=%d", path, h.N, h.K);
   }
-  std::vector<uint8_t> buf(w->wq_bytes + w->ws_bytes + wb_bytes);
+  // the payload must be exactly the rest of the file: checked before any buffer is sized from the
+  // header, so a damaged or foreign header cannot ask for an arbitrary allocation
+  const size_t payload = w->wq_bytes + w->ws_bytes + wb_bytes;
+  const off_t here = ftello(f);
+  const bool sized = here >= 0 && fseeko(f, 0, SEEK_END) == 0 && ftello(f) - here == (off_t)payload &&
+                     fseeko(f, here, SEEK_SET) == 0;
+  if (!sized) {
+    fclose(f);
+    delete w;
+    return fail(S4_ERR_IO, "%s: truncated or corrupt payload", path);
+  }
+  std::vector<uint8_t> buf;
+  try {
+    buf.resize(payload);
+  } catch (const std::bad_alloc&) {
+    fclose(f);
+    delete w;
+    return fail(S4_ERR_NOMEM, "out of host memory for %s", path);
+  }
   const bool read_ok = fread(buf.data(), 1, buf.size(), f) == buf.size() && fgetc(f) == EOF;
   fclose(f);
   if (!read_ok || cache_checksum(buf.data(), buf.size(), 0xcbf29ce484222325ull) != h.checksum) {

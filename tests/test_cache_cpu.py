@@ -40,3 +40,39 @@ def test_prefix_and_prune(tmp_path):
     assert cache.prune() == 2
     assert sorted(os.listdir(tmp_path)) == sorted([pre + "a.s4w", "other.txt"])
     assert cache.path("layers.0/mlp.q") == os.path.join(str(tmp_path), pre + "layers.0_mlp.q.s4w")
+
+
+def _header(N, K, flags=0, wq=None, ws=None, wb=None, magic=0x4C573453, version=1):
+    import struct
+    nblk, kt = (N + 127) // 128, (K + 63) // 64
+    wq = nblk * kt * 4096 if wq is None else wq
+    ws = nblk * kt * 512 if ws is None else ws
+    wb = (ws if flags & 1 else 0) if wb is None else wb
+    return struct.pack("<IIiiIIQQQQQ", magic, version, N, K, flags, 0, wq, ws, wb, 0, 0)
+
+
+def test_load_rejects_bad_entries_before_allocating(tmp_path):
+    """s4_weight_load checks the header and the file length before sizing any buffer from the
+    header: a damaged entry whose header claims a 64 GB payload, a foreign file, inconsistent
+    sections or a short payload are S4_ERR_IO without host or device allocation. The validation
+    never dereferences the context, so a zeroed stand-in suffices here (no GPU)."""
+    import ctypes
+    pkg = load_package()
+    lib = pkg.load_library()
+    fake_ctx = ctypes.create_string_buffer(4096)
+    cases = {
+        "huge": _header(128, 1 << 30),                       # consistent sections, 64 GB claimed
+        "magic": _header(128, 2048, magic=0x12345678) + bytes(4608 * 32),
+        "flags": _header(128, 2048, flags=4) + bytes(4608 * 32),
+        "sections": _header(128, 2048, wq=4096) + bytes(4608 * 32),
+        "short": _header(128, 2048) + bytes(4608 * 32 - 1),
+        "long": _header(128, 2048) + bytes(4608 * 32 + 16),
+        "shape": _header(0, 2048),
+    }
+    for name, data in cases.items():
+        p = tmp_path / f"{name}.s4w"
+        p.write_bytes(data)
+        out = ctypes.c_void_p()
+        rc = lib.s4_weight_load(ctypes.addressof(fake_ctx), str(p).encode(), ctypes.byref(out))
+        assert rc == pkg.s4mm.ERR_IO, (name, rc, lib.s4_last_error())
+        assert not out.value, name
