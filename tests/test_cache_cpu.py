@@ -76,3 +76,38 @@ def test_load_rejects_bad_entries_before_allocating(tmp_path):
         rc = lib.s4_weight_load(ctypes.addressof(fake_ctx), str(p).encode(), ctypes.byref(out))
         assert rc == pkg.s4mm.ERR_IO, (name, rc, lib.s4_last_error())
         assert not out.value, name
+
+
+def _checksum(p, h=0xCBF29CE484222325):
+    """The cache payload checksum (FNV-1a style over little-endian 8-byte words, xor-shift per word)."""
+    m = (1 << 64) - 1
+    n, i = len(p), 0
+    while i + 8 <= n:
+        h = ((h ^ int.from_bytes(p[i:i + 8], "little")) * 0x100000001B3) & m
+        h ^= h >> 29
+        i += 8
+    w = int.from_bytes(p[i:] + bytes(8 - (n - i)), "little")
+    h = ((h ^ w ^ n) * 0x100000001B3) & m
+    return h ^ (h >> 29)
+
+
+def test_load_accepts_a_valid_entry_up_to_the_device(tmp_path):
+    """A well-formed entry passes every file check and stops only at the device upload (no GPU
+    here: S4_ERR_CUDA); the same entry with one payload byte flipped is S4_ERR_IO (checksum)."""
+    import ctypes
+    import struct
+    pkg = load_package()
+    lib = pkg.load_library()
+    fake_ctx = ctypes.create_string_buffer(4096)
+    payload = bytes((i * 37) & 0xFF for i in range(4608 * 32))
+    good = bytearray(_header(128, 2048) + payload)
+    struct.pack_into("<Q", good, 48, _checksum(payload))
+    bad = bytearray(good)
+    bad[64 + 1000] ^= 1
+    for name, data, want in (("good", good, pkg.s4mm.ERR_CUDA), ("flipped", bad, pkg.s4mm.ERR_IO)):
+        p = tmp_path / f"{name}.s4w"
+        p.write_bytes(bytes(data))
+        out = ctypes.c_void_p()
+        rc = lib.s4_weight_load(ctypes.addressof(fake_ctx), str(p).encode(), ctypes.byref(out))
+        assert rc == want, (name, rc, lib.s4_last_error())
+        assert not out.value, name
