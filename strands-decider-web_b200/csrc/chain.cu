@@ -36,6 +36,7 @@
 //
 // The launch is cooperative (all CTAs resident), so waiting on other CTAs of the grid cannot
 // deadlock. The last CTA to finish resets the completion counters for the next run.
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -971,7 +972,7 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
     delete c;
     return *why = "op table upload failed", S4_ERR_CUDA;
   }
-  c->ops = ops;
+  c->ops = std::move(ops);  // no allocation after the device buffers exist
   *out = c;
   return S4_OK;
 }

@@ -902,7 +902,12 @@ int s4_chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void
   }
   DeviceGuard guard(ctx->device);
   const char* why = nullptr;
-  const int rc = s4::chain_create(ctx, nops, w, x, y, M, dep, out, &why);
+  int rc;
+  try {  // host containers sized by nops: an allocation failure is a status, not an exception
+    rc = s4::chain_create(ctx, nops, w, x, y, M, dep, out, &why);
+  } catch (const std::bad_alloc&) {
+    return fail(S4_ERR_NOMEM, "chain: out of host memory");
+  }
   if (rc != S4_OK) return fail(rc, "chain: %s", why ? why : "failed");
   return S4_OK;
 }
@@ -1081,7 +1086,11 @@ int s4_set_table(s4_ctx* ctx, const char* json) {
   if (!ctx || !json) return fail(S4_ERR_INVALID, "NULL argument");
   std::vector<Bucket> t;
   std::string why;
-  if (!parse_table(json, t, why)) return fail(S4_ERR_INVALID, "dispatch table: %s", why.c_str());
+  try {
+    if (!parse_table(json, t, why)) return fail(S4_ERR_INVALID, "dispatch table: %s", why.c_str());
+  } catch (const std::bad_alloc&) {
+    return fail(S4_ERR_NOMEM, "dispatch table: out of host memory");
+  }
   for (const Bucket& b : t)
     if (b.family == S4_FAMILY_GEMV && b.split > s4::gemv_max_split())
       return fail(S4_ERR_INVALID, "GEMV split %d exceeds %d", b.split, s4::gemv_max_split());
