@@ -191,6 +191,56 @@ def cpu_time(deqs, xs, seconds: float, sweep=cpu_sweep_once):
             return n, dt
 
 
+def cpu_stack_baseline(serve, seconds: float):
+    """Configs 4/5 on the host cores, on a bounded sample: the stack's repeating 4-layer unit (three
+    linear-attention layers sharing one set of weights, then an attention layer) over a 2048-token
+    prompt, torch fp32 on weights dequantised once (fake-quant route, export_engine.py:88-103), with
+    the residual add + RMSNorm (wgsl.js:55-78) and SiLU*mul (wgsl.js:81-90) in fp32 and fp16
+    activations between ops, wired like ``serve.stack_forward``. The 24-layer stack repeats the unit
+    six times, so its tokens/s is the unit's divided by six."""
+    import torch
+    from oracle import s4ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    T, D = 2048, serve.HIDDEN
+    weights = {}
+    for kind, layer_idx in (("linear", 0), ("attn", 3)):
+        weights[kind] = {}
+        for name, K, N in serve.projection_shapes(kind):
+            packed, scales = serve.synthetic_projection(serve.projection_seed(layer_idx, name), K, N)
+            weights[kind][name] = s4ref.dequant_torch(packed, scales)  # [N, K] fp32
+
+    def norm(x):
+        return (x * torch.rsqrt((x * x).mean(1, keepdim=True) + 1e-6)).half()
+
+    def layer(x, w):
+        a = (norm(x).float() @ w["in_proj"].T).half()
+        x = x + (a[:, :D].float() @ w["out_proj"].T).half().float()
+        gu = (norm(x).float() @ w["gate_up"].T).half().float()
+        g, u = gu[:, :gu.shape[1] // 2], gu[:, gu.shape[1] // 2:]
+        return x + ((g / (1.0 + torch.exp(-g)) * u).half().float() @ w["down"].T).half().float()
+
+    def unit(x):
+        for kind in ("linear", "linear", "linear", "attn"):
+            x = layer(x, weights[kind])
+        return x
+
+    x0 = torch.randn((T, D), generator=torch.Generator().manual_seed(0)).half().float()
+    with torch.inference_mode():
+        unit(x0)  # warm
+        n, t0 = 0, time.perf_counter()
+        while True:
+            unit(x0)
+            n += 1
+            dt = time.perf_counter() - t0
+            if dt >= seconds:
+                break
+    units = serve.N_LAYERS // 4
+    return {"value": T * n / dt / units, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{n} passes of the stack's 4-layer unit (3 linear-attention + 1 attention layer) over a "
+                      f"{T}-token prompt in {dt:.1f} s, torch fp32 on weights dequantised once (fake-quant route, "
+                      f"export_engine.py:88-103); the 24-layer stack = {units} units"}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
@@ -701,6 +751,8 @@ def run_stack(args, rank, world, local_rank):
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_stack_baseline(serve, args.cpu_seconds / 2)
         print(json.dumps(line), flush=True)
     # a graph that holds NCCL calls must be gone before destroy_process_group (the bound replay
     # method in `step` keeps it alive too)
