@@ -191,6 +191,35 @@ def cpu_time(deqs, xs, seconds: float, sweep=cpu_sweep_once):
             return n, dt
 
 
+def cpu_prefill_baseline(seconds: float):
+    """Configs 1 and 3 on the host cores: gate|up at M = 64 and gate|up / down at M = 2048, torch fp32
+    on weights dequantised once (fake-quant route), each timed for a third of ``seconds``; TFLOP/s."""
+    import numpy as np
+    import torch
+    from oracle import s4ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    w = {}
+    for name, K, N in (("gate_up", 2048, 12288), ("down", 6144, 2048)):
+        packed, scales = s4ref.config_weights(rng, K, N)
+        w[name] = s4ref.dequant_torch(packed, scales)
+    out = {}
+    with torch.inference_mode():
+        for name, M in (("gate_up", 64), ("gate_up", 2048), ("down", 2048)):
+            N, K = w[name].shape
+            x = torch.from_numpy(s4ref.config_x(rng, M, K).astype(np.float32))
+            (x @ w[name].T).half()  # warm
+            n, t0 = 0, time.perf_counter()
+            while True:
+                (x @ w[name].T).half()
+                n += 1
+                dt = time.perf_counter() - t0
+                if dt >= seconds / 3:
+                    break
+            out[f"{name}/M{M}"] = {"TFLOPs": round(2.0 * M * N * K * n / dt / 1e12, 3), "calls": n}
+    return out
+
+
 def cpu_stack_baseline(serve, seconds: float):
     """Configs 4/5 on the host cores, on a bounded sample: the stack's repeating 4-layer unit (three
     linear-attention layers sharing one set of weights, then an attention layer) over a 2048-token
@@ -559,7 +588,8 @@ def run_ours(args, rank, world, local_rank):
                          f"(fake-quant route, export_engine.py:88-103)",
                "dequant_per_call": {"value": sweep_bytes() * n2 / dt2 / 1e9, "unit": "GB/s",
                                     "sample": f"{n2} full sweeps in {dt2:.1f} s, every weight dequantised from its "
-                                              f"int4 bytes inside each call, then the same fp32 matmul"}}
+                                              f"int4 bytes inside each call, then the same fp32 matmul"},
+               "prefill": cpu_prefill_baseline(args.cpu_seconds / 2)}
 
     if rank == 0:
         per_launch_bytes = sweep_bytes()  # one chained launch moves the whole sweep
