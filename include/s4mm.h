@@ -58,6 +58,8 @@ S4_API const char* s4_last_error(void);
  * (web/public/engine/engine.js:63-87): the context owns the split-K scratch the reference
  * allocates per activation pool (engine.js:190-199) and the dispatch table. */
 S4_API int s4_init(int device, s4_ctx** out);
+/* Close a context. Its weights and chains are not freed with it: s4_weight_free / s4_chain_free
+ * stay valid on them afterwards (in either order), every other call on them needs the context. */
 S4_API int s4_destroy(s4_ctx* ctx);
 
 /* Upload one fused projection's int4 weight from HOST memory and repack it on the device into

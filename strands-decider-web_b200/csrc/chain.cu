@@ -779,6 +779,7 @@ using s4::ChainOp;
 
 struct s4_chain {
   s4_ctx* ctx;
+  int device;  // the context's device (chain_destroy needs no live context)
   int nops;
   int grid;
   int slots;
@@ -938,6 +939,7 @@ int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* c
 
   s4_chain* c = new s4_chain();
   c->ctx = ctx;
+  c->device = ctx->device;
   c->nops = nops;
   c->grid = G;
   c->slots = slots;
@@ -1028,6 +1030,7 @@ cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream, bool c
 }
 
 void chain_destroy(s4_chain* c) {
+  DeviceGuard guard(c->device);
   cudaFree(c->d_ops);
   cudaFree(c->d_scratch);
   delete c;

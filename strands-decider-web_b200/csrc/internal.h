@@ -53,6 +53,7 @@ struct s4_ctx {
 
 struct s4_weight {
   s4_ctx* ctx = nullptr;
+  int device = -1;  // the context's device: freeing or reading back the weight needs no live context
   int N = 0, K = 0, nblk = 0, ktiles = 0;
   uint8_t* wq = nullptr;
   uint8_t* ws = nullptr;

@@ -234,6 +234,7 @@ int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, i
   s4_weight* w = new (std::nothrow) s4_weight();
   if (!w) return fail(S4_ERR_NOMEM, "out of host memory");
   w->ctx = ctx;
+  w->device = ctx->device;
   w->N = N;
   w->K = K;
   w->glu = glu_I > 0;
@@ -561,7 +562,7 @@ int s4_weight_upload_glu(s4_ctx* ctx, const void* packed, const void* scales, in
 
 int s4_weight_free(s4_weight* w) {
   if (!w) return S4_OK;
-  DeviceGuard guard(w->ctx->device);
+  DeviceGuard guard(w->device);
   cudaFree(w->wq);
   cudaFree(w->ws);
   cudaFree(w->wb);
@@ -588,7 +589,7 @@ int s4_weight_layout_bytes(const s4_weight* w, size_t* wq_bytes, size_t* ws_byte
 int s4_weight_download_layout(const s4_weight* w, void* wq_host, size_t wq_bytes, void* ws_host, size_t ws_bytes) {
   if (!w || !wq_host || !ws_host) return fail(S4_ERR_INVALID, "NULL argument");
   if (wq_bytes < w->wq_bytes || ws_bytes < w->ws_bytes) return fail(S4_ERR_INVALID, "host buffers too small");
-  DeviceGuard guard(w->ctx->device);
+  DeviceGuard guard(w->device);
   cudaError_t e = cudaMemcpy(wq_host, w->wq, w->wq_bytes, cudaMemcpyDeviceToHost);
   if (e == cudaSuccess) e = cudaMemcpy(ws_host, w->ws, w->ws_bytes, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "layout download");
@@ -637,7 +638,7 @@ int s4_weight_save(const s4_weight* w, const char* path) {
     return fail(S4_ERR_NOMEM, "out of host memory for the cache copy");
   }
   {
-    DeviceGuard guard(w->ctx->device);
+    DeviceGuard guard(w->device);
     cudaError_t e = cudaMemcpy(buf.data(), w->wq, w->wq_bytes, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess) e = cudaMemcpy(buf.data() + w->wq_bytes, w->ws, w->ws_bytes, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && w->wb)
@@ -689,6 +690,7 @@ int s4_weight_load(s4_ctx* ctx, const char* path, s4_weight** out) {
     return fail(S4_ERR_NOMEM, "out of host memory");
   }
   w->ctx = ctx;
+  w->device = ctx->device;
   w->N = h.N;
   w->K = h.K;
   w->glu = (h.flags & 2u) ? 1 : 0;

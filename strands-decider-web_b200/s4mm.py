@@ -165,8 +165,8 @@ class Chain:
             self.handle = None
 
     def __del__(self):
-        try:
-            if self.handle and _lib is not None and self.ctx.handle:
+        try:  # valid after the context closed too (the library frees chains without it)
+            if self.handle and _lib is not None:
                 _lib.s4_chain_free(self.handle)
         except Exception:
             pass
@@ -203,8 +203,8 @@ class Weight:
             self.handle = None
 
     def __del__(self):
-        try:
-            if self.handle and _lib is not None and self.ctx.handle:
+        try:  # valid after the context closed too (the library frees weights without it)
+            if self.handle and _lib is not None:
                 _lib.s4_weight_free(self.handle)
         except Exception:
             pass
