@@ -172,6 +172,20 @@ class Chain:
             pass
 
 
+def _dev_f16(name: str, t, device: int, rows: int, cols: int):
+    """Require a contiguous ``[>= rows, cols]`` CUDA fp16 tensor on the context's device. The
+    kernels take raw pointers and sizes, so a wrong dtype, width, row count or device would be read
+    or written out of bounds; the wrapper refuses it with ERR_INVALID instead."""
+    import torch
+    if not isinstance(t, torch.Tensor) or t.dtype != torch.float16 or not t.is_cuda:
+        raise S4Error(ERR_INVALID, f"{name} must be a CUDA fp16 tensor")
+    if t.device.index != device:
+        raise S4Error(ERR_INVALID, f"{name} is on cuda:{t.device.index}, the context on cuda:{device}")
+    if t.dim() != 2 or not t.is_contiguous() or t.shape[1] != cols or t.shape[0] < rows:
+        raise S4Error(ERR_INVALID, f"{name} must be a contiguous [>= {rows}, {cols}] tensor, got "
+                                   f"{tuple(t.shape)}{'' if t.is_contiguous() else ' (strided)'}")
+
+
 class Weight:
     """An uploaded, device-repacked int4 weight (the engine's resolved ``.q``/``.s`` pair)."""
 
@@ -322,8 +336,10 @@ class Context:
         import torch
         if M is None:
             M = x.shape[0]
+        _dev_f16("x", x, self.device, M, W.K)
         if y is None:
             y = torch.empty((M, W.N), dtype=torch.float16, device=x.device)
+        _dev_f16("y", y, self.device, M, W.N)
         _check(_lib.s4_matmul(self.handle, W.handle, x.data_ptr(), int(M), y.data_ptr(), _stream_handle(stream)))
         return y
 
@@ -331,9 +347,14 @@ class Context:
         """Synchronous host-buffer matmul (``Gemm.setA`` + ``encode`` + ``readY``); fp16 arrays
         or their uint16 bit patterns."""
         x = np.ascontiguousarray(x)
+        if x.dtype not in (np.float16, np.uint16) or x.ndim != 2 or x.shape[1] != W.K:
+            raise S4Error(ERR_INVALID, f"x must be [M, {W.K}] fp16 (or its uint16 bits), got {x.dtype} {x.shape}")
         M = x.shape[0]
         if y is None:
             y = np.empty((M, W.N), dtype=np.float16)
+        if (not isinstance(y, np.ndarray) or y.dtype not in (np.float16, np.uint16) or y.shape != (M, W.N)
+                or not y.flags.c_contiguous or not y.flags.writeable):
+            raise S4Error(ERR_INVALID, f"y must be a writable contiguous [{M}, {W.N}] fp16 array")
         _check(_lib.s4_matmul_host(self.handle, W.handle, x.ctypes.data, int(M), y.ctypes.data))
         return y
 
@@ -351,8 +372,10 @@ class Context:
         """``mid = silu(big[:, :I]) * big[:, I:2I]`` on CUDA fp16 tensors."""
         import torch
         M = big.shape[0]
+        _dev_f16("big", big, self.device, M, 2 * I)
         if mid is None:
             mid = torch.empty((M, I), dtype=torch.float16, device=big.device)
+        _dev_f16("mid", mid, self.device, M, I)
         _check(_lib.s4_silu_mul(self.handle, big.data_ptr(), int(M), int(I), mid.data_ptr(), _stream_handle(stream)))
         return mid
 
@@ -427,9 +450,11 @@ class Context:
         ys = (_P * n)(*[_P(o[2].data_ptr()) for o in ops])
         ms = (C.c_int * n)(*[int(o[0].shape[0]) for o in ops])
         deps = (C.c_int * n)(*[int(o[3]) if len(o) > 3 else -1 for o in ops])
-        for o in ops:
+        for i, o in enumerate(ops):
             if o[0].shape[0] != o[2].shape[0] or o[0].shape[1] != o[1].K or o[2].shape[1] != o[1].N:
                 raise S4Error(1, "chain op shapes must be x [M, K], y [M, N] of its weight")
+            _dev_f16(f"op {i} x", o[0], self.device, o[0].shape[0], o[1].K)
+            _dev_f16(f"op {i} y", o[2], self.device, o[0].shape[0], o[1].N)
         h = _P()
         _check(_lib.s4_chain_create(self.handle, n, ws, xs, ys, ms, deps, C.byref(h)))
         return Chain(self, h.value, list(ops))

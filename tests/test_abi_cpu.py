@@ -79,3 +79,28 @@ def test_new_entry_points_reject_null_arguments(pkg, tmp_path):
     assert lib.s4_weight_save(None, str(tmp_path / "w").encode()) == INV
     assert lib.s4_weight_load(None, str(tmp_path / "w").encode(), C.byref(h)) == INV
     assert b"NULL" in lib.s4_last_error()
+
+
+def test_wrappers_refuse_tensors_the_kernels_would_overrun(pkg):
+    """Context.matmul / silu_mul / chain / matmul_host check dtype, device, contiguity and shape
+    against the weight before passing raw pointers to the library (ERR_INVALID, no library call):
+    a wrong width or row count would be read or written out of bounds by the kernels."""
+    import numpy as np
+    torch = pytest.importorskip("torch")
+    m = pkg.s4mm
+    ctx = m.Context.__new__(m.Context)  # no device: the checks raise before any library call
+    ctx.handle, ctx.device = None, 0
+    W = m.Weight(ctx, None, 128, 64)
+    cpu16 = torch.zeros((2, 64), dtype=torch.float16)
+    cases = [
+        lambda: ctx.matmul(cpu16, W),                                        # host tensor
+        lambda: ctx.silu_mul(torch.zeros((2, 256), dtype=torch.float16), 128),
+        lambda: ctx.chain([(cpu16, W, torch.zeros((2, 128), dtype=torch.float16))]),
+        lambda: ctx.matmul_host(np.zeros((2, 32), np.float16), W),          # K mismatch
+        lambda: ctx.matmul_host(np.zeros((2, 64), np.float32), W),          # dtype
+        lambda: ctx.matmul_host(np.zeros((2, 64), np.float16), W, np.zeros((2, 64), np.float16)),  # y width
+    ]
+    for i, case in enumerate(cases):
+        with pytest.raises(m.S4Error) as e:
+            case()
+        assert e.value.code == m.ERR_INVALID, i
