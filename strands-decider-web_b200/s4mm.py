@@ -186,6 +186,21 @@ def _dev_f16(name: str, t, device: int, rows: int, cols: int):
                                    f"{tuple(t.shape)}{'' if t.is_contiguous() else ' (strided)'}")
 
 
+def _dev_buf(name: str, t, device: int, nbytes: int, dtype=None):
+    """Require a contiguous CUDA tensor on the context's device holding at least ``nbytes`` (of
+    ``dtype`` when given): the upload kernels read that many bytes from its pointer."""
+    import torch
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise S4Error(ERR_INVALID, f"{name} must be a CUDA tensor when the weight is uploaded from the device")
+    if t.device.index != device:
+        raise S4Error(ERR_INVALID, f"{name} is on cuda:{t.device.index}, the context on cuda:{device}")
+    if dtype is not None and t.dtype != dtype:
+        raise S4Error(ERR_INVALID, f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous() or t.numel() * t.element_size() < nbytes:
+        raise S4Error(ERR_INVALID, f"{name} must be contiguous with at least {nbytes} bytes, got "
+                                   f"{t.numel() * t.element_size()}{'' if t.is_contiguous() else ' (strided)'}")
+
+
 class Weight:
     """An uploaded, device-repacked int4 weight (the engine's resolved ``.q``/``.s`` pair)."""
 
@@ -243,6 +258,9 @@ class Context:
         ``s4_weight_upload_device``. Synchronous."""
         h = _P()
         if hasattr(packed, "is_cuda") and packed.is_cuda:
+            import torch
+            _dev_buf("packed", packed, self.device, N * (K // 32) * 16, torch.uint8)
+            _dev_buf("scales", scales, self.device, N * (K // 32) * 2, torch.float16)
             _check(_lib.s4_weight_upload_device(self.handle, packed.data_ptr(), scales.data_ptr(), N, K, 0,
                                                 C.byref(h)))
         else:
@@ -258,6 +276,9 @@ class Context:
         writes silu(gate) * up, [M][I] (``s4_weight_upload_glu``). Host arrays or CUDA tensors."""
         h = _P()
         if hasattr(packed, "is_cuda") and packed.is_cuda:
+            import torch
+            _dev_buf("packed", packed, self.device, 2 * I * (K // 32) * 16, torch.uint8)
+            _dev_buf("scales", scales, self.device, 2 * I * (K // 32) * 2, torch.float16)
             _check(_lib.s4_weight_upload_glu(self.handle, packed.data_ptr(), scales.data_ptr(), I, K, UPLOAD_DEVICE,
                                              C.byref(h)))
         else:
@@ -287,6 +308,12 @@ class Context:
         arrays, or CUDA tensors (all on the device). Synchronous."""
         h = _P()
         if hasattr(q, "is_cuda") and q.is_cuda:
+            import torch
+            ng = N * (K // group) if group else 0
+            _dev_buf("q", q, self.device, N * (K // 32) * bits * 4)
+            _dev_buf("scales", scales, self.device, ng * 2, torch.float16)
+            if bias is not None:
+                _dev_buf("bias", bias, self.device, ng * 2, torch.float16)
             _check(_lib.s4_weight_upload_format(self.handle, q.data_ptr(), scales.data_ptr(),
                                                 None if bias is None else bias.data_ptr(), N, K, bits, group,
                                                 UPLOAD_DEVICE, C.byref(h)))
@@ -322,10 +349,10 @@ class Context:
         """Decode a device-resident wire scale tensor (uint8 CUDA tensor of 4*N + N*G bytes) to fp16
         ``[N, G]`` on the device (``decodeScales``), asynchronous on ``stream``."""
         import torch
-        if wire_dev.numel() * wire_dev.element_size() < 4 * N + N * G:
-            raise S4Error(ERR_INVALID, f"wire buffer smaller than 4*N + N*G for N={N} G={G}")
+        _dev_buf("wire", wire_dev, self.device, 4 * N + N * G)
         if out is None:
             out = torch.empty((N, G), dtype=torch.float16, device=wire_dev.device)
+        _dev_buf("out", out, self.device, N * G * 2, torch.float16)
         _check(_lib.s4_decode_wire_scales(self.handle, wire_dev.data_ptr(), int(N), int(G), out.data_ptr(),
                                           _stream_handle(stream)))
         return out
