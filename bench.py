@@ -36,8 +36,8 @@ if ROOT not in sys.path:
 SHAPES = [("qkvz_ab", 2048, 8224), ("attn_qkv", 2048, 3072), ("gate_up", 2048, 12288), ("down", 6144, 2048)]
 MS = [1, 2, 4, 8]
 COPIES = 8
-BLOCK = 8 * COPIES  # chained launches per replayed graph in the device-timed loop
 NSETS = 4           # bound input/output buffer sets (and end-to-end streams), used round robin
+L2_BYTES = 126 << 20
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
@@ -52,6 +52,11 @@ def load_pkg():
     sys.modules[name] = mod
     spec.loader.exec_module(mod)
     return mod
+
+
+def bench_config():
+    """The workload both arms report (the same dict, so the two lines' configs compare equal)."""
+    return {"workload": "decode_gemv_sweep_config2", "M": MS, "shapes_KN": [[K, N] for _, K, N in SHAPES]}
 
 
 def alg_bytes(M, K, N):
@@ -287,7 +292,7 @@ def run_reference(args, rank, world):
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "decode_gemv_sweep_config2", "M": MS, "shapes_KN": [[K, N] for _, K, N in SHAPES]},
+        "config": bench_config(),
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": f"{args.steps} full sweeps (16 matmuls each), torch fp32 on dequantised weights"},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -299,6 +304,104 @@ def run_reference(args, rank, world):
 # ------------------------------------------------------------------------------------------------
 # GPU side
 # ------------------------------------------------------------------------------------------------
+def linear_stack_extras(args, ctx, rank, world, dev, barrier, max_over_ranks):
+    """BASELINE configs 4 and 5 beside the decode headline, on the same ranks.
+
+    * ``stack`` (config 4): one 2048-token prompt through the 24-layer linear stack, the whole
+      forward replayed as one CUDA graph; on one GPU the plain stack, on N GPUs column-sharded with
+      the all-gathers fused into the GEMM / SiLU*mul epilogues (peer stores over NVLink) and a flag
+      barrier per projection (strong scaling: the same prompt whatever N is).
+    * ``serve`` (config 5): the first ``--requests`` of the seeded 4096 requests, assigned to ranks
+      longest-first (LPT), weights replicated, no collective (weak scaling of work per GPU); each
+      rank runs its requests packed into chunks of at most 8192 tokens.
+    Both are device-timed (CUDA events, max over ranks) after three warm-up steps."""
+    import importlib
+
+    import numpy as np
+    import torch
+
+    serve = importlib.import_module("strands_decider_web_b200.serve")
+    stream = torch.cuda.current_stream(dev)
+    flops_tok = serve.stack_flops_per_token()
+    _, tc_peak, peak_kind = peaks()
+    out = {}
+
+    def timed(step, n_steps):
+        for _ in range(3):
+            step()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n_steps):
+            step()
+        b.record(stream)
+        barrier()
+        return max_over_ranks(a.elapsed_time(b))
+
+    # ---- config 4: the 2048-token prompt ----
+    x = torch.from_numpy(np.random.default_rng(0).standard_normal((2048, serve.HIDDEN)).astype(np.float16)).to(dev)
+    fused, graph = None, None
+    full = serve.CudaStack(ctx, fuse_silu=True)  # replicated weights: the one-GPU stack and config 5
+    if world == 1:
+        full.forward(x)
+        torch.cuda.synchronize(dev)
+        l0 = ctx.launch_count
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            full.forward(x)
+        launches = ctx.launch_count - l0
+        step = graph.replay
+    else:
+        fused = serve.FusedColshardStack(ctx, None, rank, world, fuse_silu=True)
+        fused.forward(x)
+        torch.cuda.synchronize(dev)
+        l0 = ctx.launch_count
+        fused.capture(x)
+        launches = ctx.launch_count - l0
+        step = fused.replay
+    n_stack = max(1, min(args.steps, 20))
+    ms = timed(step, n_stack)
+    tok_s = 2048 * n_stack / (ms / 1e3)
+    out["stack"] = {"workload": "config4_stack_2048_prompt", "value": tok_s, "unit": "tokens/s",
+                    "ms_per_step": ms / n_stack, "steps": n_stack, "warmup": 3, "scaling": "strong",
+                    "parallelism": "one GPU" if world == 1 else
+                    f"colshard{world} (all-gathers fused into the GEMM / SiLU*mul epilogues, NVLink peer stores)",
+                    "tflops": tok_s * flops_tok / 1e12, "tensor_frac": tok_s * flops_tok / 1e12 / tc_peak,
+                    "peak_kind": peak_kind, "gpu_launches_per_step": launches, "cuda_graph": True}
+    step = graph = None
+    if fused is not None:
+        fused.close()
+        fused = None
+    torch.cuda.synchronize(dev)
+
+    # ---- config 5: batched data-parallel serving ----
+    lengths = serve.request_lengths(4096)[: args.requests]
+    mine = serve.lpt_shard(lengths, world)[rank]
+    chunks = serve.pack_chunks(lengths[mine], 8192)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    xs = [torch.randn((int(lengths[mine][c].sum()), serve.HIDDEN), generator=g, device=dev).to(torch.float16)
+          for c in chunks]
+
+    def serve_step():
+        for xc in xs:
+            full.forward(xc)
+    n_serve = max(1, min(args.steps, 3))
+    ms = timed(serve_step, n_serve)
+    tokens = int(lengths.sum())
+    tok_s = tokens * n_serve / (ms / 1e3)
+    out["serve"] = {"workload": f"config5_serve_{args.requests}_requests_lpt", "value": tok_s, "unit": "tokens/s",
+                    "ms_per_step": ms / n_serve, "steps": n_serve, "warmup": 3, "scaling": "weak",
+                    "tokens_per_step": tokens, "parallelism": f"dp{world} (LPT request shards, no collective)",
+                    "tflops": tok_s * flops_tok / 1e12, "tensor_frac": tok_s * flops_tok / 1e12 / (tc_peak * world),
+                    "peak_kind": peak_kind}
+    if ctx.check_errors():
+        raise RuntimeError("device error word set during the stack / serving runs")
+    del xs, full
+    torch.cuda.synchronize(dev)
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -367,11 +470,12 @@ def run_ours(args, rank, world, local_rank):
             for name, K, N in SHAPES:
                 ctx.matmul(xs[(M, name)], weight_for(name, rot, mi), M, ys[(M, name)], st)
 
-    # Steps are replayed from CUDA graphs so the host does not pace the GPU: graphs[n] holds the
-    # chained launches of rotations 0 .. n-1 back to back (graphs[COPIES] is a full rotation) and
-    # graphs[BLOCK] eight full rotations (consecutive launches overlap inside a graph, not across
-    # graph launches); call_graphs hold the 16 per-call launches of each rotation for comparison.
-    graphs, call_graphs = {}, []
+    # Steps are replayed from CUDA graphs so the host does not pace the GPU. The warm-up steps and
+    # the timed steps are one graph each, holding exactly that many chained launches over the weight
+    # rotations back to back, so consecutive steps overlap (programmatic dependent launch) across the
+    # whole timed region whatever --steps is; call_graphs hold the 16 per-call launches of each
+    # rotation for comparison.
+    call_graphs = []
     cap_stream = torch.cuda.Stream(dev)
     cap_stream.wait_stream(stream)
     with torch.cuda.stream(cap_stream):
@@ -383,12 +487,15 @@ def run_ours(args, rank, world, local_rank):
         chains[0].run(cap_stream)
         launches_per_step = ctx.launch_count - n0
         cap_stream.synchronize()
-        for n in list(range(1, COPIES + 1)) + [BLOCK]:
+        # the timed steps continue the warm-up's rotation, so the first timed step's weight copies are
+        # not the ones the last warm-up step left in L2
+        step_graphs = {}
+        for n, start in ((args.warmup, 0), (args.steps, args.warmup)):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=cap_stream):
                 for i in range(n):
-                    chains[i % COPIES].run(cap_stream)
-            graphs[n] = g
+                    chains[(start + i) % COPIES].run(cap_stream)
+            step_graphs[(n, start)] = g
         for rot in range(COPIES):
             g2 = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g2, stream=cap_stream):
@@ -397,15 +504,9 @@ def run_ours(args, rank, world, local_rank):
     stream.wait_stream(cap_stream)
     torch.cuda.synchronize(dev)
 
-    def steps_on_stream(k: int):
-        # k steps on `stream`: blocks of eight rotations, whole rotations, then part of one
+    def steps_on_stream(k: int, start: int):
         with torch.cuda.stream(stream):
-            for _ in range(k // BLOCK):
-                graphs[BLOCK].replay()
-            for _ in range((k % BLOCK) // COPIES):
-                graphs[COPIES].replay()
-            if k % COPIES:
-                graphs[k % COPIES].replay()
+            step_graphs[(k, start)].replay()
 
     def barrier():
         if world > 1:
@@ -419,13 +520,13 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    steps_on_stream(args.warmup)
+    steps_on_stream(args.warmup, 0)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         barrier()
         e0.record(stream)
-        steps_on_stream(args.steps)
+        steps_on_stream(args.steps, args.warmup)
         e1.record(stream)
         barrier()
     launches = launches_per_step * args.steps   # kernels inside the replayed graphs
@@ -542,22 +643,30 @@ def run_ours(args, rank, world, local_rank):
         hbm_pk, tc_pk, _ = peaks()
         pre_shapes = {"down": (6144, 2048), "gate_up": (2048, 12288)}
         pre_w = {}
+        rng_p = np.random.default_rng(0)
         for name, (K, N) in pre_shapes.items():
-            src = Ws[name] if name in Ws else None
-            pre_w[name] = src[:2]
+            # weights rotate over >= 8 device copies whose bytes exceed twice the L2, so every call
+            # streams its weight from HBM (a weight of these shapes alone fits in the L2)
+            packed, scales = s4ref.config_weights(rng_p, K, N)
+            n_copies = max(8, -(-2 * L2_BYTES // (N * K // 2 + N * K // 16)))
+            pd, sd = torch.from_numpy(packed).to(dev), torch.from_numpy(scales).to(dev)
+            pre_w[name] = [ctx.upload(pd, sd, N, K) for _ in range(n_copies)]
+            del pd, sd
+        prefill_copies = {name: len(v) for name, v in pre_w.items()}
         for name, (K, N) in pre_shapes.items():
+            nw = len(pre_w[name])
             for M in (16, 64, 128, 512, 2048):
                 x = torch.from_numpy(s4ref.config_x(np.random.default_rng(M), M, K)).to(dev)
                 y = torch.empty((M, N), dtype=torch.float16, device=dev)
-                reps = 8 if M >= 512 else 32
+                reps = max(nw, 8 if M >= 512 else 32)
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.stream(cap_stream):
                     for r in range(2):
-                        ctx.matmul(x, pre_w[name][r % 2], M, y, cap_stream)
+                        ctx.matmul(x, pre_w[name][r % nw], M, y, cap_stream)
                     cap_stream.synchronize()
                     with torch.cuda.graph(g, stream=cap_stream):
                         for r in range(reps):
-                            ctx.matmul(x, pre_w[name][r % 2], M, y, cap_stream)
+                            ctx.matmul(x, pre_w[name][r % nw], M, y, cap_stream)
                 torch.cuda.synchronize(dev)
                 g.replay()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -570,11 +679,21 @@ def run_ours(args, rank, world, local_rank):
                 flops = 2.0 * M * N * K
                 tfs = flops / (us * 1e-6) / 1e12
                 gbs = alg_bytes(M, K, N) / (us * 1e-6) / 1e9
-                fam = ctx.plan(M, N, K)[0]
+                fam, tile, split = ctx.plan(M, N, K)
                 prefill[f"{name}/M{M}"] = {"us": round(us, 2), "TFLOPs": round(tfs, 1), "GBps": round(gbs, 1),
                                            "tensor_frac": round(tfs / tc_pk, 3), "hbm_frac": round(gbs / hbm_pk, 3),
-                                           "family": fam}
+                                           "family": fam, "tile": tile, "split": split}
                 del g
+        for ws_ in pre_w.values():
+            for W in ws_:
+                W.free()
+        prefill["weight_copies"] = prefill_copies
+        prefill["l2"] = "each call streams its weight from HBM: rotation over device copies totalling > 2x L2"
+
+    # ---- BASELINE configs 4 and 5 on the same ranks (extra keys of the line) ---------------------------
+    extras = {}
+    if not args.quick and not args.no_stack:
+        extras = linear_stack_extras(args, ctx, rank, world, dev, barrier, max_over_ranks)
 
     # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------------------------------
     hbm, bf16, peak_kind = peaks()
@@ -600,11 +719,13 @@ def run_ours(args, rank, world, local_rank):
             "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "decode_gemv_sweep_config2", "launch": "the 16 matmuls of a step as one chained launch; steps back to back on one stream "
-                                 "(programmatic dependent launch)", "M": MS,
-                       "shapes_KN": [[K, N] for _, K, N in SHAPES], "weight_copies": COPIES,
-                       "l2": "inputs larger than L2: 8 rotating weight copies (272 MB) per step sequence",
-                       "parallelism": f"dp{world} (weights replicated, no collective)"},
+            "config": bench_config(),
+            "setup": {"launch": "the 16 matmuls of a step as one chained launch; the timed steps are one CUDA "
+                                "graph of that many launches back to back on one stream (programmatic dependent "
+                                "launch)",
+                      "weight_copies": COPIES,
+                      "l2": "inputs larger than L2: 8 rotating weight copies (272 MB) per step sequence",
+                      "parallelism": f"dp{world} (weights replicated, no collective)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": profile_traffic(), "peak_kind": peak_kind,
                          "kernel": "chain_kernel", "launch_us_avg": avg_launch_us},
@@ -621,8 +742,9 @@ def run_ours(args, rank, world, local_rank):
             "per_call": per,
             "prefill": prefill,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
-    del graphs, call_graphs, e2e_graphs
+    del step_graphs, call_graphs, e2e_graphs
     for ch in chains:
         ch.free()
     ctx.close()
@@ -895,7 +1017,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--quick", action="store_true", help="skip the per-call breakdown")
+    ap.add_argument("--quick", action="store_true", help="skip the per-call breakdown, prefill, stack and serving")
+    ap.add_argument("--no-stack", action="store_true", help="skip the stack and serving keys of the decode line")
     ap.add_argument("--family", choices=["auto", "gemv", "tc"], default="auto",
                     help="pin the kernel family instead of the dispatch table")
     ap.add_argument("--workload", choices=["decode", "stack", "serve", "formats"], default="decode",

@@ -157,13 +157,23 @@ S4_API int s4_matmul_host_async(s4_ctx* ctx, const s4_weight* w, const uint16_t*
 /* y[M][N] = x[M][K] @ W^T like s4_matmul, for callers that cannot allocate device memory when they
  * run a matmul (a host whose memory manager already owns the whole device, or a serving loop that
  * must not take cudaMalloc's implicit device synchronisation). It needs no context-owned scratch:
- * the tcgen05 split-K GEMM keeps its partials and tile counters in one static 8 MiB device array
- * that every GPU loading this library holds until exit. It calls no allocator. Limit:
- * ceil(M/256) * ceil(N/128) <= 16384 (larger calls are rejected with S4_ERR_INVALID); at most 31
- * CTAs split the work. The first call on a device looks up the array's device address (do it
- * before any stream capture). All calls share the array: calls that overlap on the GPU race.
- * No counterpart in the reference. DEVICE pointers, asynchronous on `stream`. */
+ * the tcgen05 split-K GEMM keeps its partials, tile counters and error word in one static 8 MiB
+ * device array that every GPU loading this library holds until exit. It calls no allocator. It needs
+ * no live context either: the weight records its device and SM count, so it may be called after
+ * s4_destroy of the context the weight was uploaded with. Limit: ceil(M/256) * ceil(N/128) <= 16384
+ * (larger calls are rejected with S4_ERR_INVALID); the CTA count is the SM count, capped so that each
+ * CTA's two partial slots of (M rounded up to 16, at most 256) x 128 fp32 fit the array (31 CTAs at
+ * M >= 256, all 148 SMs at M <= 48). The first call on a device looks up the array's device address
+ * (do it before any stream capture; a cudaDeviceReset of that device leaves the looked-up address
+ * stale, so do not reset a device this library has used). All calls share the array: calls that
+ * overlap on the GPU race. A bounded wait that expires sets the array's error word, which stays set
+ * until s4_noalloc_check_errors clears it. No counterpart in the reference. DEVICE pointers,
+ * asynchronous on `stream`. */
 S4_API int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, void* stream);
+/* Error word of s4_matmul_noalloc's static scratch on `device` (0 = clean; the bits of
+ * s4_check_errors), read after a device synchronisation; clear != 0 resets it. Allocates nothing.
+ * No counterpart in the reference. */
+S4_API int s4_noalloc_check_errors(int device, uint32_t* flags, int clear);
 
 /* Chained decode GEMV: a fixed list of matmuls y_i[M_i][N_i] = x_i @ W_i^T (1 <= M_i <= 16) run by ONE
  * persistent launch, like the engine's recorded step list submitted at once (plan(), engine.js:236-282).
@@ -243,10 +253,17 @@ S4_API int s4_silu_mul_gather(s4_ctx* ctx, const void* big, int M, int Is, void*
 S4_API int s4_peer_barrier(s4_ctx* ctx, void* const* flags, int nranks, int rank, uint32_t epoch, void* stream);
 
 /* Dispatcher. s4_plan reports the (family, tile, split) s4_matmul will use for M on an
- * (N, K) weight; replaces matmulKernel(M) (engine.js:17-33). s4_force pins a choice for every
- * later call (family 0 = back to the table), like matmulKernel's `force` (engine.js:23);
- * tile/split 0 mean "kernel default". s4_set_table loads a measured M-bucket table:
- * JSON {"buckets": [{"max_m": int, "family": "gemv"|"tc", "tile": int, "split": int}, ...]}. */
+ * (N, K) weight (for the tcgen05 family with N and K given: the tokens per tile and CTAs it launches;
+ * otherwise the bucket's values, 0 = kernel default); replaces matmulKernel(M) (engine.js:17-33).
+ * s4_force pins a choice for every later call (family 0 = back to the table), like matmulKernel's
+ * `force` (engine.js:23); tile/split 0 mean "kernel default". s4_set_table loads a measured M-bucket
+ * table (the role of the tile table tune.html produces, engine/tune.html:8-24):
+ * JSON {"buckets": [{"max_m": int, "family": "gemv"|"tc", "tile": int, "split": int,
+ * "fixup": "auto"|"kernel"|"cta", "K": int, "N": int}, ...]}. A call uses the first bucket whose max_m
+ * covers M and whose K and N (weight columns and rows, 0 or absent = any) match its weight; GEMV split =
+ * CTAs per n-block, tcgen05 split = CTAs, fixup = who sums split tiles (a second kernel or their last
+ * CTA). The last bucket without K and N covers every larger M. json == NULL restores the built-in
+ * table (the measured table compiled into the library). */
 S4_API int s4_plan(s4_ctx* ctx, int M, int N, int K, int* family, int* tile, int* split);
 S4_API int s4_force(s4_ctx* ctx, int family, int tile, int split);
 S4_API int s4_set_table(s4_ctx* ctx, const char* json);

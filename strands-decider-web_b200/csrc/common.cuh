@@ -206,6 +206,13 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v
   return old;
 }
 
+// Load with acquire semantics at GPU scope (pairs with a release by another CTA).
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void set_error(uint32_t* err, uint32_t bits) {
   if (err) atomicOr(err, bits);
 }

@@ -18,12 +18,19 @@
 // order (the allocation-free entry point instead lets the last CTA to arrive at the tile do it,
 // through an atomic ticket).
 //
-// Warp roles (512 threads): warp 0 lane 0 streams raw int4 chunks (1-D bulk copies) into a
-// kTcSlotsW-slot ring; warp 2 lane 0 loads activation tiles by TMA into a kTcStagesX-stage ring; warp 1 owns TMEM
-// and lane 0 issues the MMAs; warps 4-11 dequantise int4 -> fp16 into the MMA's A stage; warps
-// 12-15 drain TMEM (double-buffered accumulators) and write the output.
+// Warp roles (512 threads): warp 0 lane 0 streams raw int4 chunks into a ring of weight slots of
+// kTcGroup chunks each (one 1-D bulk copy per contiguous run of chunks and array); warp 2 lane 0
+// loads activation tiles by TMA into a ring of activation stages; warp 1 owns TMEM and lane 0 issues
+// the MMAs; warps 4-11 dequantise int4 -> fp16 into the MMA's A stage; warps 12-15 drain TMEM
+// (double-buffered accumulators) and write the output.
+//
+// Shared memory is planned on the host per tile width (tc_plan_smem): an activation stage is
+// tn x 128 bytes, so narrow tiles (mid-M calls) get many more stages (up to 16) than 256-token tiles
+// (3). An activation stage comes from L2 and feeds only 4 MMAs of a few dozen cycles at tn <= 64, so a
+// shallow ring leaves the tensor core waiting on L2 latency at every k-tile.
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdio>
 
 #include "common.cuh"
@@ -32,31 +39,31 @@
 namespace s4 {
 
 constexpr int kTcMaxTn = 256;
-constexpr int kTcStagesX = 3;  // activation tiles (TMA) ring
-constexpr int kTcStagesA = 3;  // dequantised weight (MMA operand A) ring
-constexpr int kTcSlotsW = 12;
+constexpr int kTcMaxStagesX = 16;  // activation tiles (TMA) ring, stages chosen per tile width
+constexpr int kTcMaxStagesA = 4;   // dequantised weight (MMA operand A) ring
+constexpr int kTcMaxGroupsW = 4;   // raw weight ring slots
+constexpr int kTcGroup = 8;        // chunks per weight slot (36 KB: 32 KB of nibbles, 4 KB of scales)
+constexpr int kTcGroupAsym = 7;    // asymmetric formats: a chunk also carries 512 bytes of biases
 constexpr int kTcThreads = 512;
 constexpr int kTcDequantWarps = 8;  // warps 4..11
 constexpr int kTcEpiWarp0 = 12;     // warps 12..15 drain TMEM (lane quarter = warp % 4)
-constexpr int kTcXStageBytes = kTcMaxTn * 128;  // tn rows x 64 fp16
-constexpr int kTcAStageBytes = 128 * 128;       // 128 rows x 64 fp16
-constexpr int kTcWSlotBytes = kChunkWBytes + kChunkSBytes;
-// asymmetric formats: a slot also holds the chunk's biases; fewer slots fit the same region
-constexpr int kTcWSlotBytesAsym = kChunkWBytes + 2 * kChunkSBytes;
-constexpr int kTcSlotsWAsym = (kTcSlotsW * kTcWSlotBytes) / kTcWSlotBytesAsym;
-constexpr int kTcOffX = 0;
-constexpr int kTcOffA = kTcOffX + kTcStagesX * kTcXStageBytes;
-constexpr int kTcOffW = kTcOffA + kTcStagesA * kTcAStageBytes;
-constexpr int kTcOffBar = kTcOffW + kTcSlotsW * kTcWSlotBytes;
-constexpr int kTcNumBars = 2 * kTcStagesX + 2 * kTcStagesA + 2 * kTcSlotsW + 2 + 2 + 1;
-constexpr int kTcOffMisc = kTcOffBar + kTcNumBars * 8;
-constexpr int kTcOffEpi = (kTcOffMisc + 64 + 127) & ~127;  // epilogue staging: 4 warps x 16 tokens x 32 n fp16
-constexpr int kTcEpiStageBytes = 16 * 32 * 2;
-constexpr size_t kTcSmem = (size_t)kTcOffEpi + 4 * kTcEpiStageBytes + 1024;  // + alignment slack
-static_assert(kTcSmem <= 227 * 1024, "tcgen05 GEMM shared memory above the per-CTA limit");
-constexpr uint32_t kTcTmemCols = 512;                       // two 256-column accumulators
+constexpr int kTcAStageBytes = 128 * 128;  // 128 rows x 64 fp16
+constexpr int kTcNumBars = 2 * kTcMaxStagesX + 2 * kTcMaxStagesA + 2 * kTcMaxGroupsW + 2 + 2 + 1;
+constexpr int kTcEpiStageBytes = 16 * 32 * 2;  // epilogue staging: per warp 16 tokens x 32 n fp16
+constexpr int kTcSmemLimit = 227 * 1024;
+constexpr int kTcSmemMax = kTcSmemLimit;  // the kernels' dynamic shared memory attribute
+constexpr uint32_t kTcTmemCols = 512;     // two 256-column accumulators
 
 constexpr int kTcMaxDst = 8;  // output copies one launch writes (this GPU + peers)
+
+// Shared-memory plan of one launch (byte offsets from the 1024-aligned base).
+struct TcSmem {
+  int xs, as, wg;  // activation stages, A stages, weight slots
+  int group;       // chunks per weight slot
+  int wslot;       // bytes per weight slot
+  int off_a, off_w, off_bar, off_misc, off_epi;
+  int bytes;  // dynamic shared memory of the launch (with alignment slack)
+};
 
 struct TcParams {
   const uint8_t* wq;
@@ -68,7 +75,7 @@ struct TcParams {
   int64_t ldy;
   int ycol0;
   int vec;  // 16-byte output stores allowed: ldy and ycol0 multiples of 8, every ydst 16-byte aligned
-  float* partials;    // [G][2][256][128] fp32
+  float* partials;    // [grid][2][tn][128] fp32
   uint32_t* tickets;  // [ntb * nblk]
   uint32_t* err;
   int M, N, K;
@@ -80,7 +87,33 @@ struct TcParams {
   int dpq;       // whole tiles per CTA (data-parallel part): CTA b takes tiles [b*dpq, (b+1)*dpq)
   int sk_base;   // first unit of the stream-K part (dpq * grid * ktiles)
   int sk_total;  // units of the stream-K part, split evenly over the grid
+  TcSmem sm;
 };
+
+// Activation stages get what the A stages and at least two weight slots leave, at most
+// kTcMaxStagesX; the weight ring the rest. 256-token tiles: 3 x 32 KB activations, 3 A stages, 2
+// weight slots; 64-token tiles: 10 x 8 KB, 4 A stages, 2 weight slots.
+inline TcSmem tc_plan_smem(int tn, bool asym) {
+  TcSmem s;
+  s.group = asym ? kTcGroupAsym : kTcGroup;
+  s.wslot = s.group * (kChunkWBytes + kChunkSBytes * (asym ? 2 : 1));
+  s.as = tn <= 128 ? 4 : 3;
+  const int xstage = tn * 128;
+  const int fixed = kTcNumBars * 8 + 64 + 128 + 4 * kTcEpiStageBytes + 1024;
+  const int budget = kTcSmemLimit - fixed - s.as * kTcAStageBytes;
+  s.xs = (budget - 2 * s.wslot) / xstage;
+  if (s.xs > kTcMaxStagesX) s.xs = kTcMaxStagesX;
+  if (s.xs < 3) s.xs = 3;
+  s.wg = (budget - s.xs * xstage) / s.wslot;
+  if (s.wg > kTcMaxGroupsW) s.wg = kTcMaxGroupsW;
+  s.off_a = s.xs * xstage;  // multiple of 1024 (tn % 16 == 0): the 128-byte swizzle's alignment
+  s.off_w = s.off_a + s.as * kTcAStageBytes;
+  s.off_bar = s.off_w + s.wg * s.wslot;
+  s.off_misc = s.off_bar + kTcNumBars * 8;
+  s.off_epi = (s.off_misc + 64 + 127) & ~127;
+  s.bytes = s.off_epi + 4 * kTcEpiStageBytes + 1024;  // + slack to align the base to 1024
+  return s;
+}
 
 // Output stores. Each destination is the local buffer or, for the column-sharded prefill, a peer's
 // gathered buffer over NVLink. Call sites branch on ndst == 1 once, outside their element loops:
@@ -176,30 +209,37 @@ __device__ __forceinline__ TcWork tc_work(int b, const TcParams& p) {
   return w;
 }
 
+// Chunk (n-block, k-tile) of the weight that work unit u reads.
+__device__ __forceinline__ int64_t tc_chunk_of(int u, const TcParams& p) {
+  const int tile = u / p.ktiles, kt = u - tile * p.ktiles;
+  return (int64_t)(tile % p.nblk) * p.ktiles + kt;
+}
+
 // kTicketFixup: split tiles are finished inside this kernel by the last CTA to arrive (atomic
 // ticket); otherwise partials are only published and tc_fixup_kernel, launched next, sums them.
 template <bool kTicketFixup, bool kAsym>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p, const __grid_constant__ CUtensorMap tmap_x) {
-  constexpr int SW = kAsym ? kTcSlotsWAsym : kTcSlotsW;            // raw weight ring slots
-  constexpr int WB = kAsym ? kTcWSlotBytesAsym : kTcWSlotBytes;    // bytes per slot
+  const int XS = p.sm.xs, AS = p.sm.as, WG = p.sm.wg;  // ring depths
+  const int GC = p.sm.group, WB = p.sm.wslot;           // chunks and bytes per weight slot
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint8_t* xs = smem + kTcOffX;
-  uint8_t* wa = smem + kTcOffA;
-  uint8_t* wraw = smem + kTcOffW;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
+  const int xstage = p.tn * 128;
+  uint8_t* xs = smem;
+  uint8_t* wa = smem + p.sm.off_a;
+  uint8_t* wraw = smem + p.sm.off_w;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.sm.off_bar);
   uint64_t* full_x = bars;
-  uint64_t* empty_x = full_x + kTcStagesX;
-  uint64_t* ddone = empty_x + kTcStagesX;
-  uint64_t* empty_a = ddone + kTcStagesA;
-  uint64_t* full_w = empty_a + kTcStagesA;
-  uint64_t* empty_w = full_w + kTcSlotsW;  // barrier arrays keep the symmetric layout's size
-  uint64_t* accf = empty_w + kTcSlotsW;
+  uint64_t* empty_x = full_x + kTcMaxStagesX;
+  uint64_t* ddone = empty_x + kTcMaxStagesX;
+  uint64_t* empty_a = ddone + kTcMaxStagesA;
+  uint64_t* full_w = empty_a + kTcMaxStagesA;
+  uint64_t* empty_w = full_w + kTcMaxGroupsW;
+  uint64_t* accf = empty_w + kTcMaxGroupsW;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTcOffMisc);
-  int* s_flag = reinterpret_cast<int*>(smem + kTcOffMisc + 16);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.sm.off_misc);
+  int* s_flag = reinterpret_cast<int*>(smem + p.sm.off_misc + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const TcWork wk = tc_work(blockIdx.x, p);
@@ -207,15 +247,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   const int KT = p.ktiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStagesX; ++s) {
+    for (int s = 0; s < XS; ++s) {
       mbar_init(full_x + s, 1);
       mbar_init(empty_x + s, 1);
     }
-    for (int s = 0; s < kTcStagesA; ++s) {
+    for (int s = 0; s < AS; ++s) {
       mbar_init(ddone + s, kTcDequantWarps);
       mbar_init(empty_a + s, 1);
     }
-    for (int s = 0; s < SW; ++s) {
+    for (int s = 0; s < WG; ++s) {
       mbar_init(full_w + s, 1);
       mbar_init(empty_w + s, kTcDequantWarps);
     }
@@ -241,31 +281,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
 
   if (warp == 0) {
     // ------------- raw int4 chunks: producer -------------
+    // Slot q holds work items [q * GC, q * GC + GC): nibbles of its chunks first, then their scales
+    // (then biases). The weights are immutable, so this runs before the grid-dependency wait and
+    // overlaps the previous kernel's tail.
     if (lane == 0) {
+      const int ngroups = (n + GC - 1) / GC;
       int issued = 0;
       bool ok = true;
-      for (int i = 0; i < n; ++i) {
-        const int slot = i % SW;
-        if (i >= SW && !mbar_wait(empty_w + slot, ((i / SW) - 1) & 1)) {
+      for (int q = 0; q < ngroups; ++q) {
+        const int slot = q % WG;
+        if (q >= WG && !mbar_wait(empty_w + slot, ((q / WG) - 1) & 1)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
           break;
         }
-        const int u = wk.unit(i);
-        const int tile = u / KT, kt = u - tile * KT;
-        const int nb = tile % p.nblk;
-        const int64_t chunk = (int64_t)nb * KT + kt;
+        const int i0 = q * GC, cnt = min(GC, n - i0);
         uint8_t* dst = wraw + slot * WB;
-        mbar_arrive_expect_tx(full_w + slot, WB);
-        bulk_g2s_plain(dst, p.wq + chunk * kChunkWBytes, kChunkWBytes, full_w + slot);
-        bulk_g2s_plain(dst + kChunkWBytes, p.ws + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
-        if (kAsym) bulk_g2s_plain(dst + kChunkWBytes + kChunkSBytes, p.wb + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
+        const uint32_t sec = (uint32_t)GC * kChunkWBytes;  // scales start after GC chunks of nibbles
+        mbar_arrive_expect_tx(full_w + slot, (uint32_t)cnt * (kChunkWBytes + kChunkSBytes * (kAsym ? 2 : 1)));
+        // one copy per array for every run of chunks that is contiguous in the weight
+        for (int j = 0; j < cnt;) {
+          const int64_t c0 = tc_chunk_of(wk.unit(i0 + j), p);
+          int r = 1;
+          while (j + r < cnt && tc_chunk_of(wk.unit(i0 + j + r), p) == c0 + r) ++r;
+          bulk_g2s_plain(dst + j * kChunkWBytes, p.wq + c0 * kChunkWBytes, (uint32_t)r * kChunkWBytes, full_w + slot);
+          bulk_g2s_plain(dst + sec + j * kChunkSBytes, p.ws + c0 * kChunkSBytes, (uint32_t)r * kChunkSBytes,
+                         full_w + slot);
+          if (kAsym)
+            bulk_g2s_plain(dst + sec + (GC + j) * kChunkSBytes, p.wb + c0 * kChunkSBytes, (uint32_t)r * kChunkSBytes,
+                           full_w + slot);
+          j += r;
+        }
         ++issued;
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
-        for (int i = (issued > SW ? issued - SW : 0); i < issued; ++i)
-          if (!mbar_wait_until(full_w + (i % SW), (i / SW) & 1, deadline)) break;
+        for (int q = (issued > WG ? issued - WG : 0); q < issued; ++q)
+          if (!mbar_wait_until(full_w + (q % WG), (q / WG) & 1, deadline)) break;
       }
     }
   } else if (warp == 2) {
@@ -274,10 +326,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       pdl_wait();  // x is written by the previous kernel in the stream
       int issued = 0;
       bool ok = true;
-      const uint32_t xbytes = (uint32_t)p.tn * 128u;
       for (int i = 0; i < n; ++i) {
-        const int s = i % kTcStagesX;
-        if (i >= kTcStagesX && !mbar_wait(empty_x + s, ((i / kTcStagesX) - 1) & 1)) {
+        const int s = i % XS;
+        if (i >= XS && !mbar_wait(empty_x + s, ((i / XS) - 1) & 1)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
           break;
@@ -285,14 +336,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         const int u = wk.unit(i);
         const int tile = u / KT, kt = u - tile * KT;
         const int tb = tile / p.nblk;
-        mbar_arrive_expect_tx(full_x + s, xbytes);
-        tma_load_2d(xs + s * kTcXStageBytes, &tmap_x, kt * 64, tb * p.tn, full_x + s);
+        mbar_arrive_expect_tx(full_x + s, (uint32_t)xstage);
+        tma_load_2d(xs + s * xstage, &tmap_x, kt * 64, tb * p.tn, full_x + s);
         ++issued;
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
-        for (int i = (issued > kTcStagesX ? issued - kTcStagesX : 0); i < issued; ++i)
-          if (!mbar_wait_until(full_x + (i % kTcStagesX), (i / kTcStagesX) & 1, deadline)) break;
+        for (int i = (issued > XS ? issued - XS : 0); i < issued; ++i)
+          if (!mbar_wait_until(full_x + (i % XS), (i / XS) & 1, deadline)) break;
       }
     }
   } else if (warp == 1) {
@@ -315,14 +366,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)(buf * 256);
         for (int u = u0; u < seg_end; ++u, ++i) {
-          const int sx = i % kTcStagesX, s = i % kTcStagesA;
-          if (!mbar_wait(full_x + sx, (i / kTcStagesX) & 1) || !mbar_wait(ddone + s, (i / kTcStagesA) & 1)) {
+          const int sx = i % XS, s = i % AS;
+          if (!mbar_wait(full_x + sx, (i / XS) & 1) || !mbar_wait(ddone + s, (i / AS) & 1)) {
             set_error(p.err, kErrWaitTimeout);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(wa + s * kTcAStageBytes), b0 = smem_u32(xs + sx * kTcXStageBytes);
+          const uint32_t a0 = smem_u32(wa + s * kTcAStageBytes), b0 = smem_u32(xs + sx * xstage);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             tc_mma(dcol, sw128_kmajor_desc(a0 + j * 32), sw128_kmajor_desc(b0 + j * 32), idesc,
@@ -342,21 +393,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     const int d = threadIdx.x - 128;
     bool ok = true;
     for (int i = 0; i < n && ok; ++i) {
-      const int s = i % kTcStagesA, slot = i % SW;
-      if (!mbar_wait(full_w + slot, (i / SW) & 1) ||
-          (i >= kTcStagesA && !mbar_wait(empty_a + s, ((i / kTcStagesA) - 1) & 1))) {
+      const int s = i % AS, q = i / GC, j = i - q * GC, slot = q % WG;
+      if (!mbar_wait(full_w + slot, (q / WG) & 1) || (i >= AS && !mbar_wait(empty_a + s, ((i / AS) - 1) & 1))) {
         set_error(p.err, kErrWaitTimeout);
         ok = false;
         break;
       }
-      const uint8_t* src = wraw + slot * WB;
+      const uint8_t* src = wraw + slot * WB + j * kChunkWBytes;                             // nibbles
+      const uint8_t* ssrc = wraw + slot * WB + GC * kChunkWBytes + j * kChunkSBytes;        // scales
+      const uint8_t* bsrc = wraw + slot * WB + GC * (kChunkWBytes + kChunkSBytes) + j * kChunkSBytes;  // biases
       const uint32_t dst = smem_u32(wa + s * kTcAStageBytes);
 #pragma unroll
       for (int rep = 0; rep < 256 / (32 * kTcDequantWarps); ++rep) {
         const int L = d + rep * 32 * kTcDequantWarps;  // 16-byte lane slot: sub-tile L / 32, lane L % 32
         const int sub = L >> 5, ln = L & 31, g = ln >> 2, t = ln & 3;
         const uint4 v = *reinterpret_cast<const uint4*>(src + L * 16);
-        const uint2 sc = *reinterpret_cast<const uint2*>(src + kChunkWBytes + sub * 64 + g * 8);
+        const uint2 sc = *reinterpret_cast<const uint2*>(ssrc + sub * 64 + g * 8);
         const uint32_t words[4] = {v.x, v.y, v.z, v.w};
         const uint32_t sh[4] = {sc.x & 0xFFFFu, sc.x >> 16, sc.y & 0xFFFFu, sc.y >> 16};  // (g,b0) (g+8,b0) (g,b1) (g+8,b1)
         const bool odd = (g & 1) != 0;
@@ -372,7 +424,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
           const int c = blk * 4 + t;
           uint32_t hv[4];
           if constexpr (kAsym) {  // w = fma(q, scale, bias) in fp16 (kernels.js:36)
-            const uint2 bi = *reinterpret_cast<const uint2*>(src + kChunkWBytes + kChunkSBytes + sub * 64 + g * 8);
+            const uint2 bi = *reinterpret_cast<const uint2*>(bsrc + sub * 64 + g * 8);
             const uint32_t jb = odd ? (jj ^ 2) : jj;
             const uint32_t bbits = ((jb >> 1) ? bi.y : bi.x) >> (16 * (jb & 1)) & 0xFFFFu;
             i4x8_to_h2x4_raw(w, hv);
@@ -393,7 +445,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(ddone + s);
-        mbar_arrive(empty_w + slot);
+        if (j == GC - 1 || i == n - 1) mbar_arrive(empty_w + slot);  // the slot's last chunk is done
       }
     }
   } else if (warp >= kTcEpiWarp0) {
@@ -401,7 +453,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     const int q = warp - kTcEpiWarp0;  // TMEM lane quarter this warp may access (warp % 4)
     const int nl = q * 32 + lane;
     const int et = threadIdx.x - kTcEpiWarp0 * 32;
-    __half* epi_stage = reinterpret_cast<__half*>(smem + kTcOffEpi + q * kTcEpiStageBytes);
+    uint8_t* epi_base = smem + p.sm.off_epi;
+    __half* epi_stage = reinterpret_cast<__half*>(epi_base + q * kTcEpiStageBytes);
     bool failed = false;
     int si = 0;
     for (int i = 0; i < n; ++si) {
@@ -415,20 +468,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       const bool full = (ks == 0 && ke == KT);
       const int tok0 = tb * p.tn;
       const int ncol = nb * 128 + nl;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
       if (!failed && !mbar_wait(accf + buf, (si >> 1) & 1)) {
         set_error(p.err, kErrWaitTimeout);
         failed = true;  // keep walking segments so the named barriers below stay matched
       }
       const int sel = (u0 == wk.sk0) ? 0 : 1;  // partial slot: first or last stream-K segment
-      float* mine = p.partials + (((int64_t)blockIdx.x * 2 + sel) * kTcMaxTn) * 128 + nl;
+      float* mine = p.partials + (((int64_t)blockIdx.x * 2 + sel) * p.tn) * 128 + nl;
       if (p.glu && full) {
         // SiLU*mul: lane quarters q and q + 2 hold the gate and up rows of the same 32 features; each
         // stages its fp16 values, then the pair computes the outputs, 8 tokens each. The pair's two
         // barriers run on every slab even after a failed wait (the partner still arrives).
         const int pq = q & 1;
-        const __half* gs = reinterpret_cast<const __half*>(smem + kTcOffEpi + pq * kTcEpiStageBytes);
-        const __half* us = reinterpret_cast<const __half*>(smem + kTcOffEpi + (pq + 2) * kTcEpiStageBytes);
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
+        const __half* gs = reinterpret_cast<const __half*>(epi_base + pq * kTcEpiStageBytes);
+        const __half* us = reinterpret_cast<const __half*>(epi_base + (pq + 2) * kTcEpiStageBytes);
         if (!failed) tc_fence_after();
         for (int cb = 0; cb < p.tn; cb += 16) {
           if (!failed) {
@@ -463,39 +516,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
           tc_fence_before();
           mbar_arrive(acce + buf);
         }
-      } else if (!failed) {
-        tc_fence_after();
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
-        for (int cb = 0; cb < p.tn; cb += 16) {
-          float v[16];
-          tmem_ld16(taddr + cb, v);
-          if (full && p.vec) {
-            // transpose 32 n x 16 tokens through shared memory, then 16-byte stores of 8 n
+      } else if (full) {
+        if (!failed) {
+          tc_fence_after();
+          for (int cb = 0; cb < p.tn; cb += 16) {
+            float v[16];
+            tmem_ld16(taddr + cb, v);
+            if (p.vec) {
+              // transpose 32 n x 16 tokens through shared memory, then 16-byte stores of 8 n
 #pragma unroll
-            for (int e = 0; e < 16; ++e) epi_stage[e * 32 + lane] = __float2half_rn(v[e]);
-            __syncwarp();
+              for (int e = 0; e < 16; ++e) epi_stage[e * 32 + lane] = __float2half_rn(v[e]);
+              __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int t = j * 8 + (lane >> 2), c = lane & 3;
-              const uint4 val = *reinterpret_cast<const uint4*>(epi_stage + t * 32 + c * 8);
-              const int tok = tok0 + cb + t;
-              const int n0 = nb * 128 + q * 32 + c * 8;
-              if (tok < p.M && n0 < p.N) {
-                const int64_t off = tc_out_off(p, tok, n0);
-                if (n0 + 8 <= p.N) {
-                  *reinterpret_cast<uint4*>(p.ydst[0] + off) = val;
-                  for (int d = 1; d < p.ndst; ++d) *reinterpret_cast<uint4*>(p.ydst[d] + off) = val;
-                } else {
-                  const __half* hv = reinterpret_cast<const __half*>(&val);
+              for (int j = 0; j < 2; ++j) {
+                const int t = j * 8 + (lane >> 2), c = lane & 3;
+                const uint4 val = *reinterpret_cast<const uint4*>(epi_stage + t * 32 + c * 8);
+                const int tok = tok0 + cb + t;
+                const int n0 = nb * 128 + q * 32 + c * 8;
+                if (tok < p.M && n0 < p.N) {
+                  const int64_t off = tc_out_off(p, tok, n0);
+                  if (n0 + 8 <= p.N) {
+                    *reinterpret_cast<uint4*>(p.ydst[0] + off) = val;
+                    for (int d = 1; d < p.ndst; ++d) *reinterpret_cast<uint4*>(p.ydst[d] + off) = val;
+                  } else {
+                    const __half* hv = reinterpret_cast<const __half*>(&val);
 #pragma unroll
-                  for (int k = 0; k < 8; ++k)
-                    if (n0 + k < p.N) tc_store_all(p, off + k, hv[k]);
+                    for (int k = 0; k < 8; ++k)
+                      if (n0 + k < p.N) tc_store_all(p, off + k, hv[k]);
+                  }
                 }
               }
-            }
-            __syncwarp();
-          } else if (full) {
-            if (ncol < p.N) {
+              __syncwarp();
+            } else if (ncol < p.N) {
               const int64_t off0 = tc_out_off(p, tok0 + cb, ncol);
               if (p.ndst == 1) {
 #pragma unroll
@@ -507,37 +559,71 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
                   if (tok0 + cb + e < p.M) tc_store_all(p, off0 + e * p.ldy, __float2half_rn(v[e]));
               }
             }
-          } else {
+          }
+          tc_fence_before();
+          mbar_arrive(acce + buf);
+        }
+      } else if (!kTicketFixup) {
+        // split tile: publish the fp32 partial for tc_fixup_kernel
+        if (!failed) {
+          tc_fence_after();
+          for (int cb = 0; cb < p.tn; cb += 16) {
+            float v[16];
+            tmem_ld16(taddr + cb, v);
 #pragma unroll
             for (int e = 0; e < 16; ++e) __stcg(mine + (int64_t)(cb + e) * 128, v[e]);
           }
+          tc_fence_before();
+          mbar_arrive(acce + buf);
         }
-        tc_fence_before();
-        mbar_arrive(acce + buf);
-      }
-      if (kTicketFixup && !full) {
-        // barrier, then one release/acquire ticket by thread 0
-        named_bar_sync(2, 128);
+      } else {
+        // split tile finished in this kernel by the part that arrives last. A part that sees every
+        // other part already published (acquire peek) adds them to its own sums straight from TMEM;
+        // otherwise it publishes its partial and takes a ticket (release/acquire), and the part whose
+        // ticket completes the count sums all published partials. Either way the parts are added in
+        // part order (the CTAs' order), so the result does not depend on which part came last.
         const int first = tc_cta_of(tile * KT, p), last = tc_cta_of(tile * KT + KT - 1, p);
-        if (et == 0) {
-          const uint32_t prev = atom_add_acq_rel_gpu(p.tickets + tile, 1u);
-          *s_flag = (prev == (uint32_t)(last - first)) ? 1 : 0;
-        }
+        const int nparts = last - first + 1;
+        if (et == 0) s_flag[0] = (!failed && ld_acquire_gpu_u32(p.tickets + tile) == (uint32_t)(nparts - 1)) ? 1 : 0;
         named_bar_sync(2, 128);
-        if (*s_flag) {
+        int mode = s_flag[0];  // 1: last, own sums in TMEM; 2: last, own sums published; 0: not last
+        if (mode == 0) {
+          if (!failed) {
+            tc_fence_after();
+            for (int cb = 0; cb < p.tn; cb += 16) {
+              float v[16];
+              tmem_ld16(taddr + cb, v);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) __stcg(mine + (int64_t)(cb + e) * 128, v[e]);
+            }
+            tc_fence_before();
+            mbar_arrive(acce + buf);
+          }
+          named_bar_sync(2, 128);  // every thread's partial is written before the ticket (release)
+          if (et == 0)
+            s_flag[1] = (!failed && atom_add_acq_rel_gpu(p.tickets + tile, 1u) == (uint32_t)(nparts - 1)) ? 2 : 0;
+          named_bar_sync(2, 128);
+          mode = s_flag[1];
+        }
+        if (mode != 0) {
           const int rows = min(p.tn, p.M - tok0);
-          // 16 tokens at a time: the loads of one CTA's partial are independent, and CTAs are
-          // summed in order (deterministic)
+          if (mode == 1) tc_fence_after();
           for (int t0 = 0; t0 < rows; t0 += 16) {
-            float acc[16];
+            float own[16], acc[16];
+            if (mode == 1) tmem_ld16(taddr + t0, own);
 #pragma unroll
             for (int e = 0; e < 16; ++e) acc[e] = 0.f;
             for (int b = first; b <= last; ++b) {
-              const int bsel = (tc_begin(b, p) >= tile * KT) ? 0 : 1;
-              const float* src = p.partials + (((int64_t)b * 2 + bsel) * kTcMaxTn + t0) * 128 + nl;
               float v[16];
+              if (mode == 1 && b == (int)blockIdx.x) {
 #pragma unroll
-              for (int e = 0; e < 16; ++e) v[e] = (t0 + e < rows) ? __ldcg(src + e * 128) : 0.f;
+                for (int e = 0; e < 16; ++e) v[e] = own[e];
+              } else {
+                const int bsel = (tc_begin(b, p) >= tile * KT) ? 0 : 1;
+                const float* src = p.partials + (((int64_t)b * 2 + bsel) * p.tn + t0) * 128 + nl;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = (t0 + e < rows) ? __ldcg(src + e * 128) : 0.f;
+              }
 #pragma unroll
               for (int e = 0; e < 16; ++e) acc[e] += v[e];
             }
@@ -547,9 +633,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
                 if (t0 + e < rows) tc_store_all(p, tc_out_off(p, tok0 + t0 + e, ncol), __float2half_rn(acc[e]));
             }
           }
-          named_bar_sync(2, 128);
-          if (et == 0) atomicExch(p.tickets + tile, 0u);
+          if (mode == 1) {
+            tc_fence_before();
+            mbar_arrive(acce + buf);
+          }
+          if (et == 0) atomicExch(p.tickets + tile, 0u);  // every part has arrived: ready for the next call
         }
+        named_bar_sync(2, 128);  // the flags are read by every thread before the next segment writes them
       }
     }
   }
@@ -596,7 +686,7 @@ __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcParams p) {
       const int bb = b0 + j;
       if (bb <= last) {
         const int bsel = (tc_begin(bb, p) >= tile * KT) ? 0 : 1;
-        const float* src = p.partials + (((int64_t)bb * 2 + bsel) * kTcMaxTn + r0) * 128 + nl;
+        const float* src = p.partials + (((int64_t)bb * 2 + bsel) * p.tn + r0) * 128 + nl;
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[j][e] = (r0 + e < rows) ? __ldcg(src + e * 128) : 0.f;
       }
@@ -700,14 +790,12 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
   const int64_t total = (int64_t)p.ntb * nblk * ktiles;
   if (total > INT32_MAX) return cudaErrorInvalidValue;
   p.total = (int)total;
+  if (grid < 1) return cudaErrorInvalidValue;
   p.grid = grid < p.total ? grid : p.total;
   const int tiles = p.ntb * nblk;
-  // fewer tiles than CTAs but at least 60 % as many: one whole tile per CTA (the idle SMs cost less
-  // than splitting every tile and fixing it up: gate|up at M = 64..256, 96 tiles for 148 SMs, ran
-  // 7-22 % faster whole; at 65 tiles for 148 SMs splitting still won)
-  if (tiles < p.grid && tiles * 5 >= p.grid * 3) p.grid = tiles;
   // the fused SiLU*mul epilogue stores 8 outputs at a time and has no in-kernel ticket fix-up
   if (glu && (!p.vec || ticket_fixup || N % 128)) return cudaErrorInvalidValue;
+  p.sm = tc_plan_smem(tn, wb != nullptr);
   p.dpq = tiles / p.grid;
   p.sk_base = p.dpq * p.grid * ktiles;
   p.sk_total = p.total - p.sk_base;
@@ -722,26 +810,27 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
 
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(tc_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    e = cudaFuncSetAttribute(tc_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tc_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+      e = cudaFuncSetAttribute(tc_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tc_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+      e = cudaFuncSetAttribute(tc_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tc_gemm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+      e = cudaFuncSetAttribute(tc_gemm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
+  if (p.sm.bytes > kTcSmemMax) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid, 1, 1);
   cfg.blockDim = dim3(kTcThreads, 1, 1);
-  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.dynamicSmemBytes = p.sm.bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -790,14 +879,26 @@ constexpr size_t kStaticTicketCount = 16384;                             // tile
 constexpr size_t kStaticErrOffset = kStaticTicketCount * sizeof(uint32_t);
 constexpr size_t kStaticPartialOffset = kStaticErrOffset + 256;
 constexpr size_t kStaticPartialBytes = kStaticScratchBytes - kStaticPartialOffset;
-constexpr size_t kPartialBytesPerCta = 2ull * s4::kTcMaxTn * 128 * sizeof(float);  // two slots of 256 x 128 fp32
-constexpr int kStaticMaxGrid = (int)(kStaticPartialBytes / kPartialBytesPerCta);
 }  // namespace
 
 static __device__ __align__(256) unsigned char g_s4_static_scratch[kStaticScratchBytes];
 
-// Device address of g_s4_static_scratch per device; the symbol itself names a host-side stand-in.
-static void* g_static_scratch_addr[64];
+// Device address of g_s4_static_scratch per device (the symbol itself names a host-side stand-in).
+// Looked up by the first call on each device; concurrent first calls store the same address.
+static std::atomic<void*> g_static_scratch_addr[64];
+
+static int static_scratch(int dev, uint8_t** base) {
+  void* ptr = g_static_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!ptr) {
+    // set-up, once per device, with that device current
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_s4_static_scratch);
+    if (e != cudaSuccess || !ptr)
+      return s4::record_error(S4_ERR_CUDA, "s4_matmul_noalloc: cudaGetSymbolAddress of the static scratch failed");
+    g_static_scratch_addr[dev].store(ptr, std::memory_order_release);
+  }
+  *base = static_cast<uint8_t*>(ptr);
+  return S4_OK;
+}
 
 extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void* y, void* stream) {
   using namespace s4;
@@ -808,7 +909,8 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   if (w->glu) return record_error(S4_ERR_UNSUPPORTED, "s4_matmul_noalloc: fused gate|up weights run through s4_matmul");
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
     return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: x and y must be 16-byte aligned");
-  const int dev = w->ctx->device;
+  // the weight records its own device and SM count: the call needs no live context
+  const int dev = w->device;
   if (dev < 0 || dev >= 64) return record_error(S4_ERR_INVALID, "s4_matmul_noalloc: device ordinal out of range");
   const int tn = M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16;
   const long long tiles = (long long)((M + tn - 1) / tn) * w->nblk;
@@ -822,26 +924,38 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   }
   DeviceGuard guard(dev);
   if (!guard.ok) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: cudaSetDevice failed");
-  if (!g_static_scratch_addr[dev]) {
-    // set-up, once per device, with that device current
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_s4_static_scratch);
-    if (e != cudaSuccess || !ptr)
-      return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: cudaGetSymbolAddress of the static scratch failed");
-    g_static_scratch_addr[dev] = ptr;
-  }
-  uint8_t* base = static_cast<uint8_t*>(g_static_scratch_addr[dev]);
+  uint8_t* base = nullptr;
+  int rc = static_scratch(dev, &base);
+  if (rc != S4_OK) return rc;
   uint32_t* tickets = reinterpret_cast<uint32_t*>(base);
   uint32_t* err = reinterpret_cast<uint32_t*>(base + kStaticErrOffset);
   float* partials = reinterpret_cast<float*>(base + kStaticPartialOffset);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // the previous call left its counters at zero unless it failed part-way: clear what must start at zero
+  // the previous call left its counters at zero unless it failed part-way: clear what must start at
+  // zero. The error word is left as it is: it accumulates until s4_noalloc_check_errors clears it.
   cudaError_t e = cudaMemsetAsync(base, 0, (size_t)tiles * sizeof(uint32_t), st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(err, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: clearing the static scratch failed");
-  const int grid = w->ctx->sm_count < kStaticMaxGrid ? w->ctx->sm_count : kStaticMaxGrid;
+  // partials: two slots of tn x 128 fp32 per CTA
+  const int max_grid = (int)(kStaticPartialBytes / (2ull * tn * 128 * sizeof(float)));
+  const int grid = w->sm_count < max_grid ? w->sm_count : max_grid;
   e = launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
                      (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true, true, 0);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: tcgen05 GEMM launch failed");
+  return S4_OK;
+}
+
+extern "C" int s4_noalloc_check_errors(int device, uint32_t* flags, int clear) {
+  using namespace s4;
+  if (!flags) return record_error(S4_ERR_INVALID, "s4_noalloc_check_errors: NULL flags");
+  if (device < 0 || device >= 64) return record_error(S4_ERR_INVALID, "s4_noalloc_check_errors: bad device");
+  DeviceGuard guard(device);
+  if (!guard.ok) return record_error(S4_ERR_CUDA, "s4_noalloc_check_errors: cudaSetDevice failed");
+  uint8_t* base = nullptr;
+  int rc = static_scratch(device, &base);
+  if (rc != S4_OK) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(flags, base + kStaticErrOffset, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear) e = cudaMemset(base + kStaticErrOffset, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_noalloc_check_errors: reading the error word failed");
   return S4_OK;
 }

@@ -11,12 +11,21 @@ namespace s4 {
 // Sets the calling thread's s4_last_error() message and returns `code`.
 int record_error(int code, const char* msg);
 
+// One entry of the dispatch table: calls with M <= max_m on a weight of K columns and N rows (0 =
+// any) use `family`; for the tcgen05 GEMM, `tile` tokens per tile and `split` CTAs (0 = automatic),
+// split tiles summed by a second kernel or by their last CTA (`fixup`, kFixup*).
 struct Bucket {
   int max_m;
   int family;
   int tile;
   int split;
+  int fixup = 0;
+  int K = 0;
+  int N = 0;
 };
+constexpr int kFixupAuto = 0;
+constexpr int kFixupKernel = 1;
+constexpr int kFixupCta = 2;
 
 // Restores the caller's current device on scope exit.
 struct DeviceGuard {
@@ -45,15 +54,17 @@ struct s4_ctx {
   size_t dx_cap = 0, dy_cap = 0;
   double* wire_pow = nullptr;     // 2^(-r/4096) table of the wire scale decoder (first wire call)
   std::vector<s4::Bucket> table;
-  s4::Bucket forced{0, S4_FAMILY_AUTO, 0, 0};
+  s4::Bucket forced{0, S4_FAMILY_AUTO, 0, 0, 0, 0, 0};
   uint64_t launches = 0;
   bool pdl = true;    // launch with programmatic dependent launch (env S4_PDL=0 turns it off)
-  bool ticket_fixup = false;  // split tcgen05 tiles summed by their last CTA in-kernel (env S4_TICKET_FIXUP=1)
+  int ticket_fixup = -1;  // split tcgen05 tiles: -1 by the table / automatic rule, 1 always summed by their
+                          // last CTA in-kernel, 0 always by the fix-up kernel (env S4_TICKET_FIXUP=1 / 0)
 };
 
 struct s4_weight {
   s4_ctx* ctx = nullptr;
   int device = -1;  // the context's device: freeing or reading back the weight needs no live context
+  int sm_count = 0;  // the device's SM count (the allocation-free matmul sizes its grid without a context)
   int N = 0, K = 0, nblk = 0, ktiles = 0;
   uint8_t* wq = nullptr;
   uint8_t* ws = nullptr;

@@ -95,19 +95,37 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 namespace {
 
-std::vector<Bucket> default_table() {
-  // M-bucket table (replaces engine.js:17-33). GEMV up to 16 tokens; tcgen05 GEMM above when the
-  // kernel is built in, else repeated GEMV launches of 16 tokens.
+std::vector<Bucket> fallback_table() {
+  // GEMV up to 16 tokens; tcgen05 GEMM above when the kernel is built in, else repeated GEMV
+  // launches of 16 tokens.
   std::vector<Bucket> t;
   t.push_back({kGemvMaxM, S4_FAMILY_GEMV, 0, 0});
   t.push_back({INT_MAX, s4::tc_available() ? S4_FAMILY_TC : S4_FAMILY_GEMV, 0, 0});
   return t;
 }
 
-Bucket choose(const s4_ctx* ctx, int M) {
+bool parse_table(const char* text, std::vector<Bucket>& out, std::string& why);
+
+// The built-in M-bucket table (replaces engine.js:17-33): the measured table tune.py wrote into
+// dispatch_table.inc, else the fallback above. Environment S4_TABLE=fallback selects the fallback.
+std::vector<Bucket> default_table() {
+#if __has_include("dispatch_table.inc")
+#include "dispatch_table.inc"
+  const char* env = getenv("S4_TABLE");
+  if (!(env && strcmp(env, "fallback") == 0)) {
+    std::vector<Bucket> t;
+    std::string why;
+    if (parse_table(kDispatchTableJson, t, why)) return t;
+  }
+#endif
+  return fallback_table();
+}
+
+// The first bucket whose max_m covers M and whose K / N (when given) match the weight.
+Bucket choose(const s4_ctx* ctx, int M, int N, int K) {
   if (ctx->forced.family != S4_FAMILY_AUTO) return ctx->forced;
   for (const Bucket& b : ctx->table)
-    if (M <= b.max_m) return b;
+    if (M <= b.max_m && (b.K == 0 || b.K == K) && (b.N == 0 || b.N == N)) return b;
   return ctx->table.empty() ? Bucket{INT_MAX, S4_FAMILY_GEMV, 0, 0} : ctx->table.back();
 }
 
@@ -204,10 +222,17 @@ bool parse_table(const char* text, std::vector<Bucket>& out, std::string& why) {
           if (k == "family") {
             std::string f;
             if (!j.str(f) || (b.family = parse_family(f)) < 0) return why = "family must be \"gemv\" or \"tc\"", false;
-          } else if (k == "max_m" || k == "tile" || k == "split") {
+          } else if (k == "fixup") {
+            std::string f;
+            if (!j.str(f)) return why = "fixup must be a string", false;
+            if (f == "auto") b.fixup = s4::kFixupAuto;
+            else if (f == "kernel") b.fixup = s4::kFixupKernel;
+            else if (f == "cta") b.fixup = s4::kFixupCta;
+            else return why = "fixup must be \"auto\", \"kernel\" or \"cta\"", false;
+          } else if (k == "max_m" || k == "tile" || k == "split" || k == "K" || k == "N") {
             long long v;
             if (!j.num(v) || v < 0 || v > INT_MAX) return why = "bad number in bucket", false;
-            (k == "max_m" ? b.max_m : k == "tile" ? b.tile : b.split) = (int)v;
+            (k == "max_m" ? b.max_m : k == "tile" ? b.tile : k == "split" ? b.split : k == "K" ? b.K : b.N) = (int)v;
           } else if (!j.skip_value()) {
             return why = "bad value", false;
           }
@@ -215,7 +240,14 @@ bool parse_table(const char* text, std::vector<Bucket>& out, std::string& why) {
         }
         if (b.family < 0) return why = "bucket without family", false;
         if (b.family == S4_FAMILY_TC && !s4::tc_available()) return why = "tc family is not built", false;
-        if (!out.empty() && b.max_m <= out.back().max_m) return why = "max_m must increase", false;
+        if (b.family == S4_FAMILY_TC && b.tile != 0 && (b.tile < 16 || b.tile > 256 || b.tile % 16))
+          return why = "tc tile must be 0 or a multiple of 16 in [16, 256]", false;
+        // within one (K, N) key the buckets go up in M
+        for (auto it = out.rbegin(); it != out.rend(); ++it)
+          if (it->K == b.K && it->N == b.N) {
+            if (b.max_m <= it->max_m) return why = "max_m must increase", false;
+            break;
+          }
         out.push_back(b);
         j.lit(',');
       }
@@ -225,7 +257,13 @@ bool parse_table(const char* text, std::vector<Bucket>& out, std::string& why) {
     j.lit(',');
   }
   if (!found || out.empty()) return why = "no buckets", false;
-  out.back().max_m = INT_MAX;  // the last bucket covers every larger M
+  // the last bucket for any shape covers every larger M; shape-specific buckets (K or N given) keep
+  // their limit, and larger calls on those shapes fall through to the general buckets
+  int last_any = -1;
+  for (int i = 0; i < (int)out.size(); ++i)
+    if (out[i].K == 0 && out[i].N == 0) last_any = i;
+  if (last_any < 0) return why = "no bucket for every shape (one without K and N)", false;
+  out[last_any].max_m = INT_MAX;
   return true;
 }
 
@@ -235,6 +273,7 @@ int upload_common(s4_ctx* ctx, const void* packed_dev, const void* scales_dev, i
   if (!w) return fail(S4_ERR_NOMEM, "out of host memory");
   w->ctx = ctx;
   w->device = ctx->device;
+  w->sm_count = ctx->sm_count;
   w->N = N;
   w->K = K;
   w->glu = glu_I > 0;
@@ -324,7 +363,7 @@ int s4_init(int device, s4_ctx** out) {
   ctx->sm_count = prop.multiProcessorCount;
   ctx->table = default_table();
   if (const char* v = getenv("S4_PDL")) ctx->pdl = (v[0] != '0');
-  if (const char* v = getenv("S4_TICKET_FIXUP")) ctx->ticket_fixup = (v[0] == '1');
+  if (const char* v = getenv("S4_TICKET_FIXUP")) ctx->ticket_fixup = (v[0] == '1') ? 1 : 0;
   e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
   const size_t part_bytes = s4::tc_partials_bytes(ctx->sm_count);
   if (e == cudaSuccess) e = cudaMalloc(&ctx->partials, part_bytes);
@@ -691,6 +730,7 @@ int s4_weight_load(s4_ctx* ctx, const char* path, s4_weight** out) {
   }
   w->ctx = ctx;
   w->device = ctx->device;
+  w->sm_count = ctx->sm_count;
   w->N = h.N;
   w->K = h.K;
   w->glu = (h.flags & 2u) ? 1 : 0;
@@ -759,6 +799,24 @@ static int auto_tile(int M, const s4_weight* w, int sms) {
   return 256;
 }
 
+// Split tiles of a (tn, grid) launch summed by their last CTA (in-kernel) or by the fix-up kernel:
+// the table's choice, else the environment's (S4_TICKET_FIXUP), else in-kernel when no tile is cut
+// into more than three parts (the last CTA then adds at most two published partials to its own
+// sums; with more parts one CTA would read them all, and the fix-up kernel spreads that work over
+// the grid). Fused gate|up weights always use the fix-up kernel (it pairs gate and up rows).
+static bool use_cta_fixup(const Bucket& b, const s4_ctx* ctx, const s4_weight* w, int M, int tn, int grid) {
+  if (w->glu) return false;
+  if (b.fixup == s4::kFixupCta) return true;
+  if (b.fixup == s4::kFixupKernel) return false;
+  if (ctx->ticket_fixup >= 0) return ctx->ticket_fixup == 1;
+  const long long tiles = (long long)((M + tn - 1) / tn) * w->nblk, total = tiles * w->ktiles;
+  const long long g = grid < total ? grid : total;
+  const long long sk = total - (tiles / g) * g * w->ktiles;  // stream-K units
+  if (sk == 0) return true;                                   // nothing is split
+  const long long per = sk / g > 0 ? sk / g : 1;
+  return (w->ktiles + per - 1) / per + 1 <= 3;
+}
+
 // Tile size and CTA count together. Two cases where whole tiles packed into whole waves beat the
 // default split (measured on gate|up, down, out_proj): (1) 256-token tiles fit in one wave: as many
 // token blocks as fit, if their tiles stay >= 224 tokens (down / out_proj M = 2048: 144 tiles of 240
@@ -785,6 +843,11 @@ static void auto_shape(int M, const s4_weight* w, int sms, int* tn_out, int* gri
       }
     }
   }
+  // fewer tiles than CTAs but at least 60 % as many: one whole tile per CTA (the idle SMs cost less
+  // than splitting every tile and fixing it up: gate|up at M = 64..256, 96 tiles for 148 SMs, ran
+  // 7-22 % faster whole; at 65 tiles for 148 SMs splitting still won)
+  const long long tiles = (long long)((M + tn - 1) / tn) * nb;
+  if (tiles < grid && tiles * 5 >= (long long)grid * 3) grid = (int)tiles;
   *tn_out = tn;
   *grid_out = grid;
 }
@@ -799,7 +862,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
     return fail(S4_ERR_INVALID, "x and y must be 16-byte aligned");
   DeviceGuard guard(ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const Bucket b = choose(ctx, M);
+  const Bucket b = choose(ctx, M, w->N, w->K);
   cudaError_t e = cudaSuccess;
   if (b.family == S4_FAMILY_TC) {
     if (b.tile != 0 && (b.tile < 16 || b.tile > 256 || b.tile % 16))
@@ -814,8 +877,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
       e = s4::launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x) + r0 * w->K,
                              static_cast<__half*>(y) + r0 * (w->glu ? w->N / 2 : w->N), ctx->partials, ctx->tickets,
                              kMaxTickets, ctx->err, rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl,
-                             ctx->ticket_fixup && !w->glu,
-                             w->glu);
+                             use_cta_fixup(b, ctx, w, rows, tn, grid), w->glu);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
       ++ctx->launches;
     }
@@ -1063,12 +1125,25 @@ int s4_peer_barrier(s4_ctx* ctx, void* const* flags, int nranks, int rank, uint3
 
 int s4_plan(s4_ctx* ctx, int M, int N, int K, int* family, int* tile, int* split) {
   if (!ctx) return fail(S4_ERR_INVALID, "NULL context");
-  (void)N;
-  (void)K;
-  const Bucket b = choose(ctx, M < 1 ? 1 : M);
+  if (M < 1) M = 1;
+  const Bucket b = choose(ctx, M, N, K);
+  int t = b.tile, g = b.split;
+  if (b.family == S4_FAMILY_TC && N > 0 && K > 0) {
+    // the tile and CTA count the call would launch with
+    s4_weight w;
+    w.N = N;
+    w.K = K;
+    w.nblk = (N + s4::kRowsPerBlock - 1) / s4::kRowsPerBlock;
+    w.ktiles = (K + s4::kKPerTile - 1) / s4::kKPerTile;
+    int tn = t, grid = ctx->sm_count;
+    if (tn == 0) auto_shape(M, &w, ctx->sm_count, &tn, &grid);
+    if (g > 0) grid = std::min(g, ctx->sm_count);
+    t = tn;
+    g = grid;
+  }
   if (family) *family = b.family;
-  if (tile) *tile = b.tile;
-  if (split) *split = b.split;
+  if (tile) *tile = t;
+  if (split) *split = g;
   return S4_OK;
 }
 
@@ -1080,15 +1155,19 @@ int s4_force(s4_ctx* ctx, int family, int tile, int split) {
   if (tile < 0 || split < 0) return fail(S4_ERR_INVALID, "tile and split must be >= 0");
   if (family == S4_FAMILY_GEMV && split > s4::gemv_max_split())
     return fail(S4_ERR_INVALID, "GEMV split %d exceeds %d", split, s4::gemv_max_split());
-  ctx->forced = Bucket{INT_MAX, family, tile, split};
+  ctx->forced = Bucket{INT_MAX, family, tile, split, s4::kFixupAuto, 0, 0};
   return S4_OK;
 }
 
 int s4_set_table(s4_ctx* ctx, const char* json) {
-  if (!ctx || !json) return fail(S4_ERR_INVALID, "NULL argument");
+  if (!ctx) return fail(S4_ERR_INVALID, "NULL argument");
   std::vector<Bucket> t;
   std::string why;
   try {
+    if (!json) {
+      ctx->table = default_table();  // back to the built-in table
+      return S4_OK;
+    }
     if (!parse_table(json, t, why)) return fail(S4_ERR_INVALID, "dispatch table: %s", why.c_str());
   } catch (const std::bad_alloc&) {
     return fail(S4_ERR_NOMEM, "dispatch table: out of host memory");

@@ -55,6 +55,7 @@ _SIGS = {
     "s4_matmul_host": (C.c_int, [_P, _P, _P, C.c_int, _P]),
     "s4_matmul_host_async": (C.c_int, [_P, _P, _P, C.c_int, _P, _P]),
     "s4_matmul_noalloc": (C.c_int, [_P, _P, C.c_int, _P, _P]),
+    "s4_noalloc_check_errors": (C.c_int, [C.c_int, C.POINTER(C.c_uint32), C.c_int]),
     "s4_silu_mul": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
     "s4_add_rmsnorm": (C.c_int, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_float, _P, _P]),
     "s4_chain_create": (C.c_int, [_P, C.c_int, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(C.c_int),
@@ -498,7 +499,12 @@ class Context:
         _check(_lib.s4_force(self.handle, int(family), int(tile), int(split)))
 
     def set_table(self, table):
+        """Load a dispatch table (dict or JSON text, the format of ``dispatch_table.json``); None
+        restores the library's built-in table."""
         import json
+        if table is None:
+            _check(_lib.s4_set_table(self.handle, None))
+            return
         text = table if isinstance(table, str) else json.dumps(table)
         _check(_lib.s4_set_table(self.handle, text.encode()))
 

@@ -98,3 +98,50 @@ def test_whole_wave_tile_shapes(ctx, K, N, M):
     _, ref = s4ref.matmul(x, packed, scales)
     _check(_run(ctx, W, x), ref, f"K={K} N={N} M={M}")
     W.free()
+
+
+@pytest.mark.parametrize("K,N", [(6144, 2048), (2048, 12288), (2048, 3072)])
+@pytest.mark.parametrize("M", [16, 64, 130, 300])
+@pytest.mark.parametrize("grid", [148, 37])
+def test_tc_fixup_modes(ctx, K, N, M, grid):
+    """Split tiles summed by the fix-up kernel or by their last CTA (in-kernel, either straight from
+    TMEM or from the published partials): both meet the tolerance and are bitwise identical, since
+    both add the parts in CTA order."""
+    rng = np.random.default_rng(K + N + M + grid)
+    packed, scales = s4ref.config_weights(rng, K, N)
+    W = ctx.upload(packed, scales, N, K)
+    x = s4ref.config_x(rng, M, K)
+    _, ref = s4ref.matmul(x, packed, scales)
+    outs = {}
+    try:
+        for fx in ("kernel", "cta"):
+            ctx.set_table({"buckets": [{"max_m": 1 << 30, "family": "tc", "split": grid, "fixup": fx}]})
+            for rep in range(2):  # twice: the tickets must be back at zero after each call
+                outs[(fx, rep)] = _run(ctx, W, x)
+                _check(outs[(fx, rep)], ref, f"K={K} N={N} M={M} grid={grid} fixup={fx} call {rep}")
+    finally:
+        ctx.set_table(None)
+    for k, v in outs.items():
+        np.testing.assert_array_equal(v.view(np.uint16), outs[("kernel", 0)].view(np.uint16), err_msg=str(k))
+    assert ctx.check_errors() == 0
+    W.free()
+
+
+def test_table_shape_buckets(ctx):
+    """Buckets with K / N apply to their shape only; other shapes fall through to the general ones;
+    s4_plan reports the tile and CTA count a tcgen05 call launches with."""
+    try:
+        ctx.set_table({"buckets": [
+            {"max_m": 64, "K": 6144, "N": 2048, "family": "tc", "tile": 32, "split": 100, "fixup": "cta"},
+            {"max_m": 16, "family": "gemv"}, {"max_m": 1 << 30, "family": "tc"}]})
+        assert ctx.plan(64, 2048, 6144) == ("tc", 32, 100)
+        assert ctx.plan(65, 2048, 6144)[0] == "tc" and ctx.plan(65, 2048, 6144)[1] == 80
+        assert ctx.plan(8, 2048, 6144) == ("tc", 32, 100)
+        assert ctx.plan(8, 3072, 2048)[0] == "gemv"
+        assert ctx.plan(64, 3072, 2048)[0] == "tc"
+        with pytest.raises(Exception):
+            ctx.set_table({"buckets": [{"max_m": 64, "K": 6144, "family": "tc"}]})  # no general bucket
+        with pytest.raises(Exception):
+            ctx.set_table({"buckets": [{"max_m": 64, "family": "tc", "fixup": "sometimes"}]})
+    finally:
+        ctx.set_table(None)
