@@ -919,6 +919,70 @@ def run_stack(args, rank, world, local_rank):
     return 0
 
 
+GEMM_SHAPES = {"qkvz_ab": (2048, 8224), "attn_qkv": (2048, 3072), "gate_up": (2048, 12288), "down": (6144, 2048),
+               "out_proj": (2048, 2048)}
+
+
+def run_gemm(args, rank, world, local_rank):
+    """One (shape, M) matmul through s4_matmul (BASELINE configs 1 and 3), back to back over rotating
+    device copies of the weight whose bytes exceed twice the L2, replayed from one CUDA graph per
+    step of 64 calls: GB/s and TFLOP/s of the algorithmic work. The small, single-kernel command the
+    ncu captures of the mid-M and prefill kernels run."""
+    import numpy as np
+    import torch
+    from oracle import s4ref
+
+    if world > 1:
+        print(json.dumps({"workload": "gemm", "skipped": "single-GPU measurement"}) if rank == 0 else "")
+        return 0
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    pkg = load_pkg()
+    ctx = pkg.Context(local_rank)
+    K, N = GEMM_SHAPES[args.shape]
+    M = args.m
+    rng = np.random.default_rng(0)
+    packed, scales = s4ref.config_weights(rng, K, N)
+    copies = max(8, -(-2 * L2_BYTES // (N * K // 2 + N * K // 16)))
+    pd, sd = torch.from_numpy(packed).to(dev), torch.from_numpy(scales).to(dev)
+    Ws = [ctx.upload(pd, sd, N, K) for _ in range(copies)]
+    x = torch.from_numpy(s4ref.config_x(rng, M, K)).to(dev)
+    y = torch.empty((M, N), dtype=torch.float16, device=dev)
+    reps = 64
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for r in range(reps):
+            ctx.matmul(x, Ws[r % copies], M, y)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        a.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+    us = a.elapsed_time(b) * 1e3 / (args.steps * reps)
+    _, ref = s4ref.matmul(x.cpu().numpy(), packed, scales)
+    ok, mr, mc = s4ref.check(y.cpu().numpy(), ref)
+    hbm, tc_peak, peak_kind = peaks()
+    alg = N * K // 2 + N * K // 16 + 2 * M * K + 2 * M * N
+    fam, tile, split = ctx.plan(M, N, K)
+    print(json.dumps({"workload": "gemm", "shape": args.shape, "K": K, "N": N, "M": M, "us": us,
+                      "GBps": alg / us / 1e3, "TFLOPs": 2.0 * M * N * K / us / 1e6,
+                      "hbm_frac": alg / us / 1e3 / hbm, "tensor_frac": 2.0 * M * N * K / us / 1e6 / tc_peak,
+                      "peak_kind": peak_kind, "family": fam, "tile": tile, "split": split, "weight_copies": copies,
+                      "calls_per_step": reps, "steps": args.steps, "warmup": args.warmup,
+                      "parity": {"ok": bool(ok), "max_rel": mr, "min_cos": mc}, "clocks": clk.summary()}))
+    if ctx.check_errors():
+        raise RuntimeError("device error word set")
+    del g
+    ctx.close()
+    return 0
+
+
 # formats: the non-default weight formats, the online FWHT and the wire scale decode, measured
 FORMATS = [(4, 32, False), (2, 32, False), (3, 32, False), (4, 64, False), (2, 64, True), (4, 32, True),
            (3, 64, True)]
@@ -1021,11 +1085,12 @@ def main():
     ap.add_argument("--no-stack", action="store_true", help="skip the stack and serving keys of the decode line")
     ap.add_argument("--family", choices=["auto", "gemv", "tc"], default="auto",
                     help="pin the kernel family instead of the dispatch table")
-    ap.add_argument("--workload", choices=["decode", "stack", "serve", "formats"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "stack", "serve", "formats", "gemm"], default="decode",
                     help="decode: configs[1] GEMV sweep (default); stack: config 4, one 2048-token prompt "
                          "through the 24-layer linear stack, column-sharded over the ranks; serve: config 5, "
                          "requests sharded over the ranks (weights replicated); formats: the non-default weight "
-                         "formats, FWHT and wire scale decode (one GPU)")
+                         "formats, FWHT and wire scale decode (one GPU); gemm: one (--shape, --m) matmul back to "
+                         "back (one GPU)")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="stack: fuse the all-gathers into the producing kernels (peer stores over NVLink) or "
                          "call NCCL all-gather after every projection")
@@ -1033,6 +1098,8 @@ def main():
                     help="stack: replay the whole forward as one CUDA graph (1, default) or launch eagerly (0)")
     ap.add_argument("--fuse-silu", type=int, default=1,
                     help="stack/serve: SiLU*mul in the gate|up GEMM epilogue (1, default) or as its own kernel (0)")
+    ap.add_argument("--shape", choices=sorted(GEMM_SHAPES), default="gate_up", help="gemm: the projection shape")
+    ap.add_argument("--m", type=int, default=64, help="gemm: tokens per call")
     ap.add_argument("--requests", type=int, default=512,
                     help="serve: number of config-5 requests timed per step (the first n of the seeded 4096)")
     args = ap.parse_args()
@@ -1049,6 +1116,8 @@ def main():
         return run_stack(args, rank, world, local_rank)
     if args.workload == "formats":
         return run_formats(args, rank, world, local_rank)
+    if args.workload == "gemm":
+        return run_gemm(args, rank, world, local_rank)
     return run_ours(args, rank, world, local_rank)
 
 

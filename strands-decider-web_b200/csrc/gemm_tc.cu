@@ -14,20 +14,14 @@
 // of the remaining T mod G tiles are cut into G equal stream-K ranges, so every SM gets the same
 // number of MMAs and only those last tiles can be split. A run of units of one tile is a segment; a
 // segment that covers the whole K range is written as fp16 directly, otherwise its fp32 partial goes
-// to scratch and a fix-up kernel launched right after sums the partials of each split tile in CTA
-// order (the allocation-free entry point instead lets the last CTA to arrive at the tile do it,
-// through an atomic ticket).
+// to scratch and either a fix-up kernel launched right after sums the partials of each split tile in
+// CTA order, or the last CTA to arrive at the tile does it in this kernel (atomic ticket; the
+// dispatcher's choice, and always for the allocation-free entry point).
 //
-// Warp roles (512 threads): warp 0 lane 0 streams raw int4 chunks into a ring of weight slots of
-// kTcGroup chunks each (one 1-D bulk copy per contiguous run of chunks and array); warp 2 lane 0
-// loads activation tiles by TMA into a ring of activation stages; warp 1 owns TMEM and lane 0 issues
-// the MMAs; warps 4-11 dequantise int4 -> fp16 into the MMA's A stage; warps 12-15 drain TMEM
-// (double-buffered accumulators) and write the output.
-//
-// Shared memory is planned on the host per tile width (tc_plan_smem): an activation stage is
-// tn x 128 bytes, so narrow tiles (mid-M calls) get many more stages (up to 16) than 256-token tiles
-// (3). An activation stage comes from L2 and feeds only 4 MMAs of a few dozen cycles at tn <= 64, so a
-// shallow ring leaves the tensor core waiting on L2 latency at every k-tile.
+// Warp roles (512 threads): warp 0 lane 0 streams raw int4 chunks (1-D bulk copies) into a
+// kTcSlotsW-slot ring; warp 2 lane 0 loads activation tiles by TMA into a kTcStagesX-stage ring; warp 1 owns TMEM
+// and lane 0 issues the MMAs; warps 4-11 dequantise int4 -> fp16 into the MMA's A stage; warps
+// 12-15 drain TMEM (double-buffered accumulators) and write the output.
 #include <cuda.h>
 
 #include <atomic>
@@ -39,31 +33,31 @@
 namespace s4 {
 
 constexpr int kTcMaxTn = 256;
-constexpr int kTcMaxStagesX = 16;  // activation tiles (TMA) ring, stages chosen per tile width
-constexpr int kTcMaxStagesA = 4;   // dequantised weight (MMA operand A) ring
-constexpr int kTcMaxGroupsW = 4;   // raw weight ring slots
-constexpr int kTcGroup = 8;        // chunks per weight slot (36 KB: 32 KB of nibbles, 4 KB of scales)
-constexpr int kTcGroupAsym = 7;    // asymmetric formats: a chunk also carries 512 bytes of biases
+constexpr int kTcStagesX = 3;  // activation tiles (TMA) ring
+constexpr int kTcStagesA = 3;  // dequantised weight (MMA operand A) ring
+constexpr int kTcSlotsW = 12;
 constexpr int kTcThreads = 512;
 constexpr int kTcDequantWarps = 8;  // warps 4..11
 constexpr int kTcEpiWarp0 = 12;     // warps 12..15 drain TMEM (lane quarter = warp % 4)
-constexpr int kTcAStageBytes = 128 * 128;  // 128 rows x 64 fp16
-constexpr int kTcNumBars = 2 * kTcMaxStagesX + 2 * kTcMaxStagesA + 2 * kTcMaxGroupsW + 2 + 2 + 1;
-constexpr int kTcEpiStageBytes = 16 * 32 * 2;  // epilogue staging: per warp 16 tokens x 32 n fp16
-constexpr int kTcSmemLimit = 227 * 1024;
-constexpr int kTcSmemMax = kTcSmemLimit;  // the kernels' dynamic shared memory attribute
-constexpr uint32_t kTcTmemCols = 512;     // two 256-column accumulators
+constexpr int kTcXStageBytes = kTcMaxTn * 128;  // tn rows x 64 fp16
+constexpr int kTcAStageBytes = 128 * 128;       // 128 rows x 64 fp16
+constexpr int kTcWSlotBytes = kChunkWBytes + kChunkSBytes;
+// asymmetric formats: a slot also holds the chunk's biases; fewer slots fit the same region
+constexpr int kTcWSlotBytesAsym = kChunkWBytes + 2 * kChunkSBytes;
+constexpr int kTcSlotsWAsym = (kTcSlotsW * kTcWSlotBytes) / kTcWSlotBytesAsym;
+constexpr int kTcOffX = 0;
+constexpr int kTcOffA = kTcOffX + kTcStagesX * kTcXStageBytes;
+constexpr int kTcOffW = kTcOffA + kTcStagesA * kTcAStageBytes;
+constexpr int kTcOffBar = kTcOffW + kTcSlotsW * kTcWSlotBytes;
+constexpr int kTcNumBars = 2 * kTcStagesX + 2 * kTcStagesA + 2 * kTcSlotsW + 2 + 2 + 1;
+constexpr int kTcOffMisc = kTcOffBar + kTcNumBars * 8;
+constexpr int kTcOffEpi = (kTcOffMisc + 64 + 127) & ~127;  // epilogue staging: 4 warps x 16 tokens x 32 n fp16
+constexpr int kTcEpiStageBytes = 16 * 32 * 2;
+constexpr size_t kTcSmem = (size_t)kTcOffEpi + 4 * kTcEpiStageBytes + 1024;  // + alignment slack
+static_assert(kTcSmem <= 227 * 1024, "tcgen05 GEMM shared memory above the per-CTA limit");
+constexpr uint32_t kTcTmemCols = 512;                       // two 256-column accumulators
 
 constexpr int kTcMaxDst = 8;  // output copies one launch writes (this GPU + peers)
-
-// Shared-memory plan of one launch (byte offsets from the 1024-aligned base).
-struct TcSmem {
-  int xs, as, wg;  // activation stages, A stages, weight slots
-  int group;       // chunks per weight slot
-  int wslot;       // bytes per weight slot
-  int off_a, off_w, off_bar, off_misc, off_epi;
-  int bytes;  // dynamic shared memory of the launch (with alignment slack)
-};
 
 struct TcParams {
   const uint8_t* wq;
@@ -87,33 +81,7 @@ struct TcParams {
   int dpq;       // whole tiles per CTA (data-parallel part): CTA b takes tiles [b*dpq, (b+1)*dpq)
   int sk_base;   // first unit of the stream-K part (dpq * grid * ktiles)
   int sk_total;  // units of the stream-K part, split evenly over the grid
-  TcSmem sm;
 };
-
-// Activation stages get what the A stages and at least two weight slots leave, at most
-// kTcMaxStagesX; the weight ring the rest. 256-token tiles: 3 x 32 KB activations, 3 A stages, 2
-// weight slots; 64-token tiles: 10 x 8 KB, 4 A stages, 2 weight slots.
-inline TcSmem tc_plan_smem(int tn, bool asym) {
-  TcSmem s;
-  s.group = asym ? kTcGroupAsym : kTcGroup;
-  s.wslot = s.group * (kChunkWBytes + kChunkSBytes * (asym ? 2 : 1));
-  s.as = tn <= 128 ? 4 : 3;
-  const int xstage = tn * 128;
-  const int fixed = kTcNumBars * 8 + 64 + 128 + 4 * kTcEpiStageBytes + 1024;
-  const int budget = kTcSmemLimit - fixed - s.as * kTcAStageBytes;
-  s.xs = (budget - 2 * s.wslot) / xstage;
-  if (s.xs > kTcMaxStagesX) s.xs = kTcMaxStagesX;
-  if (s.xs < 3) s.xs = 3;
-  s.wg = (budget - s.xs * xstage) / s.wslot;
-  if (s.wg > kTcMaxGroupsW) s.wg = kTcMaxGroupsW;
-  s.off_a = s.xs * xstage;  // multiple of 1024 (tn % 16 == 0): the 128-byte swizzle's alignment
-  s.off_w = s.off_a + s.as * kTcAStageBytes;
-  s.off_bar = s.off_w + s.wg * s.wslot;
-  s.off_misc = s.off_bar + kTcNumBars * 8;
-  s.off_epi = (s.off_misc + 64 + 127) & ~127;
-  s.bytes = s.off_epi + 4 * kTcEpiStageBytes + 1024;  // + slack to align the base to 1024
-  return s;
-}
 
 // Output stores. Each destination is the local buffer or, for the column-sharded prefill, a peer's
 // gathered buffer over NVLink. Call sites branch on ndst == 1 once, outside their element loops:
@@ -209,37 +177,30 @@ __device__ __forceinline__ TcWork tc_work(int b, const TcParams& p) {
   return w;
 }
 
-// Chunk (n-block, k-tile) of the weight that work unit u reads.
-__device__ __forceinline__ int64_t tc_chunk_of(int u, const TcParams& p) {
-  const int tile = u / p.ktiles, kt = u - tile * p.ktiles;
-  return (int64_t)(tile % p.nblk) * p.ktiles + kt;
-}
-
 // kTicketFixup: split tiles are finished inside this kernel by the last CTA to arrive (atomic
 // ticket); otherwise partials are only published and tc_fixup_kernel, launched next, sums them.
 template <bool kTicketFixup, bool kAsym>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p, const __grid_constant__ CUtensorMap tmap_x) {
-  const int XS = p.sm.xs, AS = p.sm.as, WG = p.sm.wg;  // ring depths
-  const int GC = p.sm.group, WB = p.sm.wslot;           // chunks and bytes per weight slot
+  constexpr int SW = kAsym ? kTcSlotsWAsym : kTcSlotsW;            // raw weight ring slots
+  constexpr int WB = kAsym ? kTcWSlotBytesAsym : kTcWSlotBytes;    // bytes per slot
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  const int xstage = p.tn * 128;
-  uint8_t* xs = smem;
-  uint8_t* wa = smem + p.sm.off_a;
-  uint8_t* wraw = smem + p.sm.off_w;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.sm.off_bar);
+  uint8_t* xs = smem + kTcOffX;
+  uint8_t* wa = smem + kTcOffA;
+  uint8_t* wraw = smem + kTcOffW;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
   uint64_t* full_x = bars;
-  uint64_t* empty_x = full_x + kTcMaxStagesX;
-  uint64_t* ddone = empty_x + kTcMaxStagesX;
-  uint64_t* empty_a = ddone + kTcMaxStagesA;
-  uint64_t* full_w = empty_a + kTcMaxStagesA;
-  uint64_t* empty_w = full_w + kTcMaxGroupsW;
-  uint64_t* accf = empty_w + kTcMaxGroupsW;
+  uint64_t* empty_x = full_x + kTcStagesX;
+  uint64_t* ddone = empty_x + kTcStagesX;
+  uint64_t* empty_a = ddone + kTcStagesA;
+  uint64_t* full_w = empty_a + kTcStagesA;
+  uint64_t* empty_w = full_w + kTcSlotsW;  // barrier arrays keep the symmetric layout's size
+  uint64_t* accf = empty_w + kTcSlotsW;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.sm.off_misc);
-  int* s_flag = reinterpret_cast<int*>(smem + p.sm.off_misc + 16);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTcOffMisc);
+  int* s_flag = reinterpret_cast<int*>(smem + kTcOffMisc + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const TcWork wk = tc_work(blockIdx.x, p);
@@ -247,15 +208,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   const int KT = p.ktiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < XS; ++s) {
+    for (int s = 0; s < kTcStagesX; ++s) {
       mbar_init(full_x + s, 1);
       mbar_init(empty_x + s, 1);
     }
-    for (int s = 0; s < AS; ++s) {
+    for (int s = 0; s < kTcStagesA; ++s) {
       mbar_init(ddone + s, kTcDequantWarps);
       mbar_init(empty_a + s, 1);
     }
-    for (int s = 0; s < WG; ++s) {
+    for (int s = 0; s < SW; ++s) {
       mbar_init(full_w + s, 1);
       mbar_init(empty_w + s, kTcDequantWarps);
     }
@@ -281,43 +242,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
 
   if (warp == 0) {
     // ------------- raw int4 chunks: producer -------------
-    // Slot q holds work items [q * GC, q * GC + GC): nibbles of its chunks first, then their scales
-    // (then biases). The weights are immutable, so this runs before the grid-dependency wait and
-    // overlaps the previous kernel's tail.
     if (lane == 0) {
-      const int ngroups = (n + GC - 1) / GC;
       int issued = 0;
       bool ok = true;
-      for (int q = 0; q < ngroups; ++q) {
-        const int slot = q % WG;
-        if (q >= WG && !mbar_wait(empty_w + slot, ((q / WG) - 1) & 1)) {
+      for (int i = 0; i < n; ++i) {
+        const int slot = i % SW;
+        if (i >= SW && !mbar_wait(empty_w + slot, ((i / SW) - 1) & 1)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
           break;
         }
-        const int i0 = q * GC, cnt = min(GC, n - i0);
+        const int u = wk.unit(i);
+        const int tile = u / KT, kt = u - tile * KT;
+        const int nb = tile % p.nblk;
+        const int64_t chunk = (int64_t)nb * KT + kt;
         uint8_t* dst = wraw + slot * WB;
-        const uint32_t sec = (uint32_t)GC * kChunkWBytes;  // scales start after GC chunks of nibbles
-        mbar_arrive_expect_tx(full_w + slot, (uint32_t)cnt * (kChunkWBytes + kChunkSBytes * (kAsym ? 2 : 1)));
-        // one copy per array for every run of chunks that is contiguous in the weight
-        for (int j = 0; j < cnt;) {
-          const int64_t c0 = tc_chunk_of(wk.unit(i0 + j), p);
-          int r = 1;
-          while (j + r < cnt && tc_chunk_of(wk.unit(i0 + j + r), p) == c0 + r) ++r;
-          bulk_g2s_plain(dst + j * kChunkWBytes, p.wq + c0 * kChunkWBytes, (uint32_t)r * kChunkWBytes, full_w + slot);
-          bulk_g2s_plain(dst + sec + j * kChunkSBytes, p.ws + c0 * kChunkSBytes, (uint32_t)r * kChunkSBytes,
-                         full_w + slot);
-          if (kAsym)
-            bulk_g2s_plain(dst + sec + (GC + j) * kChunkSBytes, p.wb + c0 * kChunkSBytes, (uint32_t)r * kChunkSBytes,
-                           full_w + slot);
-          j += r;
-        }
+        mbar_arrive_expect_tx(full_w + slot, WB);
+        bulk_g2s_plain(dst, p.wq + chunk * kChunkWBytes, kChunkWBytes, full_w + slot);
+        bulk_g2s_plain(dst + kChunkWBytes, p.ws + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
+        if (kAsym) bulk_g2s_plain(dst + kChunkWBytes + kChunkSBytes, p.wb + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
         ++issued;
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
-        for (int q = (issued > WG ? issued - WG : 0); q < issued; ++q)
-          if (!mbar_wait_until(full_w + (q % WG), (q / WG) & 1, deadline)) break;
+        for (int i = (issued > SW ? issued - SW : 0); i < issued; ++i)
+          if (!mbar_wait_until(full_w + (i % SW), (i / SW) & 1, deadline)) break;
       }
     }
   } else if (warp == 2) {
@@ -326,9 +275,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       pdl_wait();  // x is written by the previous kernel in the stream
       int issued = 0;
       bool ok = true;
+      const uint32_t xbytes = (uint32_t)p.tn * 128u;
       for (int i = 0; i < n; ++i) {
-        const int s = i % XS;
-        if (i >= XS && !mbar_wait(empty_x + s, ((i / XS) - 1) & 1)) {
+        const int s = i % kTcStagesX;
+        if (i >= kTcStagesX && !mbar_wait(empty_x + s, ((i / kTcStagesX) - 1) & 1)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
           break;
@@ -336,14 +286,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         const int u = wk.unit(i);
         const int tile = u / KT, kt = u - tile * KT;
         const int tb = tile / p.nblk;
-        mbar_arrive_expect_tx(full_x + s, (uint32_t)xstage);
-        tma_load_2d(xs + s * xstage, &tmap_x, kt * 64, tb * p.tn, full_x + s);
+        mbar_arrive_expect_tx(full_x + s, xbytes);
+        tma_load_2d(xs + s * kTcXStageBytes, &tmap_x, kt * 64, tb * p.tn, full_x + s);
         ++issued;
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
-        for (int i = (issued > XS ? issued - XS : 0); i < issued; ++i)
-          if (!mbar_wait_until(full_x + (i % XS), (i / XS) & 1, deadline)) break;
+        for (int i = (issued > kTcStagesX ? issued - kTcStagesX : 0); i < issued; ++i)
+          if (!mbar_wait_until(full_x + (i % kTcStagesX), (i / kTcStagesX) & 1, deadline)) break;
       }
     }
   } else if (warp == 1) {
@@ -366,14 +316,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)(buf * 256);
         for (int u = u0; u < seg_end; ++u, ++i) {
-          const int sx = i % XS, s = i % AS;
-          if (!mbar_wait(full_x + sx, (i / XS) & 1) || !mbar_wait(ddone + s, (i / AS) & 1)) {
+          const int sx = i % kTcStagesX, s = i % kTcStagesA;
+          if (!mbar_wait(full_x + sx, (i / kTcStagesX) & 1) || !mbar_wait(ddone + s, (i / kTcStagesA) & 1)) {
             set_error(p.err, kErrWaitTimeout);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(wa + s * kTcAStageBytes), b0 = smem_u32(xs + sx * xstage);
+          const uint32_t a0 = smem_u32(wa + s * kTcAStageBytes), b0 = smem_u32(xs + sx * kTcXStageBytes);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             tc_mma(dcol, sw128_kmajor_desc(a0 + j * 32), sw128_kmajor_desc(b0 + j * 32), idesc,
@@ -393,22 +343,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     const int d = threadIdx.x - 128;
     bool ok = true;
     for (int i = 0; i < n && ok; ++i) {
-      const int s = i % AS, q = i / GC, j = i - q * GC, slot = q % WG;
-      if (!mbar_wait(full_w + slot, (q / WG) & 1) || (i >= AS && !mbar_wait(empty_a + s, ((i / AS) - 1) & 1))) {
+      const int s = i % kTcStagesA, slot = i % SW;
+      if (!mbar_wait(full_w + slot, (i / SW) & 1) ||
+          (i >= kTcStagesA && !mbar_wait(empty_a + s, ((i / kTcStagesA) - 1) & 1))) {
         set_error(p.err, kErrWaitTimeout);
         ok = false;
         break;
       }
-      const uint8_t* src = wraw + slot * WB + j * kChunkWBytes;                             // nibbles
-      const uint8_t* ssrc = wraw + slot * WB + GC * kChunkWBytes + j * kChunkSBytes;        // scales
-      const uint8_t* bsrc = wraw + slot * WB + GC * (kChunkWBytes + kChunkSBytes) + j * kChunkSBytes;  // biases
+      const uint8_t* src = wraw + slot * WB;
       const uint32_t dst = smem_u32(wa + s * kTcAStageBytes);
 #pragma unroll
       for (int rep = 0; rep < 256 / (32 * kTcDequantWarps); ++rep) {
         const int L = d + rep * 32 * kTcDequantWarps;  // 16-byte lane slot: sub-tile L / 32, lane L % 32
         const int sub = L >> 5, ln = L & 31, g = ln >> 2, t = ln & 3;
         const uint4 v = *reinterpret_cast<const uint4*>(src + L * 16);
-        const uint2 sc = *reinterpret_cast<const uint2*>(ssrc + sub * 64 + g * 8);
+        const uint2 sc = *reinterpret_cast<const uint2*>(src + kChunkWBytes + sub * 64 + g * 8);
         const uint32_t words[4] = {v.x, v.y, v.z, v.w};
         const uint32_t sh[4] = {sc.x & 0xFFFFu, sc.x >> 16, sc.y & 0xFFFFu, sc.y >> 16};  // (g,b0) (g+8,b0) (g,b1) (g+8,b1)
         const bool odd = (g & 1) != 0;
@@ -424,7 +373,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
           const int c = blk * 4 + t;
           uint32_t hv[4];
           if constexpr (kAsym) {  // w = fma(q, scale, bias) in fp16 (kernels.js:36)
-            const uint2 bi = *reinterpret_cast<const uint2*>(bsrc + sub * 64 + g * 8);
+            const uint2 bi = *reinterpret_cast<const uint2*>(src + kChunkWBytes + kChunkSBytes + sub * 64 + g * 8);
             const uint32_t jb = odd ? (jj ^ 2) : jj;
             const uint32_t bbits = ((jb >> 1) ? bi.y : bi.x) >> (16 * (jb & 1)) & 0xFFFFu;
             i4x8_to_h2x4_raw(w, hv);
@@ -445,7 +394,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(ddone + s);
-        if (j == GC - 1 || i == n - 1) mbar_arrive(empty_w + slot);  // the slot's last chunk is done
+        mbar_arrive(empty_w + slot);
       }
     }
   } else if (warp >= kTcEpiWarp0) {
@@ -453,7 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     const int q = warp - kTcEpiWarp0;  // TMEM lane quarter this warp may access (warp % 4)
     const int nl = q * 32 + lane;
     const int et = threadIdx.x - kTcEpiWarp0 * 32;
-    uint8_t* epi_base = smem + p.sm.off_epi;
+    uint8_t* epi_base = smem + kTcOffEpi;
     __half* epi_stage = reinterpret_cast<__half*>(epi_base + q * kTcEpiStageBytes);
     bool failed = false;
     int si = 0;
@@ -795,8 +744,11 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
   const int tiles = p.ntb * nblk;
   // the fused SiLU*mul epilogue stores 8 outputs at a time and has no in-kernel ticket fix-up
   if (glu && (!p.vec || ticket_fixup || N % 128)) return cudaErrorInvalidValue;
-  p.sm = tc_plan_smem(tn, wb != nullptr);
   p.dpq = tiles / p.grid;
+  // every CTA's stream-K range must hold at least one unit: an empty range inside a split tile's
+  // CTA span would count as a part that never arrives. With fewer leftover units than CTAs, one wave
+  // of whole tiles moves into the stream-K part.
+  if (p.dpq > 0 && (int64_t)(tiles - p.dpq * p.grid) * ktiles < p.grid && tiles % p.grid != 0) --p.dpq;
   p.sk_base = p.dpq * p.grid * ktiles;
   p.sk_total = p.total - p.sk_base;
 
@@ -816,21 +768,20 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(tc_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
+    e = cudaFuncSetAttribute(tc_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tc_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
+      e = cudaFuncSetAttribute(tc_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tc_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
+      e = cudaFuncSetAttribute(tc_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tc_gemm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
+      e = cudaFuncSetAttribute(tc_gemm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  if (p.sm.bytes > kTcSmemMax) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid, 1, 1);
   cfg.blockDim = dim3(kTcThreads, 1, 1);
-  cfg.dynamicSmemBytes = p.sm.bytes;
+  cfg.dynamicSmemBytes = kTcSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -811,8 +811,10 @@ static bool use_cta_fixup(const Bucket& b, const s4_ctx* ctx, const s4_weight* w
   if (ctx->ticket_fixup >= 0) return ctx->ticket_fixup == 1;
   const long long tiles = (long long)((M + tn - 1) / tn) * w->nblk, total = tiles * w->ktiles;
   const long long g = grid < total ? grid : total;
-  const long long sk = total - (tiles / g) * g * w->ktiles;  // stream-K units
-  if (sk == 0) return true;                                   // nothing is split
+  long long dpq = tiles / g;  // the work split of csrc/gemm_tc.cu (launch_tc_gemm_ex)
+  if (dpq > 0 && (tiles - dpq * g) * w->ktiles < g && tiles % g != 0) --dpq;
+  const long long sk = total - dpq * g * w->ktiles;  // stream-K units
+  if (sk == 0) return false;  // nothing is split: the kernel without the ticket path
   const long long per = sk / g > 0 ? sk / g : 1;
   return (w->ktiles + per - 1) / per + 1 <= 3;
 }

@@ -77,7 +77,10 @@ def has_split(M: int, K: int, N: int, tn: int, grid: int) -> bool:
     tiles = ((M + tn - 1) // tn) * nblk
     total = tiles * KT
     g = min(grid, total)
-    base = (tiles // g) * g * KT
+    dpq = tiles // g
+    if dpq > 0 and (tiles - dpq * g) * KT < g and tiles % g:
+        dpq -= 1
+    base = dpq * g * KT
     sk = total - base
     return any((base + (b * sk) // g) % KT for b in range(1, g))
 

@@ -145,3 +145,23 @@ def test_table_shape_buckets(ctx):
             ctx.set_table({"buckets": [{"max_m": 64, "family": "tc", "fixup": "sometimes"}]})
     finally:
         ctx.set_table(None)
+
+
+def test_tc_few_leftover_units(ctx):
+    """Fewer leftover stream-K units than CTAs (65 n-blocks x 16 token blocks of 128 on 148 CTAs: 4
+    leftover tiles of 32 k-tiles): one wave of whole tiles joins the stream-K part so that no CTA
+    inside a split tile's span has an empty range, with either fix-up."""
+    K, N, M = 2048, 8224, 2048
+    rng = np.random.default_rng(5)
+    packed, scales = s4ref.config_weights(rng, K, N)
+    W = ctx.upload(packed, scales, N, K)
+    x = s4ref.config_x(rng, M, K)
+    _, ref = s4ref.matmul(x, packed, scales)
+    try:
+        for fx in ("kernel", "cta"):
+            ctx.set_table({"buckets": [{"max_m": 1 << 30, "family": "tc", "tile": 128, "split": 148, "fixup": fx}]})
+            _check(_run(ctx, W, x), ref, f"tile 128 fixup={fx}")
+    finally:
+        ctx.set_table(None)
+    assert ctx.check_errors() == 0
+    W.free()
