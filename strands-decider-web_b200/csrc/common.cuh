@@ -62,6 +62,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking check of phase `parity` (no suspend): the fast path of a wait whose phase is usually
+// complete already.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Wait for phase `parity` of `bar` until %globaltimer passes `deadline`; false on expiry.
 __device__ __forceinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, uint64_t deadline) {
   const uint32_t a = smem_u32(bar);
@@ -73,6 +86,7 @@ __device__ __forceinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, 
 // Wait for phase `parity` of `bar` to complete; false if kWaitTimeoutNs passed first.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
+  if (mbar_test_wait(a, parity)) return true;
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
   while (true) {

@@ -33,11 +33,33 @@
 namespace s4 {
 
 constexpr int kTcMaxTn = 256;
-constexpr int kTcStagesX = 3;  // activation tiles (TMA) ring
-constexpr int kTcStagesA = 3;  // dequantised weight (MMA operand A) ring
+// Pipeline stages: stage s holds one k-tile's activations (TMA) and its dequantised weights (A). One
+// "full" barrier per stage completes when the activation bytes have landed AND all dequant warps have
+// arrived; one "empty" barrier per stage is signalled by a single tcgen05.commit once the stage's
+// MMAs are done. The MMA thread thus waits once and commits once per k-tile: its per-k-tile issue
+// time (measured ~750 cycles with separate activation / weight barriers and two commits, against 136
+// cycles of tensor work for a 64-token tile) bounds every shape of this kernel.
+constexpr int kTcStages = 3;
+constexpr int kTcStagesX = kTcStages;  // activation tiles (TMA)
+constexpr int kTcStagesA = kTcStages;  // dequantised weight (MMA operand A)
 constexpr int kTcSlotsW = 12;
 constexpr int kTcThreads = 512;
 constexpr int kTcDequantWarps = 8;  // warps 4..11
+// The dequant warps form kTcDqGroups groups that take alternate chunks (group g: chunks i with
+// i % kTcDqGroups == g), so that many chunks convert at once and each thread has
+// kTcDqGroups independent 16-byte lane slots per chunk.
+#ifndef S4_TC_DQ_GROUPS
+#define S4_TC_DQ_GROUPS 2
+#endif
+constexpr int kTcDqGroups = S4_TC_DQ_GROUPS;
+constexpr int kTcDqWarpsPerChunk = kTcDequantWarps / kTcDqGroups;
+// Every stage wait is a parity wait, which cannot tell a phase from the one two back. A group reaching
+// chunk j (stage j % kTcStages) waits for the MMAs of chunk j - kTcStages; that is safe only if chunk
+// j - 2 * kTcStages is known to be consumed, which the group's own previous wait (chunk j - groups)
+// guarantees when groups <= stages. With more groups than stages a group could write a stage that is
+// still in use and over-arrive on its barrier.
+static_assert(kTcDqGroups >= 1 && kTcDqGroups <= 3 && kTcDequantWarps % kTcDqGroups == 0,
+              "dequant groups must not outnumber the pipeline stages");
 constexpr int kTcEpiWarp0 = 12;     // warps 12..15 drain TMEM (lane quarter = warp % 4)
 constexpr int kTcXStageBytes = kTcMaxTn * 128;  // tn rows x 64 fp16
 constexpr int kTcAStageBytes = 128 * 128;       // 128 rows x 64 fp16
@@ -49,7 +71,7 @@ constexpr int kTcOffX = 0;
 constexpr int kTcOffA = kTcOffX + kTcStagesX * kTcXStageBytes;
 constexpr int kTcOffW = kTcOffA + kTcStagesA * kTcAStageBytes;
 constexpr int kTcOffBar = kTcOffW + kTcSlotsW * kTcWSlotBytes;
-constexpr int kTcNumBars = 2 * kTcStagesX + 2 * kTcStagesA + 2 * kTcSlotsW + 2 + 2 + 1;
+constexpr int kTcNumBars = 2 * kTcStages + 2 * kTcSlotsW + 2 + 2 + 1;
 constexpr int kTcOffMisc = kTcOffBar + kTcNumBars * 8;
 constexpr int kTcOffEpi = (kTcOffMisc + 64 + 127) & ~127;  // epilogue staging: 4 warps x 16 tokens x 32 n fp16
 constexpr int kTcEpiStageBytes = 16 * 32 * 2;
@@ -190,11 +212,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   uint8_t* wa = smem + kTcOffA;
   uint8_t* wraw = smem + kTcOffW;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
-  uint64_t* full_x = bars;
-  uint64_t* empty_x = full_x + kTcStagesX;
-  uint64_t* ddone = empty_x + kTcStagesX;
-  uint64_t* empty_a = ddone + kTcStagesA;
-  uint64_t* full_w = empty_a + kTcStagesA;
+  uint64_t* full = bars;                 // stage full: activation bytes + dequant warps
+  uint64_t* empty = full + kTcStages;    // stage consumed by the MMAs (tcgen05.commit)
+  uint64_t* full_w = empty + kTcStages;
   uint64_t* empty_w = full_w + kTcSlotsW;  // barrier arrays keep the symmetric layout's size
   uint64_t* accf = empty_w + kTcSlotsW;
   uint64_t* acce = accf + 2;
@@ -208,17 +228,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
   const int KT = p.ktiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStagesX; ++s) {
-      mbar_init(full_x + s, 1);
-      mbar_init(empty_x + s, 1);
-    }
-    for (int s = 0; s < kTcStagesA; ++s) {
-      mbar_init(ddone + s, kTcDequantWarps);
-      mbar_init(empty_a + s, 1);
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(full + s, kTcDqWarpsPerChunk + 1);  // + the activation producer's expect-tx arrival
+      mbar_init(empty + s, 1);
     }
     for (int s = 0; s < SW; ++s) {
       mbar_init(full_w + s, 1);
-      mbar_init(empty_w + s, kTcDequantWarps);
+      mbar_init(empty_w + s, kTcDqWarpsPerChunk);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf + b, 1);
@@ -278,7 +294,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       const uint32_t xbytes = (uint32_t)p.tn * 128u;
       for (int i = 0; i < n; ++i) {
         const int s = i % kTcStagesX;
-        if (i >= kTcStagesX && !mbar_wait(empty_x + s, ((i / kTcStagesX) - 1) & 1)) {
+        if (i >= kTcStagesX && !mbar_wait(empty + s, ((i / kTcStagesX) - 1) & 1)) {
           set_error(p.err, kErrWaitTimeout);
           ok = false;
           break;
@@ -286,23 +302,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         const int u = wk.unit(i);
         const int tile = u / KT, kt = u - tile * KT;
         const int tb = tile / p.nblk;
-        mbar_arrive_expect_tx(full_x + s, xbytes);
-        tma_load_2d(xs + s * kTcXStageBytes, &tmap_x, kt * 64, tb * p.tn, full_x + s);
+        mbar_arrive_expect_tx(full + s, xbytes);
+        tma_load_2d(xs + s * kTcXStageBytes, &tmap_x, kt * 64, tb * p.tn, full + s);
         ++issued;
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
         for (int i = (issued > kTcStagesX ? issued - kTcStagesX : 0); i < issued; ++i)
-          if (!mbar_wait_until(full_x + (i % kTcStagesX), (i / kTcStagesX) & 1, deadline)) break;
+          if (!mbar_wait_until(full + (i % kTcStagesX), (i / kTcStagesX) & 1, deadline)) break;
       }
     }
   } else if (warp == 1) {
     // ------------- MMA issuer -------------
     if (lane == 0) {
       const uint32_t idesc = f16_f32_idesc(p.tn);
+      // descriptors of stage 0; a stage adds its byte offset >> 4, each 16-K step 32 bytes >> 4 = 2
+      const uint64_t adesc0 = sw128_kmajor_desc(smem_u32(wa)), bdesc0 = sw128_kmajor_desc(smem_u32(xs));
       bool ok = true;
       int si = 0;
       int i = 0;
+      int s = 0;
+      uint32_t ph = 0;
       while (ok && i < n) {
         const int u0 = wk.unit(i);
         const int tile = u0 / KT;
@@ -316,20 +336,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)(buf * 256);
         for (int u = u0; u < seg_end; ++u, ++i) {
-          const int sx = i % kTcStagesX, s = i % kTcStagesA;
-          if (!mbar_wait(full_x + sx, (i / kTcStagesX) & 1) || !mbar_wait(ddone + s, (i / kTcStagesA) & 1)) {
+          if (!mbar_wait(full + s, ph)) {
             set_error(p.err, kErrWaitTimeout);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(wa + s * kTcAStageBytes), b0 = smem_u32(xs + sx * kTcXStageBytes);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tc_mma(dcol, sw128_kmajor_desc(a0 + j * 32), sw128_kmajor_desc(b0 + j * 32), idesc,
-                   (u != u0 || j > 0) ? 1u : 0u);
-          tc_commit(empty_a + s);
-          tc_commit(empty_x + sx);
+          const uint64_t ad = adesc0 + (uint64_t)((s * kTcAStageBytes) >> 4);
+          const uint64_t bd = bdesc0 + (uint64_t)((s * kTcXStageBytes) >> 4);
+          tc_mma(dcol, ad, bd, idesc, u != u0 ? 1u : 0u);
+          tc_mma(dcol, ad + 2, bd + 2, idesc, 1u);
+          tc_mma(dcol, ad + 4, bd + 4, idesc, 1u);
+          tc_mma(dcol, ad + 6, bd + 6, idesc, 1u);
+          tc_commit(empty + s);
+          if (++s == kTcStages) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
         if (!ok) break;
         tc_commit(accf + buf);
@@ -340,12 +363,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     }
   } else if (warp >= 4 && warp < 4 + kTcDequantWarps) {
     // ------------- dequantisers: int4 chunk -> fp16 A stage (128-byte swizzled, K-major) -------------
-    const int d = threadIdx.x - 128;
+    const int dg = (warp - 4) / kTcDqWarpsPerChunk;              // this warp's group
+    const int d = threadIdx.x - 128 - dg * kTcDqWarpsPerChunk * 32;  // thread index within the group
     bool ok = true;
-    for (int i = 0; i < n && ok; ++i) {
+    for (int i = dg; i < n && ok; i += kTcDqGroups) {
       const int s = i % kTcStagesA, slot = i % SW;
       if (!mbar_wait(full_w + slot, (i / SW) & 1) ||
-          (i >= kTcStagesA && !mbar_wait(empty_a + s, ((i / kTcStagesA) - 1) & 1))) {
+          (i >= kTcStagesA && !mbar_wait(empty + s, ((i / kTcStagesA) - 1) & 1))) {
         set_error(p.err, kErrWaitTimeout);
         ok = false;
         break;
@@ -353,8 +377,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       const uint8_t* src = wraw + slot * WB;
       const uint32_t dst = smem_u32(wa + s * kTcAStageBytes);
 #pragma unroll
-      for (int rep = 0; rep < 256 / (32 * kTcDequantWarps); ++rep) {
-        const int L = d + rep * 32 * kTcDequantWarps;  // 16-byte lane slot: sub-tile L / 32, lane L % 32
+      for (int rep = 0; rep < 256 / (32 * kTcDqWarpsPerChunk); ++rep) {
+        const int L = d + rep * 32 * kTcDqWarpsPerChunk;  // 16-byte lane slot: sub-tile L / 32, lane L % 32
         const int sub = L >> 5, ln = L & 31, g = ln >> 2, t = ln & 3;
         const uint4 v = *reinterpret_cast<const uint4*>(src + L * 16);
         const uint2 sc = *reinterpret_cast<const uint2*>(src + kChunkWBytes + sub * 64 + g * 8);
@@ -393,7 +417,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(ddone + s);
+        mbar_arrive(full + s);
         mbar_arrive(empty_w + slot);
       }
     }
