@@ -58,7 +58,7 @@ constexpr int kTcDqWarpsPerChunk = kTcDequantWarps / kTcDqGroups;
 // j - 2 * kTcStages is known to be consumed, which the group's own previous wait (chunk j - groups)
 // guarantees when groups <= stages. With more groups than stages a group could write a stage that is
 // still in use and over-arrive on its barrier.
-static_assert(kTcDqGroups >= 1 && kTcDqGroups <= 3 && kTcDequantWarps % kTcDqGroups == 0,
+static_assert(kTcDqGroups >= 1 && kTcDqGroups <= kTcStages && kTcDequantWarps % kTcDqGroups == 0,
               "dequant groups must not outnumber the pipeline stages");
 constexpr int kTcEpiWarp0 = 12;     // warps 12..15 drain TMEM (lane quarter = warp % 4)
 constexpr int kTcXStageBytes = kTcMaxTn * 128;  // tn rows x 64 fp16
