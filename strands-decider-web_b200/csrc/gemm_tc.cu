@@ -913,8 +913,10 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   // partials: two slots of tn x 128 fp32 per CTA
   const int max_grid = (int)(kStaticPartialBytes / (2ull * tn * 128 * sizeof(float)));
   const int grid = w->sm_count < max_grid ? w->sm_count : max_grid;
+  // split tiles are summed by the fix-up kernel launched right after (it reads the partials from the
+  // same static array); a second launch allocates nothing either
   e = launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
-                     (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true, true, 0);
+                     (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true, false, 0);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: tcgen05 GEMM launch failed");
   return S4_OK;
 }

@@ -799,24 +799,17 @@ static int auto_tile(int M, const s4_weight* w, int sms) {
   return 256;
 }
 
-// Split tiles of a (tn, grid) launch summed by their last CTA (in-kernel) or by the fix-up kernel:
-// the table's choice, else the environment's (S4_TICKET_FIXUP), else in-kernel when no tile is cut
-// into more than three parts (the last CTA then adds at most two published partials to its own
-// sums; with more parts one CTA would read them all, and the fix-up kernel spreads that work over
-// the grid). Fused gate|up weights always use the fix-up kernel (it pairs gate and up rows).
-static bool use_cta_fixup(const Bucket& b, const s4_ctx* ctx, const s4_weight* w, int M, int tn, int grid) {
+// Split tiles of a launch summed by their last CTA (in-kernel) or by the fix-up kernel: the table's
+// choice, else the environment's (S4_TICKET_FIXUP), else the fix-up kernel. The tuner measured the
+// in-kernel form slower on every shape and M of the sweep (1.2x with two parts per tile, up to 6x with
+// ten): one CTA's four epilogue warps sum the other parts 16 rows at a time, a chain of L2 round
+// trips, while the fix-up kernel spreads the same reads over the whole grid. Fused gate|up weights
+// always use the fix-up kernel (it pairs gate and up rows).
+static bool use_cta_fixup(const Bucket& b, const s4_ctx* ctx, const s4_weight* w) {
   if (w->glu) return false;
   if (b.fixup == s4::kFixupCta) return true;
   if (b.fixup == s4::kFixupKernel) return false;
-  if (ctx->ticket_fixup >= 0) return ctx->ticket_fixup == 1;
-  const long long tiles = (long long)((M + tn - 1) / tn) * w->nblk, total = tiles * w->ktiles;
-  const long long g = grid < total ? grid : total;
-  long long dpq = tiles / g;  // the work split of csrc/gemm_tc.cu (launch_tc_gemm_ex)
-  if (dpq > 0 && (tiles - dpq * g) * w->ktiles < g && tiles % g != 0) --dpq;
-  const long long sk = total - dpq * g * w->ktiles;  // stream-K units
-  if (sk == 0) return false;  // nothing is split: the kernel without the ticket path
-  const long long per = sk / g > 0 ? sk / g : 1;
-  return (w->ktiles + per - 1) / per + 1 <= 3;
+  return ctx->ticket_fixup == 1;
 }
 
 // Tile size and CTA count together. Two cases where whole tiles packed into whole waves beat the
@@ -879,7 +872,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
       e = s4::launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x) + r0 * w->K,
                              static_cast<__half*>(y) + r0 * (w->glu ? w->N / 2 : w->N), ctx->partials, ctx->tickets,
                              kMaxTickets, ctx->err, rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl,
-                             use_cta_fixup(b, ctx, w, rows, tn, grid), w->glu);
+                             use_cta_fixup(b, ctx, w), w->glu);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
       ++ctx->launches;
     }

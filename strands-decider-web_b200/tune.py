@@ -33,6 +33,7 @@ SHAPES = {"qkvz_ab": (2048, 8224), "attn_qkv": (2048, 3072), "gate_up": (2048, 1
           "out_proj": (2048, 2048)}
 MS = [1, 2, 4, 8, 12, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512, 1024, 2048]
 L2_BYTES = 126 << 20
+TIE = 0.03  # candidates within 3 % of the fastest count as ties (run-to-run noise is about 1 %)
 
 
 def _pkg():
@@ -85,6 +86,29 @@ def has_split(M: int, K: int, N: int, tn: int, grid: int) -> bool:
     return any((base + (b * sk) // g) % KT for b in range(1, g))
 
 
+def _parse_label(lab: str):
+    """Inverse of _label."""
+    f = lab.split("/")
+    if f[0] == "gemv":
+        return {"family": "gemv", "split": int(f[1][1:])}
+    return {"family": "tc", "tile": int(f[1][1:]), "split": int(f[2][1:]), "fixup": f[3]}
+
+
+def pick(timings: dict, prev):
+    """The kept candidate of one (shape, M) from {label: us or 'FAIL ...'}: the fastest, unless a
+    candidate within TIE of it is the previous M's choice (so buckets merge) or the automatic one
+    (family default, tile 0, split 0, fix-up kernel)."""
+    ok = {k: v for k, v in timings.items() if isinstance(v, (int, float))}
+    best = min(ok.values())
+    near = [k for k, v in ok.items() if v <= best * (1 + TIE)]
+    if prev is not None and _label(prev) in near:
+        return prev
+    for auto in ("gemv/s0", "tc/t0/g0/kernel"):
+        if auto in near:
+            return _parse_label(auto)
+    return _parse_label(min(ok, key=ok.get))
+
+
 def _label(c):
     if c["family"] == "gemv":
         return f"gemv/s{c['split']}"
@@ -112,6 +136,7 @@ def tune(ctx, shapes, ms, reps_min=64, log=print):
         sd = torch.from_numpy(scales).to(dev)
         Ws = [ctx.upload(pd, sd, N, K) for _ in range(copies)]
         del pd, sd
+        prev_m = []
         for M in ms:
             x = torch.from_numpy(s4ref.config_x(rng, M, K)).to(dev)
             ref = (x.float().cpu() @ deq.T).numpy()
@@ -158,21 +183,27 @@ def tune(ctx, shapes, ms, reps_min=64, log=print):
                 rows.append({"cand": c, "ok": True, "us": round(us, 3), "max_rel": mr})
             if ctx.check_errors():
                 raise RuntimeError(f"device error word set while tuning {name} M={M}")
-            good = [r for r in rows if r["ok"]]
-            best = min(good, key=lambda r: r["us"])
-            alg = wbytes + 2 * M * K + 2 * M * N
-            results[(name, M)] = {"K": K, "N": N, "M": M, "best": best["cand"], "us": best["us"],
-                                  "GBps": round(alg / best["us"] / 1e3, 1),
-                                  "TFLOPs": round(2.0 * M * N * K / best["us"] / 1e6, 1),
-                                  "all": {_label(r["cand"]): (r["us"] if r["ok"] else "FAIL " + r["why"]) for r in rows}}
-            log(json.dumps({"shape": name, "M": M, "best": _label(best["cand"]), "us": best["us"],
-                            "GBps": results[(name, M)]["GBps"], "TFLOPs": results[(name, M)]["TFLOPs"],
+            timings = {_label(r["cand"]): (r["us"] if r["ok"] else "FAIL " + r["why"]) for r in rows}
+            results[(name, M)] = measured(name, K, N, M, timings, results.get((name, prev_m[0])) if prev_m else None)
+            prev_m[:] = [M]
+            log(json.dumps({"shape": name, "M": M, "best": _label(results[(name, M)]["best"]),
+                            "us": results[(name, M)]["us"], "GBps": results[(name, M)]["GBps"],
+                            "TFLOPs": results[(name, M)]["TFLOPs"],
                             "failed": [_label(r["cand"]) for r in rows if not r["ok"]]}))
         for W in Ws:
             W.free()
         torch.cuda.empty_cache()
     ctx.set_table(None)  # leave the context on the built-in table
     return results
+
+
+def measured(name, K, N, M, timings, prev_result):
+    """One (shape, M) result: the kept candidate (pick) and its figures."""
+    best = pick(timings, prev_result["best"] if prev_result else None)
+    us = timings[_label(best)]
+    alg = N * K // 2 + N * K // 16 + 2 * M * K + 2 * M * N
+    return {"K": K, "N": N, "M": M, "best": best, "us": us, "GBps": round(alg / us / 1e3, 1),
+            "TFLOPs": round(2.0 * M * N * K / us / 1e6, 1), "all": timings}
 
 
 def default_table_json():
@@ -222,14 +253,27 @@ def main():
     ap.add_argument("--shapes", default=",".join(SHAPES), help="comma-separated subset of " + ",".join(SHAPES))
     ap.add_argument("--ms", default=",".join(map(str, MS)))
     ap.add_argument("--no-write", action="store_true", help="print the measurements only")
+    ap.add_argument("--from-json", help="rebuild the table from the candidate timings of an earlier run (no GPU)")
     args = ap.parse_args()
-    pkg = _pkg()
-    ctx = pkg.Context(0)
     shapes = {k: SHAPES[k] for k in args.shapes.split(",")}
     ms = [int(m) for m in args.ms.split(",")]
     t0 = time.time()
-    res = tune(ctx, shapes, ms)
-    table = build_table(res, shapes, ms, ctx.sm_count)
+    if args.from_json:
+        old = json.load(open(args.from_json))
+        res, sms = {}, old["measured_on"]["sm_count"]
+        for name, (K, N) in shapes.items():
+            prev = None
+            for M in ms:
+                key = f"{name}/M{M}"
+                if key in old["candidates"]:
+                    res[(name, M)] = prev = measured(name, K, N, M, old["candidates"][key], prev)
+        ctx = None
+    else:
+        pkg = _pkg()
+        ctx = pkg.Context(0)
+        res = tune(ctx, shapes, ms)
+        sms = ctx.sm_count
+    table = build_table(res, shapes, ms, sms)
     table["measurements"] = {f"{k[0]}/M{k[1]}": {kk: v for kk, v in r.items() if kk != "all"} for k, r in res.items()}
     table["candidates"] = {f"{k[0]}/M{k[1]}": r["all"] for k, r in res.items()}
     print(json.dumps({"tuned_s": round(time.time() - t0, 1), "buckets": len(table["buckets"])}))
@@ -237,7 +281,8 @@ def main():
         with open(args.out, "w") as f:
             json.dump(table, f, indent=1)
         write_inc(table, args.inc)
-    ctx.close()
+    if ctx is not None:
+        ctx.close()
 
 
 if __name__ == "__main__":

@@ -104,3 +104,19 @@ def test_wrappers_refuse_tensors_the_kernels_would_overrun(pkg):
         with pytest.raises(m.S4Error) as e:
             case()
         assert e.value.code == m.ERR_INVALID, i
+
+
+def test_builtin_table_is_the_committed_json():
+    """csrc/dispatch_table.inc (the library's built-in table) holds exactly the buckets of
+    dispatch_table.json, and every bucket is well formed."""
+    import json
+    pkg_dir = os.path.join(ROOT, "strands-decider-web_b200")
+    table = json.load(open(os.path.join(pkg_dir, "dispatch_table.json")))
+    inc = open(os.path.join(pkg_dir, "csrc", "dispatch_table.inc")).read()
+    text = "".join(re.findall(r'^\s*"(.*)"', inc, flags=re.M)).replace('\\"', '"').replace("\\\\", "\\")
+    assert json.loads(text) == {"buckets": table["buckets"]}
+    general = [b for b in table["buckets"] if not b.get("K") and not b.get("N")]
+    assert general and general[-1]["max_m"] >= 1 << 30
+    for b in table["buckets"]:
+        assert b["family"] in ("gemv", "tc")
+        assert b.get("fixup", "kernel") in ("auto", "kernel", "cta")
