@@ -847,6 +847,22 @@ static void auto_shape(int M, const s4_weight* w, int sms, int* tn_out, int* gri
   *grid_out = grid;
 }
 
+// Tokens per tile, CTAs and fix-up form of a tcgen05 launch for bucket b (the table's values, the
+// automatic shape where it gives 0). s4_matmul and s4_matmul_gather both use it, so the two entry
+// points split a matmul's K range the same way and agree bit for bit.
+static int tc_launch_shape(const s4_ctx* ctx, const s4_weight* w, const Bucket& b, int M, int* tn, int* grid,
+                           bool* cta_fixup) {
+  const bool tc = b.family == S4_FAMILY_TC;
+  if (tc && b.tile != 0 && (b.tile < 16 || b.tile > 256 || b.tile % 16))
+    return fail(S4_ERR_INVALID, "tc tile must be a multiple of 16 in [16, 256] (got %d)", b.tile);
+  *tn = tc ? b.tile : 0;
+  *grid = ctx->sm_count;
+  if (*tn == 0) auto_shape(M, w, ctx->sm_count, tn, grid);
+  if (tc && b.split > 0) *grid = std::min(b.split, ctx->sm_count);
+  *cta_fixup = tc && use_cta_fixup(b, ctx, w);
+  return S4_OK;
+}
+
 int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, void* stream) {
   if (!ctx || !w) return fail(S4_ERR_INVALID, "NULL context or weight");
   if (w->ctx != ctx) return fail(S4_ERR_INVALID, "weight belongs to another context");
@@ -860,11 +876,10 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
   const Bucket b = choose(ctx, M, w->N, w->K);
   cudaError_t e = cudaSuccess;
   if (b.family == S4_FAMILY_TC) {
-    if (b.tile != 0 && (b.tile < 16 || b.tile > 256 || b.tile % 16))
-      return fail(S4_ERR_INVALID, "tc tile must be a multiple of 16 in [16, 256] (got %d)", b.tile);
-    int tn = b.tile, grid = ctx->sm_count;
-    if (tn == 0) auto_shape(M, w, ctx->sm_count, &tn, &grid);
-    if (b.split > 0) grid = std::min(b.split, ctx->sm_count);
+    int tn = 0, grid = 0;
+    bool cta = false;
+    const int rc = tc_launch_shape(ctx, w, b, M, &tn, &grid, &cta);
+    if (rc != S4_OK) return rc;
     // token rows per launch: the arrival counters hold one entry per (token block, n-block) tile
     const long long rows_cap = (long long)(kMaxTickets / w->nblk) * tn;
     for (long long r0 = 0; r0 < M; r0 += rows_cap) {
@@ -872,7 +887,7 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
       e = s4::launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x) + r0 * w->K,
                              static_cast<__half*>(y) + r0 * (w->glu ? w->N / 2 : w->N), ctx->partials, ctx->tickets,
                              kMaxTickets, ctx->err, rows, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, ctx->pdl,
-                             use_cta_fixup(b, ctx, w), w->glu);
+                             cta, w->glu);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch");
       ++ctx->launches;
     }
@@ -1081,13 +1096,17 @@ int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, in
   for (int d = 0; d < ndst; ++d)
     if (!dst[d]) return fail(S4_ERR_INVALID, "NULL destination %d", d);
   DeviceGuard guard(ctx->device);
-  int tn = 256, grid = ctx->sm_count;
-  auto_shape(M, w, ctx->sm_count, &tn, &grid);
+  // the dispatch table's tcgen05 shape for this weight and M (a GEMV bucket: the automatic shape), the
+  // same split as s4_matmul's
+  int tn = 0, grid = 0;
+  bool cta = false;
+  const int rc = tc_launch_shape(ctx, w, choose(ctx, M, w->N, w->K), M, &tn, &grid, &cta);
+  if (rc != S4_OK) return rc;
   if ((long long)((M + tn - 1) / tn) * w->nblk > kMaxTickets) return fail(S4_ERR_INVALID, "M too large for one launch");
   cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, w->wb, static_cast<const __half*>(x), ldx,
                                         reinterpret_cast<__half* const*>(dst), ndst, ldy, col0, ctx->partials,
                                         ctx->tickets, kMaxTickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tn,
-                                        grid, static_cast<cudaStream_t>(stream), ctx->pdl, false, w->glu);
+                                        grid, static_cast<cudaStream_t>(stream), ctx->pdl, cta, w->glu);
   if (e != cudaSuccess) return cuda_fail(e, "gathered tc gemm launch");
   ++ctx->launches;
   return S4_OK;
