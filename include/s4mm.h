@@ -47,6 +47,7 @@ extern "C" {
 typedef struct s4_ctx s4_ctx;
 typedef struct s4_weight s4_weight;
 typedef struct s4_chain s4_chain;
+typedef struct s4_manifest s4_manifest;
 
 /* Library version, (major << 16) | minor. */
 S4_API int s4_version(void);
@@ -116,6 +117,30 @@ S4_API int s4_weight_upload_glu(s4_ctx* ctx, const void* packed, const void* sca
                                 s4_weight** out);
 
 S4_API int s4_weight_free(s4_weight* w);
+
+/* Weight manifest of an exported engine: the JSON the exporter writes (convert/export_engine.py:29-34,
+ * 83-85), "shards": [{"path", "start", "bytes"}] laid out back to back from global offset 0 and
+ * "tensors": {name: {"offset", "bytes", "dtype", "shape", "N", "K"}} with global offsets. Parsing and
+ * lookups are host-only (no device, no context). s4_manifest_tensor is the engine's w(name)
+ * (web/public/engine/engine.js:175-180): the shard holding the tensor and the byte offset inside it
+ * (S4_ERR_INVALID "no tensor <name>" when absent, engine.js:177), its size, and N / K for a quantised
+ * projection's ".q" tensor (-1 otherwise). s4_manifest_shard gives a shard's path (valid while the
+ * manifest lives) and size. */
+S4_API int s4_manifest_open(const char* json, s4_manifest** out);
+S4_API int s4_manifest_free(s4_manifest* m);
+S4_API int s4_manifest_counts(const s4_manifest* m, int* nshards, int* ntensors);
+S4_API int s4_manifest_shard(const s4_manifest* m, int i, const char** path, size_t* bytes);
+S4_API int s4_manifest_tensor(const s4_manifest* m, const char* name, int* shard, size_t* offset, size_t* bytes,
+                              int* N, int* K);
+
+/* Upload the quantised projection `name` (the pair name.q / name.s of the manifest, N = the exported,
+ * 64-row padded N) from the engine's shard buffers: shards[i] is shard i's bytes, in host memory, or in
+ * device memory with flags = S4_UPLOAD_DEVICE (a device range must leave name.q 4-byte and name.s
+ * 2-byte aligned). Checks dtypes and sizes against N and K, then runs s4_weight_upload /
+ * s4_weight_upload_device. Replaces the shard upload + w(name) binding of a projection in
+ * Engine.create / plan() (engine.js:76-84, 175-180, 239). Synchronous. */
+S4_API int s4_weight_upload_named(s4_ctx* ctx, const s4_manifest* m, const void* const* shards, const char* name,
+                                  uint32_t flags, s4_weight** out);
 
 /* On-disk cache of repacked weights (the role of the worker's OPFS asset cache, worker.js:27-44,
  * 82-100, here holding the device layout so a later load skips decode and repack). A file is a

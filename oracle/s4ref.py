@@ -429,3 +429,66 @@ def unrepack_device(wq: np.ndarray, ws: np.ndarray, N: int, K: int):
     s6 = ws.reshape(nblk, kt, 8, 8, 2, 2).transpose(0, 2, 5, 3, 1, 4)     # -> nb, sub, h, g, kt, blk
     sc = s6.reshape(Np, Kp // BLOCK)[:N, :K // BLOCK]
     return np.ascontiguousarray(packed), np.ascontiguousarray(sc)
+
+
+# --------------------------------------------------------------------------------------------
+# exported engine layout  (convert/export_engine.py:29-43, 70-85)
+# --------------------------------------------------------------------------------------------
+def export_engine(tensors, shard_limit: int = 512 << 20, config=None):
+    """Restates the exporter's tensor index and shard split: tensors are appended in order to one byte
+    sequence, each at the next 256-byte aligned offset (``add``, :29-34; the padding is its own piece);
+    a quantised projection ``p`` becomes ``p.q`` (with ``N`` padded to a multiple of 64 by zero rows and
+    ``K``) then ``p.s`` (``add_q``, :36-43); the pieces are cut into shards, a new shard starting at the
+    piece that would push the current one past ``shard_limit`` (:70-78). ``tensors`` lists
+    ``(name, array)`` for plain tensors and ``(name, "q", W f32 [N, K])`` for projections. Returns
+    ``(manifest dict, [shard bytes], {name: (packed, scales)})``."""
+    pieces, index, quantised = [], {}, {}
+    offset = 0
+
+    def add(name, arr, **meta):
+        nonlocal offset
+        arr = np.ascontiguousarray(arr)
+        pad = (-offset) % 256
+        if pad:
+            pieces.append(b"\0" * pad)
+            offset += pad
+        index[name] = {"offset": offset, "bytes": arr.nbytes, "dtype": str(arr.dtype), "shape": list(arr.shape), **meta}
+        pieces.append(arr.tobytes())
+        offset += arr.nbytes
+
+    for t in tensors:
+        if len(t) == 3 and isinstance(t[1], str) and t[1] == "q":
+            name, _, W = t
+            N = W.shape[0]
+            Np = (N + 63) // 64 * 64
+            if Np != N:
+                W = np.concatenate([W, np.zeros((Np - N, W.shape[1]), np.float32)])
+            pk, sc, _ = quant(W)
+            add(name + ".q", pk, N=Np, K=W.shape[1])
+            add(name + ".s", sc)
+            quantised[name] = (pk, sc)
+        else:
+            add(*t)
+    shards, cur, cur_start, pos = [], [], 0, 0
+    for b in pieces:
+        if cur and pos + len(b) - cur_start > shard_limit:
+            shards.append((cur_start, cur))
+            cur, cur_start = [], pos
+        cur.append(b)
+        pos += len(b)
+    shards.append((cur_start, cur))
+    manifest = {"config": config or {},
+                "shards": [{"path": f"weights.{n}.bin", "start": s, "bytes": sum(len(b) for b in bs)}
+                           for n, (s, bs) in enumerate(shards)],
+                "tensors": index}
+    return manifest, [b"".join(bs) for _, bs in shards], quantised
+
+
+def resolve_tensor(manifest: dict, name: str):
+    """The engine's ``w(name)`` (web/public/engine/engine.js:175-180): the shard whose
+    [start, start + bytes) holds the tensor's offset, and the offset inside it."""
+    t = manifest["tensors"][name]
+    for i, s in enumerate(manifest["shards"]):
+        if s["start"] <= t["offset"] < s["start"] + s["bytes"]:
+            return i, t["offset"] - s["start"]
+    raise KeyError(name)

@@ -46,6 +46,13 @@ _SIGS = {
     "s4_fwht": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, _P]),
     "s4_weight_upload_glu": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.c_uint32, C.POINTER(_P)]),
     "s4_weight_free": (C.c_int, [_P]),
+    "s4_manifest_open": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
+    "s4_manifest_free": (C.c_int, [_P]),
+    "s4_manifest_counts": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "s4_manifest_shard": (C.c_int, [_P, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_size_t)]),
+    "s4_manifest_tensor": (C.c_int, [_P, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t),
+                                     C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "s4_weight_upload_named": (C.c_int, [_P, _P, C.POINTER(_P), C.c_char_p, C.c_uint32, C.POINTER(_P)]),
     "s4_weight_save": (C.c_int, [_P, C.c_char_p]),
     "s4_weight_load": (C.c_int, [_P, C.c_char_p, C.POINTER(_P)]),
     "s4_weight_info": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_size_t)]),
@@ -202,6 +209,51 @@ def _dev_buf(name: str, t, device: int, nbytes: int, dtype=None):
                                    f"{t.numel() * t.element_size()}{'' if t.is_contiguous() else ' (strided)'}")
 
 
+class Manifest:
+    """The weight manifest of an exported engine (``manifest.json`` of convert/export_engine.py:29-34,
+    83-85), parsed by the library (``s4_manifest_open``); :meth:`tensor` is the engine's ``w(name)``
+    (web/public/engine/engine.js:175-180). Needs no GPU."""
+
+    def __init__(self, manifest):
+        import json
+        load_library()
+        text = manifest if isinstance(manifest, (str, bytes)) else json.dumps(manifest)
+        h = _P()
+        _check(_lib.s4_manifest_open(text.encode() if isinstance(text, str) else text, C.byref(h)))
+        self.handle = h.value
+
+    @property
+    def shards(self):
+        """[(path, bytes)] in shard order."""
+        ns, nt = C.c_int(), C.c_int()
+        _check(_lib.s4_manifest_counts(self.handle, C.byref(ns), C.byref(nt)))
+        out = []
+        for i in range(ns.value):
+            p, b = C.c_char_p(), C.c_size_t()
+            _check(_lib.s4_manifest_shard(self.handle, i, C.byref(p), C.byref(b)))
+            out.append((p.value.decode(), b.value))
+        return out
+
+    def tensor(self, name: str) -> dict:
+        """``{shard, offset, bytes, N, K}`` of a tensor (offset inside its shard; N / K -1 unless it is a
+        projection's ``.q``). Raises S4Error ``no tensor <name>`` when absent (engine.js:177)."""
+        sh, off, nb, n, k = C.c_int(), C.c_size_t(), C.c_size_t(), C.c_int(), C.c_int()
+        _check(_lib.s4_manifest_tensor(self.handle, name.encode(), C.byref(sh), C.byref(off), C.byref(nb), C.byref(n),
+                                       C.byref(k)))
+        return {"shard": sh.value, "offset": off.value, "bytes": nb.value, "N": n.value, "K": k.value}
+
+    def close(self):
+        if self.handle:
+            _lib.s4_manifest_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Weight:
     """An uploaded, device-repacked int4 weight (the engine's resolved ``.q``/``.s`` pair)."""
 
@@ -271,6 +323,36 @@ class Context:
                 raise S4Error(ERR_INVALID, f"packed/scales sizes do not match N={N} K={K}")
             _check(_lib.s4_weight_upload(self.handle, p.ctypes.data, s.ctypes.data, N, K, 0, C.byref(h)))
         return Weight(self, h.value, N, K)
+
+    def upload_named(self, manifest: "Manifest", shards, name: str) -> Weight:
+        """Upload projection ``name`` (``name.q`` / ``name.s`` of the manifest) from the engine's shard
+        buffers (``s4_weight_upload_named``): ``shards`` lists every shard's bytes in manifest order, as
+        host uint8 arrays or as CUDA uint8 tensors on this context's device (all on one side). Synchronous."""
+        import torch
+        expect = manifest.shards
+        if len(shards) != len(expect):
+            raise S4Error(ERR_INVALID, f"{len(shards)} shard buffers for a manifest of {len(expect)} shards")
+        on_dev = [hasattr(b, "is_cuda") and b.is_cuda for b in shards]
+        if any(on_dev) and not all(on_dev):
+            raise S4Error(ERR_INVALID, "shard buffers must all be host arrays or all CUDA tensors")
+        keep, ptrs = [], []
+        for b, (path, nbytes) in zip(shards, expect):
+            if on_dev[0]:
+                _dev_buf(f"shard {path}", b, self.device, nbytes, torch.uint8)
+                ptrs.append(b.data_ptr())
+            else:
+                a = np.ascontiguousarray(np.frombuffer(b, dtype=np.uint8) if isinstance(b, (bytes, bytearray))
+                                         else np.asarray(b, dtype=np.uint8).reshape(-1))
+                if a.size < nbytes:
+                    raise S4Error(ERR_INVALID, f"shard {path}: {a.size} bytes, the manifest says {nbytes}")
+                keep.append(a)
+                ptrs.append(a.ctypes.data)
+        arr = (_P * len(ptrs))(*[_P(p) for p in ptrs])
+        h = _P()
+        _check(_lib.s4_weight_upload_named(self.handle, manifest.handle, arr, name.encode(),
+                                           UPLOAD_DEVICE if on_dev[0] else 0, C.byref(h)))
+        t = manifest.tensor(name + ".q")
+        return Weight(self, h.value, t["N"], t["K"])
 
     def upload_glu(self, packed, scales, I: int, K: int) -> Weight:
         """Upload a fused gate|up weight ([2I][K] MatMulNBits bytes, gate rows first) whose matmul
