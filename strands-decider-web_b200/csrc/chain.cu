@@ -104,31 +104,64 @@ struct ChainParams {
 // A CTA's share of one op: op-local chunks [c0, c1). The chunks of a phase (consecutive ops none
 // of which reads another's output) are concatenated and cut into min(G, U) equal contiguous
 // ranges, U = the phase's chunk count, so an n-block is split only where a CTA's range ends.
+//
+// Only the first and the last n-block of a range can be shared with other CTAs: every n-block in
+// between lies wholly inside the range and is written directly. The range and the kinds of its two
+// end segments are computed once per launch (chain_range_make, one thread per op at kernel entry, into
+// shared memory): they need 64-bit divisions, a slow software sequence, and the role warps that walk
+// the op list every launch (skipping ops with empty ranges) used to recompute them per op and per
+// segment, ~5 us per launch for a CTA whose range lies in the 14th op.
+enum ChainSeg { kSegDirect = 0, kSegPart0 = 1, kSegPartial = 2 };
 struct ChainRange {
-  int U, G, base, c0, c1;
+  int c0, c1;           // op-local chunks [c0, c1)
+  int nb0, nb1;         // first and last n-block of the range
+  int kind0, part0, np0;  // segment kind, part index and part count of n-block nb0
+  int kind1, part1, np1;  // the same for nb1
 };
 __device__ __forceinline__ int chain_begin(int b, int U, int G) { return (int)(((int64_t)b * U) / G); }
 __device__ __forceinline__ int chain_cta_of(int u, int U, int G) { return (int)((((int64_t)u + 1) * G - 1) / U); }
-__device__ __forceinline__ ChainRange chain_range(const ChainOp& op, int b, int grid) {
+__device__ __forceinline__ void chain_seg_calc(const ChainOp& op, int U, int G, int nb, int b, int* kind, int* part,
+                                               int* nparts) {
+  const int KT = op.ktiles, base = op.phase_base;
+  const int first = chain_cta_of(base + nb * KT, U, G), last = chain_cta_of(base + nb * KT + KT - 1, U, G);
+  *nparts = last - first + 1;
+  *part = b - first;
+  *kind = first == last ? kSegDirect : (*part == 0 ? kSegPart0 : kSegPartial);
+}
+__device__ __forceinline__ ChainRange chain_range_make(const ChainOp& op, int b, int grid) {
   ChainRange r;
-  r.U = op.phase_U;
-  r.G = min(grid, r.U);
-  r.base = op.phase_base;
-  const int u0 = b < r.G ? chain_begin(b, r.U, r.G) : 0, u1 = b < r.G ? chain_begin(b + 1, r.U, r.G) : 0;
+  const int U = op.phase_U, G = min(grid, U);
+  const int u0 = b < G ? chain_begin(b, U, G) : 0, u1 = b < G ? chain_begin(b + 1, U, G) : 0;
   const int n = op.nblk * op.ktiles;
-  r.c0 = min(max(u0 - r.base, 0), n);
-  r.c1 = max(min(u1 - r.base, n), r.c0);
+  r.c0 = min(max(u0 - op.phase_base, 0), n);
+  r.c1 = max(min(u1 - op.phase_base, n), r.c0);
+  r.nb0 = r.nb1 = 0;
+  r.kind0 = r.kind1 = kSegDirect;
+  r.part0 = r.part1 = 0;
+  r.np0 = r.np1 = 1;
+  if (r.c0 < r.c1) {
+    r.nb0 = r.c0 / op.ktiles;
+    r.nb1 = (r.c1 - 1) / op.ktiles;
+    chain_seg_calc(op, U, G, r.nb0, b, &r.kind0, &r.part0, &r.np0);
+    chain_seg_calc(op, U, G, r.nb1, b, &r.kind1, &r.part1, &r.np1);
+  }
   return r;
 }
-// Kind of the segment of n-block nb inside range r.
-enum ChainSeg { kSegDirect = 0, kSegPart0 = 1, kSegPartial = 2 };
-__device__ __forceinline__ int chain_seg_kind(const ChainOp& op, const ChainRange& r, int nb, int* part, int* nparts) {
-  const int KT = op.ktiles;
-  const int first = chain_cta_of(r.base + nb * KT, r.U, r.G), last = chain_cta_of(r.base + nb * KT + KT - 1, r.U, r.G);
-  *nparts = last - first + 1;
-  *part = (int)blockIdx.x - first;
-  if (first == last) return kSegDirect;
-  return *part == 0 ? kSegPart0 : kSegPartial;
+// Kind of the segment of n-block nb inside range r (nb within [r.nb0, r.nb1]).
+__device__ __forceinline__ int chain_seg_kind(const ChainRange& r, int nb, int* part, int* nparts) {
+  if (nb == r.nb0) {
+    *part = r.part0;
+    *nparts = r.np0;
+    return r.kind0;
+  }
+  if (nb == r.nb1) {
+    *part = r.part1;
+    *nparts = r.np1;
+    return r.kind1;
+  }
+  *part = 0;
+  *nparts = 1;
+  return kSegDirect;
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
@@ -166,10 +199,14 @@ struct ChainSmem {
   float4* pub;  // [2] finished segments for the publisher
   uint64_t *full, *empty, *xfull, *xempty, *evfull, *evempty, *pubfull, *pubempty;
   const ChainOp* ops;  // op descriptor cache (the first kChainCachedOps)
+  const ChainRange* rng;  // this CTA's range of each cached op
   int* fail;
 };
 __device__ __forceinline__ ChainOp chain_op_at(const ChainParams& p, const ChainSmem& sm, int i) {
   return i < kChainCachedOps ? sm.ops[i] : p.ops[i];
+}
+__device__ __forceinline__ ChainRange chain_range_at(const ChainSmem& sm, const ChainOp& op, int i, int b, int G) {
+  return i < kChainCachedOps ? sm.rng[i] : chain_range_make(op, b, G);
 }
 
 // fp32 sums of one 16-row sub-tile (lane layout of gemv_tile: rows g, g+8; tokens 2t, 2t+1 per
@@ -196,7 +233,7 @@ __device__ __forceinline__ bool chain_flush(const ChainOp& op, const ChainRange&
                                             const ChainSmem& sm, int nb, float (&acc)[MG][4], int& evk, int& pubk) {
   const int sub = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int part, nparts;
-  const int kind = chain_seg_kind(op, r, nb, &part, &nparts);
+  const int kind = chain_seg_kind(r, nb, &part, &nparts);
   float4* dst;
   uint64_t* full;
   if (kind == kSegPart0) {
@@ -327,7 +364,7 @@ __device__ bool chain_publish_op(const ChainOp& op, const ChainRange& r, const C
     const int nb = c / KT;
     c = min(r.c1, (nb + 1) * KT);
     int part, nparts;
-    const int kind = chain_seg_kind(op, r, nb, &part, &nparts);
+    const int kind = chain_seg_kind(r, nb, &part, &nparts);
     if (kind == kSegPart0) continue;  // the reducer's
     const int e = pubk & 1;
     if (!mbar_wait(sm.pubfull + e, (uint32_t)(pubk >> 1) & 1u)) return false;
@@ -576,6 +613,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
   __shared__ int s_slot_unit[kChainMaxSlots];
   __shared__ int s_pub_nb[2];
   __shared__ __align__(16) ChainOp s_ops[kChainCachedOps];
+  __shared__ ChainRange s_rng[kChainCachedOps];
   ChainSmem sm;
   sm.slot_unit = s_slot_unit;
   sm.pub_nb = s_pub_nb;
@@ -592,6 +630,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
   sm.pubfull = sm.evempty + kChainEv;
   sm.pubempty = sm.pubfull + 2;
   sm.ops = s_ops;
+  sm.rng = s_rng;
   sm.fail = &s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -601,6 +640,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     const uint32_t* src = reinterpret_cast<const uint32_t*>(p.ops);
     uint32_t* dst = reinterpret_cast<uint32_t*>(s_ops);
     for (int q = threadIdx.x; q < ncached; q += kChainThreads) dst[q] = src[q];
+    // this CTA's range of every cached op, one thread per op (ordered before use by the barrier below)
+    for (int i = threadIdx.x; i < min(p.nops, kChainCachedOps); i += kChainThreads)
+      s_rng[i] = chain_range_make(p.ops[i], b, G);
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.slots; ++s) {
@@ -640,7 +682,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       int seq = 0;
       for (int i = 0; i < p.nops && ok; ++i) {
         const ChainOp op = chain_op_at(p, sm, i);
-        const ChainRange r = chain_range(op, b, G);
+        const ChainRange r = chain_range_at(sm, op, i, b, G);
         for (int g0 = r.c0; g0 < r.c1; g0 += kChainGroup, ++seq) {
           const int n = min(kChainGroup, r.c1 - g0);
           const int slot = seq % p.slots;
@@ -675,7 +717,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
       const uint64_t pol = policy_evict_last();  // every CTA reads the same activations
       for (int i = 0; i < p.nops && ok; ++i) {
         const ChainOp op = chain_op_at(p, sm, i);
-        ChainRange r = chain_range(op, b, G);
+        ChainRange r = chain_range_at(sm, op, i, b, G);
         if (i == p.dyn_op) {  // the whole of K: any n-block may be claimed
           r.c0 = 0;
           r.c1 = op.ktiles;
@@ -722,7 +764,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     int pubk = 0;
     for (int i = 0; i < p.nops && ok; ++i) {
       const ChainOp op = chain_op_at(p, sm, i);
-      const ChainRange r = chain_range(op, b, G);
+      const ChainRange r = chain_range_at(sm, op, i, b, G);
       if (r.c0 >= r.c1) continue;
       ok = chain_publish_op<MG>(op, r, p, sm, i, pubk);
     }
@@ -732,11 +774,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     int evk = 0;
     for (int i = 0; i < p.nops && ok; ++i) {
       const ChainOp op = chain_op_at(p, sm, i);
-      const ChainRange r = chain_range(op, b, G);
+      const ChainRange r = chain_range_at(sm, op, i, b, G);
       if (r.c0 >= r.c1) continue;
       const int nb = (r.c1 - 1) / op.ktiles;  // only the last segment of a range can be a part 0
       int part, nparts;
-      if (chain_seg_kind(op, r, nb, &part, &nparts) != kSegPart0) continue;
+      if (chain_seg_kind(r, nb, &part, &nparts) != kSegPart0) continue;
       ok = chain_reduce<MG>(op, r, p, sm, i, nb, nparts, evk);
       ++evk;
     }
@@ -746,7 +788,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     uint32_t phase = 0;
     for (int i = 0; i < p.nops && ok; ++i) {
       const ChainOp op = chain_op_at(p, sm, i);
-      const ChainRange r = chain_range(op, b, G);
+      const ChainRange r = chain_range_at(sm, op, i, b, G);
       if (r.c0 >= r.c1) continue;
       ok = chain_consume<MG>(op, r, p, sm, slot, phase, xk, evk, pubk);
       ++xk;
