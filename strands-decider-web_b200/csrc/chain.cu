@@ -614,6 +614,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
   __shared__ int s_pub_nb[2];
   __shared__ __align__(16) ChainOp s_ops[kChainCachedOps];
   __shared__ ChainRange s_rng[kChainCachedOps];
+  __shared__ int s_act[kChainCachedOps];  // ops with a range in this CTA (and the dynamic op), in order
+  __shared__ int s_nact;                  // their count, or -1 when the op list is longer than the cache
   ChainSmem sm;
   sm.slot_unit = s_slot_unit;
   sm.pub_nb = s_pub_nb;
@@ -666,6 +668,19 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
   }
   __syncwarp();  // each warp reaches the (warp-aligned) block barrier as a whole after its role code
   __syncthreads();
+  // the ops this CTA takes part in: every role walks only these (a walk over all ops cost each CTA
+  // ~0.1 us per op it has no range in)
+  if (threadIdx.x == 0) {
+    int n = -1;
+    if (p.nops <= kChainCachedOps) {
+      n = 0;
+      for (int i = 0; i < p.nops; ++i)
+        if (s_rng[i].c0 < s_rng[i].c1 || i == p.dyn_op) s_act[n++] = i;
+    }
+    s_nact = n;
+  }
+  __syncthreads();
+  const int nwalk = s_nact >= 0 ? s_nact : p.nops;
   // Launched with programmatic stream serialization, the next grid in the stream may start its
   // CTAs as ours exit. Only the producer runs before the previous grid has completed: it reads
   // nothing but the weights (immutable after upload) and fills this CTA's ring. Every other role
@@ -680,7 +695,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       int seq = 0;
-      for (int i = 0; i < p.nops && ok; ++i) {
+      for (int ii = 0; ii < nwalk && ok; ++ii) {
+        const int i = s_nact >= 0 ? s_act[ii] : ii;
         const ChainOp op = chain_op_at(p, sm, i);
         const ChainRange r = chain_range_at(sm, op, i, b, G);
         for (int g0 = r.c0; g0 < r.c1; g0 += kChainGroup, ++seq) {
@@ -715,7 +731,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     if (lane == 0) {
       int xk = 0;
       const uint64_t pol = policy_evict_last();  // every CTA reads the same activations
-      for (int i = 0; i < p.nops && ok; ++i) {
+      for (int ii = 0; ii < nwalk && ok; ++ii) {
+        const int i = s_nact >= 0 ? s_act[ii] : ii;
         const ChainOp op = chain_op_at(p, sm, i);
         ChainRange r = chain_range_at(sm, op, i, b, G);
         if (i == p.dyn_op) {  // the whole of K: any n-block may be claimed
@@ -762,7 +779,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
   } else if (warp == kChainPublisherWarp) {
     // ---------------- publisher ----------------
     int pubk = 0;
-    for (int i = 0; i < p.nops && ok; ++i) {
+    for (int ii = 0; ii < nwalk && ok; ++ii) {
+        const int i = s_nact >= 0 ? s_act[ii] : ii;
       const ChainOp op = chain_op_at(p, sm, i);
       const ChainRange r = chain_range_at(sm, op, i, b, G);
       if (r.c0 >= r.c1) continue;
@@ -772,7 +790,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
   } else if (warp == kChainReducerWarp) {
     // ---------------- reducer ----------------
     int evk = 0;
-    for (int i = 0; i < p.nops && ok; ++i) {
+    for (int ii = 0; ii < nwalk && ok; ++ii) {
+        const int i = s_nact >= 0 ? s_act[ii] : ii;
       const ChainOp op = chain_op_at(p, sm, i);
       const ChainRange r = chain_range_at(sm, op, i, b, G);
       if (r.c0 >= r.c1) continue;
@@ -786,7 +805,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainPara
     // ---------------- consumers ----------------
     int slot = 0, xk = 0, evk = 0, pubk = 0;
     uint32_t phase = 0;
-    for (int i = 0; i < p.nops && ok; ++i) {
+    for (int ii = 0; ii < nwalk && ok; ++ii) {
+        const int i = s_nact >= 0 ? s_act[ii] : ii;
       const ChainOp op = chain_op_at(p, sm, i);
       const ChainRange r = chain_range_at(sm, op, i, b, G);
       if (r.c0 >= r.c1) continue;
