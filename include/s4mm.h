@@ -186,9 +186,10 @@ S4_API int s4_matmul_host_async(s4_ctx* ctx, const s4_weight* w, const uint16_t*
  * device array that every GPU loading this library holds until exit. It calls no allocator. It needs
  * no live context either: the weight records its device and SM count, so it may be called after
  * s4_destroy of the context the weight was uploaded with. Limit: ceil(M/256) * ceil(N/128) <= 16384
- * (larger calls are rejected with S4_ERR_INVALID); the CTA count is the SM count, capped so that each
- * CTA's two partial slots of (M rounded up to 16, at most 256) x 128 fp32 fit the array (31 CTAs at
- * M >= 256, all 148 SMs at M <= 48). The first call on a device looks up the array's device address
+ * (larger calls are rejected with S4_ERR_INVALID); the CTA count is a divisor of the tile count between
+ * half the SMs and all of them when there is one (whole tiles, no partials), else the SM count capped so
+ * that each CTA's two partial slots of (M rounded up to 16, at most 256) x 128 fp32 fit the array (31
+ * CTAs at M >= 256, all 148 SMs at M <= 48). The first call on a device looks up the array's device address
  * (do it before any stream capture; a cudaDeviceReset of that device leaves the looked-up address
  * stale, so do not reset a device this library has used). All calls share the array: calls that
  * overlap on the GPU race. A bounded wait that expires sets the array's error word, which stays set

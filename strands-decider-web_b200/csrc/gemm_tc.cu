@@ -910,9 +910,16 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   // zero. The error word is left as it is: it accumulates until s4_noalloc_check_errors clears it.
   cudaError_t e = cudaMemsetAsync(base, 0, (size_t)tiles * sizeof(uint32_t), st);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: clearing the static scratch failed");
-  // partials: two slots of tn x 128 fp32 per CTA
+  // CTAs: whole tiles need no partials, so a CTA count that divides the tile count (at least half the
+  // SMs) runs at any size; otherwise stream-K with two partial slots of tn x 128 fp32 per CTA, as many
+  // CTAs as the array holds
   const int max_grid = (int)(kStaticPartialBytes / (2ull * tn * 128 * sizeof(float)));
-  const int grid = w->sm_count < max_grid ? w->sm_count : max_grid;
+  int grid = w->sm_count < max_grid ? w->sm_count : max_grid;
+  for (int g = w->sm_count; g * 2 >= w->sm_count && g > grid; --g)
+    if (tiles % g == 0) {
+      grid = g;
+      break;
+    }
   // split tiles are summed by the fix-up kernel launched right after (it reads the partials from the
   // same static array); a second launch allocates nothing either
   e = launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
