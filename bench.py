@@ -54,6 +54,18 @@ def load_pkg():
     return mod
 
 
+def upload_graph(g, stream) -> bool:
+    """Upload an instantiated CUDA graph to the device before it is first replayed (cuGraphUpload:
+    executes nothing), so the first replay's upload does not land inside a timed region."""
+    try:
+        from cuda.bindings import driver as cu
+        exec_ = g.raw_cuda_graph_exec()
+        err, = cu.cuGraphUpload(cu.CUgraphExec(int(exec_)), cu.CUstream(int(stream.cuda_stream)))
+        return int(err) == 0
+    except Exception:
+        return False
+
+
 def bench_config():
     """The workload both arms report (the same dict, so the two lines' configs compare equal)."""
     return {"workload": "decode_gemv_sweep_config2", "M": MS, "shapes_KN": [[K, N] for _, K, N in SHAPES]}
@@ -502,6 +514,7 @@ def run_ours(args, rank, world, local_rank):
                 sweep(rot, cap_stream)
             call_graphs.append(g2)
     stream.wait_stream(cap_stream)
+    graphs_uploaded = all([upload_graph(g, stream) for g in step_graphs.values()])
     torch.cuda.synchronize(dev)
 
     def steps_on_stream(k: int, start: int):
@@ -568,6 +581,8 @@ def run_ours(args, rank, world, local_rank):
             with torch.cuda.graph(g, stream=cap_stream):
                 chains[rot].run_host(hx[k], sets[k][0], hy[k], sets[k][1], cap_stream)
             e2e_graphs.append(g)
+    for g in e2e_graphs:
+        upload_graph(g, stream)
     torch.cuda.synchronize(dev)
 
     def e2e_step():
@@ -722,7 +737,8 @@ def run_ours(args, rank, world, local_rank):
             "config": bench_config(),
             "setup": {"launch": "the 16 matmuls of a step as one chained launch; the timed steps are one CUDA "
                                 "graph of that many launches back to back on one stream (programmatic dependent "
-                                "launch)",
+                                "launch), uploaded to the device before the timed region",
+                      "graph_uploaded": graphs_uploaded,
                       "weight_copies": COPIES,
                       "l2": "inputs larger than L2: 8 rotating weight copies (272 MB) per step sequence",
                       "parallelism": f"dp{world} (weights replicated, no collective)"},
