@@ -533,10 +533,11 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    steps_on_stream(args.warmup, 0)
-    barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # the clock sampler starts (it waits for its first reading) before the warm-up, so the GPU is not
+    # left idle, and clocking down, right before the timed steps
     with ClockSampler(local_rank) as clocks:
+        steps_on_stream(args.warmup, 0)
         barrier()
         e0.record(stream)
         steps_on_stream(args.steps, args.warmup)
@@ -982,11 +983,11 @@ def run_gemm(args, rank, world, local_rank):
         for r in range(reps):
             call(r)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
-        g.replay()
-    torch.cuda.synchronize(dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize(dev)
         a.record(stream)
         for _ in range(args.steps):
             g.replay()

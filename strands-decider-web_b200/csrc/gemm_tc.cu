@@ -906,10 +906,8 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
   uint32_t* err = reinterpret_cast<uint32_t*>(base + kStaticErrOffset);
   float* partials = reinterpret_cast<float*>(base + kStaticPartialOffset);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // the previous call left its counters at zero unless it failed part-way: clear what must start at
-  // zero. The error word is left as it is: it accumulates until s4_noalloc_check_errors clears it.
-  cudaError_t e = cudaMemsetAsync(base, 0, (size_t)tiles * sizeof(uint32_t), st);
-  if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: clearing the static scratch failed");
+  // Nothing needs clearing per call: split tiles are summed by the fix-up kernel, which uses no tile
+  // counters, and the error word accumulates until s4_noalloc_check_errors clears it.
   // CTAs: whole tiles need no partials, so a CTA count that divides the tile count (at least half the
   // SMs) runs at any size; otherwise stream-K with two partial slots of tn x 128 fp32 per CTA, as many
   // CTAs as the array holds
@@ -922,7 +920,7 @@ extern "C" int s4_matmul_noalloc(const s4_weight* w, const void* x, int M, void*
     }
   // split tiles are summed by the fix-up kernel launched right after (it reads the partials from the
   // same static array); a second launch allocates nothing either
-  e = launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
+  const cudaError_t e = launch_tc_gemm(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), partials, tickets,
                      (int)kStaticTicketCount, err, M, w->N, w->K, w->nblk, w->ktiles, tn, grid, st, true, false, 0);
   if (e != cudaSuccess) return record_error(S4_ERR_CUDA, "s4_matmul_noalloc: tcgen05 GEMM launch failed");
   return S4_OK;
