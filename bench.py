@@ -810,7 +810,8 @@ def run_stack(args, rank, world, local_rank):
             fused = serve.FusedColshardStack(ctx, None, rank, world, fuse_silu=bool(args.fuse_silu))
             stack = fused.stack
         else:
-            stack = serve.CudaStack(ctx, rank=rank, world=world, fuse_silu=bool(args.fuse_silu))
+            stack = serve.CudaStack(ctx, rank=rank, world=world, fuse_silu=bool(args.fuse_silu),
+                                    fuse_norm=bool(args.fuse_norm))
         x = torch.from_numpy(np.random.default_rng(0).standard_normal((2048, serve.HIDDEN)).astype(np.float16)).to(dev)
         timing = {"on": False}
 
@@ -832,7 +833,8 @@ def run_stack(args, rank, world, local_rank):
         tokens_per_step = 2048 * 1  # the prompt, whatever the number of ranks (strong scaling)
         label = f"config4_stack_2048_prompt_colshard_{args.gather}"
     else:
-        stack = serve.CudaStack(ctx, fuse_silu=bool(args.fuse_silu))  # weights replicated on every rank
+        # weights replicated on every rank
+        stack = serve.CudaStack(ctx, fuse_silu=bool(args.fuse_silu), fuse_norm=bool(args.fuse_norm))
         lengths = serve.request_lengths(4096)[: args.requests]
         mine = serve.lpt_shard(lengths, world)[rank]
         chunks = serve.pack_chunks(lengths[mine], 8192)
@@ -917,6 +919,9 @@ def run_stack(args, rank, world, local_rank):
             "gather_share": comm_share,
             "cuda_graph": bool(args.workload == "stack" and args.graph),
             "silu_mul": "in the gate|up GEMM epilogue" if args.fuse_silu else "separate kernel",
+            "add_norm": ("residual add in the out_proj / down GEMM epilogue, one row pass"
+                         if args.fuse_norm and not (args.workload == "stack" and args.gather == "fused")
+                         else "separate kernel"),
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
@@ -1128,6 +1133,9 @@ def main():
                     help="stack: replay the whole forward as one CUDA graph (1, default) or launch eagerly (0)")
     ap.add_argument("--fuse-silu", type=int, default=1,
                     help="stack/serve: SiLU*mul in the gate|up GEMM epilogue (1, default) or as its own kernel (0)")
+    ap.add_argument("--fuse-norm", type=int, default=0,
+                    help="stack/serve on one GPU: the residual add of out_proj / down in the GEMM epilogue "
+                         "(s4_matmul_add_rmsnorm, 1) or the separate ADD_NORM kernel (0, default)")
     ap.add_argument("--shape", choices=sorted(GEMM_SHAPES), default="gate_up", help="gemm: the projection shape")
     ap.add_argument("--m", type=int, default=64, help="gemm: tokens per call")
     ap.add_argument("--noalloc", action="store_true", help="gemm: time s4_matmul_noalloc instead of s4_matmul")

@@ -239,6 +239,17 @@ S4_API int s4_silu_mul(s4_ctx* ctx, const void* big, int M, int I, void* mid, vo
 S4_API int s4_add_rmsnorm(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps, void* h,
                           void* stream);
 
+/* A projection followed by ADD_NORM in one call (out_proj / o_proj / down then post_norm / in_norm,
+ * web/public/engine/engine.js:247, 277; wgsl.js:55-78): y = x @ W^T is never stored; instead
+ * resid[M][N] (fp32, updated in place) += f16(y) and h[M][N] = f16(resid * rsqrt(mean(resid^2) + eps)
+ * * norm_w), norm_w fp32 [N] (the stored 1 + weight) or NULL for ones. On the tcgen05 path (N a
+ * multiple of 32) the residual add and the row sums of squares run in the GEMM's epilogue and one
+ * row kernel normalises; on the GEMV path y goes through h and is normalised in place. x [M][K] fp16.
+ * Not for fused gate|up weights. DEVICE pointers, 16-byte aligned; asynchronous on `stream`. Uses the
+ * context's scratch, so calls on one context must not overlap on the GPU. */
+S4_API int s4_matmul_add_rmsnorm(s4_ctx* ctx, const s4_weight* w, const void* x, int M, float* resid,
+                                 const float* norm_w, float eps, void* h, void* stream);
+
 /* Online input rotation of a tensor exported with `had: n` (engine.js:238, wgsl.js:94-110): every
  * contiguous n-block of a[M][K] (fp16, K % n == 0, n a power of two in [2, 32768]) is replaced in place
  * by its orthonormal Walsh-Hadamard transform, computed in fp32 with the shader's butterfly order and

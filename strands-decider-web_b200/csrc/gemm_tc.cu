@@ -103,6 +103,14 @@ struct TcParams {
   int dpq;       // whole tiles per CTA (data-parallel part): CTA b takes tiles [b*dpq, (b+1)*dpq)
   int sk_base;   // first unit of the stream-K part (dpq * grid * ktiles)
   int sk_total;  // units of the stream-K part, split evenly over the grid
+  // Residual add + RMSNorm epilogue (resid != nullptr): instead of storing y, each output adds
+  // f16(y) to the fp32 residual stream resid[tok * ldr + n] in place and the squares of the updated
+  // values are summed per 32-column group into ssp[(n / 32) * ldss + tok]; a row kernel then
+  // normalises (ADD_NORM, web/public/engine/wgsl.js:55-78, after out_proj / down, engine.js:247, 277).
+  float* resid;
+  int64_t ldr;
+  float* ssp;
+  int64_t ldss;
 };
 
 // Output stores. Each destination is the local buffer or, for the column-sharded prefill, a peer's
@@ -112,6 +120,52 @@ struct TcParams {
 // next tile's main loop.
 __device__ __forceinline__ int64_t tc_out_off(const TcParams& p, int tok, int ncol) {
   return (int64_t)tok * p.ldy + p.ycol0 + ncol;
+}
+
+// resid[tok][n0 .. n0 + 8) = a, b + f16 outputs v (the projection's y, rounded to fp16 as the
+// reference stores it; a, b the loaded residual); returns the sum of the updated values' squares, in
+// column order
+__device__ __forceinline__ float tc_add_resid8(const TcParams& p, int tok, int n0, float4 a, float4 b,
+                                               const uint4& v) {
+  float4* r = reinterpret_cast<float4*>(p.resid + (int64_t)tok * p.ldr + n0);
+  const __half2* h2 = reinterpret_cast<const __half2*>(&v);
+  const float2 y0 = __half22float2(h2[0]), y1 = __half22float2(h2[1]);
+  const float2 y2 = __half22float2(h2[2]), y3 = __half22float2(h2[3]);
+  a.x += y0.x;
+  a.y += y0.y;
+  a.z += y1.x;
+  a.w += y1.y;
+  b.x += y2.x;
+  b.y += y2.y;
+  b.z += y3.x;
+  b.w += y3.y;
+  r[0] = a;
+  r[1] = b;
+  float ss = a.x * a.x;
+  ss += a.y * a.y;
+  ss += a.z * a.z;
+  ss += a.w * a.w;
+  ss += b.x * b.x;
+  ss += b.y * b.y;
+  ss += b.z * b.z;
+  ss += b.w * b.w;
+  return ss;
+}
+
+// the residual values tc_add_resid8 needs for tokens tok .. tok + 16 of this lane (j = 0, 1: token
+// tok + j * 8 + lane / 4); rows at or past M read nothing
+__device__ __forceinline__ void tc_load_resid16(const TcParams& p, int tok, int n0, int lane, float4 (&r)[2][2]) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int t = tok + j * 8 + (lane >> 2);
+    if (t < p.M && n0 < p.N) {
+      const float4* src = reinterpret_cast<const float4*>(p.resid + (int64_t)t * p.ldr + n0);
+      r[j][0] = src[0];
+      r[j][1] = src[1];
+    } else {
+      r[j][0] = r[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
 }
 __device__ __forceinline__ void tc_store_all(const TcParams& p, int64_t off, __half h) {
   for (int d = 0; d < p.ndst; ++d) p.ydst[d][off] = h;
@@ -442,6 +496,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       const int tok0 = tb * p.tn;
       const int ncol = nb * 128 + nl;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
+      if (p.resid && full && !failed) {
+        // the tile's residual rows go to L2 while its MMAs run, so the epilogue's loads hit L2
+        const int nbytes = min(128, p.N - nb * 128) * 4;
+        for (int t = et; t < p.tn && tok0 + t < p.M; t += 128)
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.resid + (int64_t)(tok0 + t) * p.ldr +
+                                                                          nb * 128),
+                       "r"(nbytes)
+                       : "memory");
+      }
       if (!failed && !mbar_wait(accf + buf, (si >> 1) & 1)) {
         set_error(p.err, kErrWaitTimeout);
         failed = true;  // keep walking segments so the named barriers below stay matched
@@ -492,8 +555,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       } else if (full) {
         if (!failed) {
           tc_fence_after();
+          // residual mode: this lane's residual values of the next 16 tokens are loaded one chunk
+          // ahead (t = j * 8 + lane / 4, columns n0 .. n0 + 8)
+          const int n0r = nb * 128 + q * 32 + (lane & 3) * 8;
+          float4 rnext[2][2];
+          if (p.resid) tc_load_resid16(p, tok0, n0r, lane, rnext);
           for (int cb = 0; cb < p.tn; cb += 16) {
             float v[16];
+            float4 rcur[2][2];
+            if (p.resid) {
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                rcur[j][0] = rnext[j][0];
+                rcur[j][1] = rnext[j][1];
+              }
+              if (cb + 16 < p.tn) tc_load_resid16(p, tok0 + cb + 16, n0r, lane, rnext);
+            }
             tmem_ld16(taddr + cb, v);
             if (p.vec) {
               // transpose 32 n x 16 tokens through shared memory, then 16-byte stores of 8 n
@@ -506,7 +583,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
                 const uint4 val = *reinterpret_cast<const uint4*>(epi_stage + t * 32 + c * 8);
                 const int tok = tok0 + cb + t;
                 const int n0 = nb * 128 + q * 32 + c * 8;
-                if (tok < p.M && n0 < p.N) {
+                if (p.resid) {
+                  // residual add; the four lanes of a token hold its 32 columns of this quarter
+                  float ss = (tok < p.M && n0 < p.N) ? tc_add_resid8(p, tok, n0, rcur[j][0], rcur[j][1], val) : 0.f;
+                  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                  if (c == 0 && tok < p.M && n0 < p.N) p.ssp[(int64_t)(nb * 4 + q) * p.ldss + tok] = ss;
+                } else if (tok < p.M && n0 < p.N) {
                   const int64_t off = tc_out_off(p, tok, n0);
                   if (n0 + 8 <= p.N) {
                     *reinterpret_cast<uint4*>(p.ydst[0] + off) = val;
@@ -687,6 +770,32 @@ __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcParams p) {
     }
     return;
   }
+  if (p.resid) {  // residual add + per-group sums of squares (see TcParams)
+    float ss[8], rv[8];
+    float* rrow = p.resid + (int64_t)(tok0 + r0) * p.ldr + ncol;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) rv[e] = (r0 + e < rows && ncol < p.N) ? rrow[(int64_t)e * p.ldr] : 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ss[e] = 0.f;
+      if (r0 + e < rows && ncol < p.N) {
+        const float a = rv[e] + __half2float(__float2half_rn(acc[e]));
+        rrow[(int64_t)e * p.ldr] = a;
+        ss[e] = a * a;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) ss[e] += __shfl_xor_sync(0xffffffffu, ss[e], o);
+    if ((nl & 31) == 0 && ncol < p.N) {
+      float* dst = p.ssp + (int64_t)(nb * 4 + (nl >> 5)) * p.ldss + tok0 + r0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (r0 + e < rows) dst[e] = ss[e];
+    }
+    return;
+  }
   if (ncol < p.N) {
     const int64_t off0 = tc_out_off(p, tok0 + r0, ncol);
     if (p.ndst == 1) {
@@ -731,7 +840,8 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
                               __half* const* ydst,
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
-                              cudaStream_t stream, bool pdl, bool ticket_fixup, int glu) {
+                              cudaStream_t stream, bool pdl, bool ticket_fixup, int glu, float* resid,
+                              int64_t ldr, float* ssp, int64_t ldss) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   int tn = tile_n > 0 ? tile_n : (M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16);
@@ -749,6 +859,10 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
   p.vec = (ldy % 8 == 0 && ycol0 % 8 == 0) ? 1 : 0;
   for (int d = 0; d < ndst; ++d)
     if (reinterpret_cast<uintptr_t>(ydst[d]) & 15) p.vec = 0;
+  p.resid = resid;
+  p.ldr = ldr;
+  p.ssp = ssp;
+  p.ldss = ldss;
   p.partials = partials;
   p.tickets = tickets;
   p.err = err;
@@ -768,6 +882,11 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
   const int tiles = p.ntb * nblk;
   // the fused SiLU*mul epilogue stores 8 outputs at a time and has no in-kernel ticket fix-up
   if (glu && (!p.vec || ticket_fixup || N % 128)) return cudaErrorInvalidValue;
+  // the residual epilogue: 16-byte residual accesses of 8 columns, whole 32-column groups, the
+  // fix-up kernel for split tiles, no fused gate|up
+  if (resid && (!p.vec || ticket_fixup || glu || N % 32 || ldr % 4 || ldr < N || !ssp || ldss < M ||
+                (reinterpret_cast<uintptr_t>(resid) & 15)))
+    return cudaErrorInvalidValue;
   p.dpq = tiles / p.grid;
   // every CTA's stream-K range must hold at least one unit: an empty range inside a split tile's
   // CTA span would count as a part that never arrives. With fewer leftover units than CTAs, one wave
@@ -836,7 +955,7 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const uint8_t* 
                            bool ticket_fixup, int glu) {
   __half* dst[1] = {y};
   return launch_tc_gemm_ex(wq, ws, wb, x, K, dst, 1, glu ? N / 2 : N, 0, partials, tickets, max_tickets, err, M, N, K,
-                           nblk, ktiles, tile_n, grid, stream, pdl, ticket_fixup, glu);
+                           nblk, ktiles, tile_n, grid, stream, pdl, ticket_fixup, glu, nullptr, 0, nullptr, 0);
 }
 
 }  // namespace s4

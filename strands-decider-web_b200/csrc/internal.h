@@ -49,6 +49,7 @@ struct s4_ctx {
   float* partials = nullptr;      // tcgen05 split-K partials
   uint32_t* tickets = nullptr;    // tcgen05 tile arrival counters (self-resetting)
   uint32_t* err = nullptr;        // device error word
+  float* norm_ss = nullptr;       // per-32-column sums of squares of s4_matmul_add_rmsnorm (kNormSums floats)
   void* dx = nullptr;             // staging for s4_matmul_host
   void* dy = nullptr;
   size_t dx_cap = 0, dy_cap = 0;

@@ -24,9 +24,11 @@ __device__ __forceinline__ float block_sum_256(float v, float* red) {
 constexpr int kNormMaxNV = 8;
 
 template <int NV>
-__global__ void __launch_bounds__(256) add_rmsnorm_reg_kernel(float* __restrict__ x, const __half* __restrict__ y,
+// y and h may be the same buffer (the projection's output normalised in place): every thread reads
+// its elements of y before the block reduction and writes the same elements of h after it.
+__global__ void __launch_bounds__(256) add_rmsnorm_reg_kernel(float* __restrict__ x, const __half* y,
                                                               const float* __restrict__ w, int D, float eps,
-                                                              __half* __restrict__ h) {
+                                                              __half* h) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float red[8];
@@ -64,9 +66,8 @@ __global__ void __launch_bounds__(256) add_rmsnorm_reg_kernel(float* __restrict_
   }
 }
 
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x, const __half* __restrict__ y,
-                                                          const float* __restrict__ w, int D, float eps,
-                                                          __half* __restrict__ h) {
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x, const __half* y,
+                                                          const float* __restrict__ w, int D, float eps, __half* h) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float red[8];
@@ -87,6 +88,50 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x,
     const float a = xr[c];
     h[row * D + c] = __float2half_rn(a * inv * (w ? w[c] : 1.f));
   }
+}
+
+// The normalisation half of ADD_NORM when the residual add ran in the matmul's epilogue (the
+// tcgen05 GEMM's residual mode): x already holds x + y, and ssp[g * ldss + row] the sum of squares of
+// row's columns [32 g, 32 g + 32), g < D / 32. One CTA per row sums the groups (in a fixed order: the
+// result does not depend on the GEMM's tile split beyond the per-group sums) and writes
+// h = f16(x * rsqrt(sum / D + eps) * w). Algorithmic bytes per row: 4D read of x, 2D write of h.
+__global__ void __launch_bounds__(256) rmsnorm_from_sums_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ ssp, int64_t ldss,
+                                                                const float* __restrict__ w, int D, float eps,
+                                                                __half* __restrict__ h) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  float s = 0.f;
+  for (int g = threadIdx.x; g < D / 32; g += 256) s += ssp[g * ldss + row];
+  const float inv = rsqrtf(block_sum_256(s, red) / (float)D + eps);
+  const float4* xr = reinterpret_cast<const float4*>(x + row * D);
+  for (int c4 = threadIdx.x; c4 < D / 4; c4 += 256) {
+    const float4 v = xr[c4];
+    const float4 g = w ? reinterpret_cast<const float4*>(w)[c4] : make_float4(1.f, 1.f, 1.f, 1.f);
+    const __half2 lo = __floats2half2_rn(v.x * inv * g.x, v.y * inv * g.y);
+    const __half2 hi = __floats2half2_rn(v.z * inv * g.z, v.w * inv * g.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&lo);
+    o.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(h + row * D + 4 * c4) = o;
+  }
+}
+
+// D % 32 == 0; x and w 16-byte aligned, h 8-byte aligned (checked by the caller)
+cudaError_t launch_rmsnorm_from_sums(const float* x, const float* ssp, int64_t ldss, const float* w, int M, int D,
+                                     float eps, __half* h, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, rmsnorm_from_sums_kernel, x, ssp, ldss, w, D, eps, h);
 }
 
 cudaError_t launch_add_rmsnorm(float* x, const __half* y, const float* w, int M, int D, float eps, __half* h,

@@ -45,7 +45,10 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
                               __half* const* ydst,
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
-                              cudaStream_t stream, bool pdl, bool ticket_fixup, int glu);
+                              cudaStream_t stream, bool pdl, bool ticket_fixup, int glu, float* resid,
+                              int64_t ldr, float* ssp, int64_t ldss);
+cudaError_t launch_rmsnorm_from_sums(const float* x, const float* ssp, int64_t ldss, const float* w, int M, int D,
+                                     float eps, __half* h, cudaStream_t stream, bool pdl);
 int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y, const int* M,
                  const int* dep, s4_chain** out, const char** why);
 cudaError_t chain_launch(s4_chain* c, uint32_t* err, cudaStream_t stream, bool cooperative);
@@ -62,6 +65,8 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const uint8_t* 
 namespace {
 
 constexpr int kMaxTickets = 1 << 16;  // n-blocks per weight: N <= 8,388,608
+// s4_matmul_add_rmsnorm's sums of squares: (N / 32) x rows per launch (16384 rows at N = 2048)
+constexpr size_t kNormSums = 1u << 20;
 constexpr int kGemvMaxM = 16;  // tokens one GEMV launch covers (two 8-token mma column groups)
 
 thread_local std::string g_last_error;
@@ -369,6 +374,7 @@ int s4_init(int device, s4_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&ctx->partials, part_bytes);
   if (e == cudaSuccess) e = cudaMalloc(&ctx->tickets, kMaxTickets * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->err, sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->norm_ss, kNormSums * sizeof(float));
   if (e == cudaSuccess) e = cudaMemsetAsync(ctx->tickets, 0, kMaxTickets * sizeof(uint32_t), ctx->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(ctx->err, 0, sizeof(uint32_t), ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
@@ -388,6 +394,7 @@ int s4_destroy(s4_ctx* ctx) {
   cudaFree(ctx->partials);
   cudaFree(ctx->tickets);
   cudaFree(ctx->err);
+  cudaFree(ctx->norm_ss);
   cudaFree(ctx->dx);
   cudaFree(ctx->dy);
   cudaFree(ctx->wire_pow);
@@ -1036,6 +1043,54 @@ int s4_add_rmsnorm(s4_ctx* ctx, float* x, const void* y, const float* w, int M, 
   return S4_OK;
 }
 
+int s4_matmul_add_rmsnorm(s4_ctx* ctx, const s4_weight* w, const void* x, int M, float* resid, const float* norm_w,
+                          float eps, void* h, void* stream) {
+  if (!ctx || !w) return fail(S4_ERR_INVALID, "NULL context or weight");
+  if (w->ctx != ctx) return fail(S4_ERR_INVALID, "weight belongs to another context");
+  if (M < 0) return fail(S4_ERR_INVALID, "M must be >= 0 (got %d)", M);
+  if (M == 0) return S4_OK;
+  if (!x || !resid || !h) return fail(S4_ERR_INVALID, "NULL x, residual or h");
+  if (w->glu) return fail(S4_ERR_UNSUPPORTED, "a fused gate|up weight has no residual epilogue");
+  const auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
+  if (misaligned(x) || misaligned(resid) || misaligned(h) || (norm_w && misaligned(norm_w)))
+    return fail(S4_ERR_INVALID, "x, residual, norm weight and h must be 16-byte aligned");
+  DeviceGuard guard(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int N = w->N;
+  const Bucket b = choose(ctx, M, N, w->K);
+  if (b.family == S4_FAMILY_TC && N % 32 == 0) {
+    // the residual add and the per-32-column sums of squares in the GEMM epilogue, then one row pass
+    int tn = 0, grid = 0;
+    bool cta = false;
+    const int rc = tc_launch_shape(ctx, w, b, M, &tn, &grid, &cta);
+    if (rc != S4_OK) return rc;
+    const long long rows_cap = std::min<long long>((long long)(kMaxTickets / w->nblk) * tn,
+                                                   (long long)(kNormSums / (size_t)(N / 32)));
+    for (long long r0 = 0; r0 < M; r0 += rows_cap) {
+      const int rows = (int)std::min<long long>(rows_cap, M - r0);
+      __half* hr = static_cast<__half*>(h) + r0 * N;
+      float* xr = resid + r0 * N;
+      cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, w->wb, static_cast<const __half*>(x) + r0 * w->K, w->K, &hr,
+                                            1, N, 0, ctx->partials, ctx->tickets, kMaxTickets, ctx->err, rows, N, w->K,
+                                            w->nblk, w->ktiles, tn, grid, st, ctx->pdl, false, 0, xr, N, ctx->norm_ss,
+                                            rows);
+      if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch (residual epilogue)");
+      e = s4::launch_rmsnorm_from_sums(xr, ctx->norm_ss, rows, norm_w, rows, N, eps, hr, st, ctx->pdl);
+      if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+      ctx->launches += 2;
+    }
+    return S4_OK;
+  }
+  // other families: y into h, then ADD_NORM over it in place
+  int rc = s4_matmul(ctx, w, x, M, h, stream);
+  if (rc != S4_OK) return rc;
+  cudaError_t e = s4::launch_add_rmsnorm(resid, static_cast<const __half*>(h), norm_w, M, N, eps,
+                                         static_cast<__half*>(h), st);
+  if (e != cudaSuccess) return cuda_fail(e, "add_rmsnorm launch");
+  ++ctx->launches;
+  return S4_OK;
+}
+
 int s4_buffer_alloc(s4_ctx* ctx, size_t bytes, void** ptr) {
   if (!ctx || !ptr || bytes == 0) return fail(S4_ERR_INVALID, "bad argument");
   DeviceGuard guard(ctx->device);
@@ -1106,7 +1161,8 @@ int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, in
   cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, w->wb, static_cast<const __half*>(x), ldx,
                                         reinterpret_cast<__half* const*>(dst), ndst, ldy, col0, ctx->partials,
                                         ctx->tickets, kMaxTickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tn,
-                                        grid, static_cast<cudaStream_t>(stream), ctx->pdl, cta, w->glu);
+                                        grid, static_cast<cudaStream_t>(stream), ctx->pdl, cta, w->glu, nullptr, 0,
+                                        nullptr, 0);
   if (e != cudaSuccess) return cuda_fail(e, "gathered tc gemm launch");
   ++ctx->launches;
   return S4_OK;

@@ -65,6 +65,7 @@ _SIGS = {
     "s4_noalloc_check_errors": (C.c_int, [C.c_int, C.POINTER(C.c_uint32), C.c_int]),
     "s4_silu_mul": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
     "s4_add_rmsnorm": (C.c_int, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_float, _P, _P]),
+    "s4_matmul_add_rmsnorm": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, C.c_float, _P, _P]),
     "s4_chain_create": (C.c_int, [_P, C.c_int, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(C.c_int),
                                   C.POINTER(C.c_int), C.POINTER(_P)]),
     "s4_chain_run": (C.c_int, [_P, _P, _P]),
@@ -503,6 +504,27 @@ class Context:
         _check(_lib.s4_add_rmsnorm(self.handle, x.data_ptr(), y.data_ptr() if y is not None else None,
                                    w.data_ptr() if w is not None else None, int(M), int(D), float(eps), h.data_ptr(),
                                    _stream_handle(stream)))
+        return h
+
+    def matmul_add_rmsnorm(self, x, W: Weight, resid, w=None, eps: float = 1e-6, h=None, stream=None):
+        """A projection followed by ADD_NORM in one call: ``resid += f16(x @ W^T)`` (fp32, in
+        place) and ``h = f16(resid * rsqrt(mean(resid^2) + eps) * w)`` (w None = ones); y itself is
+        not stored. Returns h."""
+        import torch
+        M = x.shape[0]
+        _dev_f16("x", x, self.device, M, W.K)
+        if (resid.dtype != torch.float32 or not resid.is_contiguous() or tuple(resid.shape) != (M, W.N)
+                or resid.device != torch.device("cuda", self.device)):
+            raise S4Error(ERR_INVALID, f"matmul_add_rmsnorm: resid must be a contiguous [{M}, {W.N}] fp32 "
+                                       f"tensor on cuda:{self.device}")
+        if w is not None and (w.dtype != torch.float32 or not w.is_contiguous() or w.numel() != W.N):
+            raise S4Error(ERR_INVALID, f"matmul_add_rmsnorm: w must be a contiguous fp32 tensor of {W.N} values")
+        if h is None:
+            h = torch.empty((M, W.N), dtype=torch.float16, device=x.device)
+        _dev_f16("h", h, self.device, M, W.N)
+        _check(_lib.s4_matmul_add_rmsnorm(self.handle, W.handle, x.data_ptr(), int(M), resid.data_ptr(),
+                                          w.data_ptr() if w is not None else None, float(eps), h.data_ptr(),
+                                          _stream_handle(stream)))
         return h
 
     # -- column-sharded prefill over peer memory --------------------------------------------------

@@ -128,6 +128,9 @@ class Ops:
     add_norm: object    # (x f32 [M, D], y f16 or None) -> (x + y f32, rmsnorm(x + y) f16)
     cols: object        # (x, c0, c1) -> contiguous x[:, c0:c1]
     to_f32: object      # x f16 -> fp32 residual stream (a new tensor)
+    # (act f16, weight, x f32) -> (x + act @ W^T, rmsnorm of it f16) as one call, the add in the
+    # projection's epilogue; None: matmul, then add_norm. Used on one GPU (no gather in between).
+    matmul_add_norm: object = None
 
 
 def stack_forward(x, layers, ops: Ops, world: int = 1, timers=None):
@@ -146,18 +149,21 @@ def stack_forward(x, layers, ops: Ops, world: int = 1, timers=None):
         g = timers("gather", lambda: ops.all_gather(local)) if timers else ops.all_gather(local)
         return gathered_to_rows(g, M, world, ns)
 
+    def proj_norm(act, wt, x):
+        """A projection whose output is added to the residual stream and normalised (ADD_NORM)."""
+        if ops.matmul_add_norm is not None and world == 1:
+            return ops.matmul_add_norm(act, wt, x)
+        return ops.add_norm(x, gather(ops.matmul(act, wt)))
+
     x = ops.to_f32(x)
-    y = None
+    x, h = ops.add_norm(x, None)                                    # layer 0's in_norm (engine.js:255)
     for w in layers:
-        x, h = ops.add_norm(x, y)                                   # in_norm (engine.js:255)
         a = gather(ops.matmul(h, w["in_proj"]))
-        y = gather(ops.matmul(ops.cols(a, 0, HIDDEN), w["out_proj"]))
-        x, h = ops.add_norm(x, y)                                   # post_norm (engine.js:277)
+        x, h = proj_norm(ops.cols(a, 0, HIDDEN), w["out_proj"], x)  # out_proj + post_norm (engine.js:277)
         gu = ops.matmul(h, w["gate_up"])
         mid = gather(gu if ops.silu_mul is None else ops.silu_mul(gu, gu.shape[1] // 2))
-        y = gather(ops.matmul(mid, w["down"]))
-    x, h = ops.add_norm(x, y)                                       # final norm (engine.js:284)
-    return h
+        x, h = proj_norm(mid, w["down"], x)                         # down + the next in_norm / final norm
+    return h                                                        # (engine.js:255, 284)
 
 
 # --------------------------------------------------------------------------------------------------
@@ -189,13 +195,19 @@ def projection_seed(layer: int, name: str) -> int:
 class CudaStack:
     """The stack's weights uploaded through the C ABI, optionally as this rank's column shard.
     With ``fuse_silu`` (default) every gate|up projection is uploaded as a fused weight whose matmul
-    writes SiLU*mul directly (``s4_weight_upload_glu``), so no separate SiLU*mul pass runs."""
+    writes SiLU*mul directly (``s4_weight_upload_glu``), so no separate SiLU*mul pass runs. With
+    ``fuse_norm`` out_proj and down add their output to the residual stream in the GEMM epilogue and
+    normalise in one row pass (``s4_matmul_add_rmsnorm``) on one GPU. It is off by default: at the
+    stack's 2048-token shapes every CTA holds one tile, so the epilogue's fp32 residual traffic
+    cannot hide behind a next tile's MMAs, and the one-call form measured 3-5 us slower per
+    projection than the GEMM followed by the separate ADD_NORM kernel."""
 
     def __init__(self, ctx, n_layers: int = N_LAYERS, rank: int = 0, world: int = 1, device=None, host_gen=False,
-                 fuse_silu: bool = True):
+                 fuse_silu: bool = True, fuse_norm: bool = False):
         import torch
         self.ctx, self.rank, self.world = ctx, rank, world
         self.fuse_silu = fuse_silu
+        self.fuse_norm = fuse_norm
         self.device = device or torch.device("cuda", ctx.device)
         self.layers = []
         self.n_layers = n_layers
@@ -231,12 +243,16 @@ class CudaStack:
         def add_norm(x, y):
             return x, ctx.add_rmsnorm(x, y)
 
+        def matmul_add_norm(act, w, x):
+            return x, ctx.matmul_add_rmsnorm(act, w, x)
+
         return Ops(matmul=lambda x, w: ctx.matmul(x, w),
                    silu_mul=None if self.fuse_silu else (lambda big, I: ctx.silu_mul(big, I)),
                    all_gather=all_gather,
                    add_norm=add_norm,
                    cols=lambda x, c0, c1: x[:, c0:c1].contiguous(),
-                   to_f32=lambda x: x.float())
+                   to_f32=lambda x: x.float(),
+                   matmul_add_norm=matmul_add_norm if self.fuse_norm else None)
 
     def forward(self, x, group=None, timers=None):
         return stack_forward(x, self.layers, self.ops(group), self.world, timers)
@@ -269,7 +285,8 @@ class FusedColshardStack:
         import torch.distributed as dist
         self.ctx, self.group, self.rank, self.world = ctx, group, rank, world
         self.device = torch.device("cuda", ctx.device)
-        self.stack = CudaStack(ctx, n_layers, rank, world, self.device, fuse_silu=fuse_silu)
+        # its forward runs the norms itself (replicated, after each gather)
+        self.stack = CudaStack(ctx, n_layers, rank, world, self.device, fuse_silu=fuse_silu, fuse_norm=False)
         self.max_tokens = max_tokens
         self.widths = {"a": N_LINEAR_IN, "b": HIDDEN, "mid": INTER, "d": HIDDEN}
         sizes = {k: max_tokens * w * 2 for k, w in self.widths.items()}

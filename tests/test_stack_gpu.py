@@ -43,8 +43,9 @@ def _cpu_ops(serve):
 
 
 @pytest.mark.parametrize("M", [8, 64, 300])
-def test_stack_two_layers_matches_oracle(ctx, serve, M):
-    stack = serve.CudaStack(ctx, n_layers=4, host_gen=True)  # layers 0-3: linear, linear, linear, attn
+@pytest.mark.parametrize("fuse_norm", [False, True])
+def test_stack_two_layers_matches_oracle(ctx, serve, M, fuse_norm):
+    stack = serve.CudaStack(ctx, n_layers=4, host_gen=True, fuse_norm=fuse_norm)  # layers: L L L A
     stack.layers = [stack.layers[0], stack.layers[3]]
     x = s4ref.config_x(np.random.default_rng(M), M, serve.HIDDEN)
     y = stack.forward(torch.from_numpy(x).cuda())
@@ -93,6 +94,70 @@ def test_add_rmsnorm_matches_oracle(ctx, M, D, with_y, with_w):
     np.testing.assert_array_equal(xd.cpu().numpy(), xr)          # fp32 add: one rounding, bit-exact
     # the fp32 sum of squares differs only in summation order: at most one fp16 ulp on h
     np.testing.assert_allclose(h.cpu().numpy().astype(np.float32), hr.astype(np.float32), rtol=1e-3, atol=1e-3)
+
+
+# (K, N, M, norm weight, forced tcgen05 shape): out_proj / down shapes on the GEMV and tcgen05 paths,
+# split tiles (fix-up kernel) and whole tiles, a ragged last n-block (N % 128 == 32) and an N that is
+# not a multiple of 32 (matmul into h, then ADD_NORM in place)
+ADDNORM_CASES = [(2048, 2048, 1, False, None), (2048, 2048, 8, True, None), (2048, 2048, 64, True, None),
+                 (6144, 2048, 300, True, None), (6144, 2048, 2048, False, None),
+                 (2048, 2048, 300, True, ("tc", 64, 148)), (2048, 2048, 300, True, ("tc", 64, 80)),
+                 (512, 2080, 100, True, None), (512, 2056, 100, True, None)]
+
+
+@pytest.mark.parametrize("K,N,M,with_w,force", ADDNORM_CASES)
+def test_matmul_add_rmsnorm_matches_oracle(ctx, K, N, M, with_w, force):
+    """s4_matmul_add_rmsnorm against the oracle's matmul then ADD_NORM, and against the GPU's own
+    two-call form (s4_matmul, s4_add_rmsnorm): same fp16 y, so the residual agrees bit for bit."""
+    rng = np.random.default_rng(K + N + M)
+    packed, scales = s4ref.config_weights(rng, K, N)
+    x = s4ref.config_x(rng, M, K)
+    resid = (rng.standard_normal((M, N)) * 0.5).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32) if with_w else None
+    W = ctx.upload(packed, scales, N, K)
+    if force:
+        ctx.force(*force)
+    try:
+        xd = torch.from_numpy(x).cuda()
+        wd = None if w is None else torch.from_numpy(w).cuda()
+        r1 = torch.from_numpy(resid).cuda()
+        h1 = ctx.matmul_add_rmsnorm(xd, W, r1, wd)
+        r2 = torch.from_numpy(resid).cuda()
+        h2 = ctx.add_rmsnorm(r2, ctx.matmul(xd, W), wd)
+        torch.cuda.synchronize()
+        assert ctx.check_errors() == 0
+    finally:
+        ctx.force()
+        W.free()
+    y16, _ = s4ref.matmul(x, packed, scales)
+    xr, hr = s4ref.add_rmsnorm(resid, y16, w)
+    # the residual: y's fp16 rounding may differ by one ulp from the oracle's (fp32 sums in another order)
+    tol = 2e-3 * float(np.abs(y16.astype(np.float32)).max()) + 1e-6
+    np.testing.assert_allclose(r1.cpu().numpy(), xr, rtol=0, atol=tol)
+    ok, mr, mc = s4ref.check(h1.cpu().numpy(), hr.astype(np.float32))
+    assert ok, (mr, mc)
+    np.testing.assert_array_equal(r1.cpu().numpy(), r2.cpu().numpy())
+    # the sums of squares differ only in order: at most one fp16 ulp on h
+    np.testing.assert_allclose(h1.cpu().numpy().astype(np.float32), h2.cpu().numpy().astype(np.float32),
+                               rtol=1e-3, atol=1e-3)
+
+
+def test_matmul_add_rmsnorm_rejects_bad_arguments(ctx):
+    rng = np.random.default_rng(1)
+    packed, scales = s4ref.config_weights(rng, 256, 256)
+    W = ctx.upload(packed, scales, 256, 256)
+    G = ctx.upload_glu(packed, scales, 128, 256)
+    try:
+        x = torch.zeros((4, 256), dtype=torch.float16, device="cuda")
+        with pytest.raises(Exception):
+            ctx.matmul_add_rmsnorm(x, W, torch.zeros((4, 256), dtype=torch.float16, device="cuda"))
+        with pytest.raises(Exception):
+            ctx.matmul_add_rmsnorm(x, W, torch.zeros((4, 128), dtype=torch.float32, device="cuda"))
+        with pytest.raises(Exception):
+            ctx.matmul_add_rmsnorm(x, G, torch.zeros((4, 128), dtype=torch.float32, device="cuda"))
+    finally:
+        W.free()
+        G.free()
 
 
 def test_fused_stack_one_gpu_eager_graph_and_plain_agree(ctx, serve):
