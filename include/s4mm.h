@@ -289,6 +289,21 @@ S4_API int s4_silu_mul_gather(s4_ctx* ctx, const void* big, int M, int Is, void*
  * sets the context's error word (s4_check_errors) instead of hanging. Asynchronous on `stream`. */
 S4_API int s4_peer_barrier(s4_ctx* ctx, void* const* flags, int nranks, int rank, uint32_t epoch, void* stream);
 
+/* The barrier split in two, so its wait overlaps the next kernel's start. s4_peer_signal: once the
+ * work before it on `stream` has finished (its peer stores included), count the next epoch on the
+ * device (slot 8 of this rank's array, as s4_peer_barrier with epoch 0) and store it into every rank's
+ * array (flags as for s4_peer_barrier). The consumers of the gathered data then wait themselves:
+ * s4_matmul_gather_wait (its activation loads wait; the weight stream starts at once) and
+ * s4_add_rmsnorm_wait take this rank's own flag array and wait until all nranks ranks have signalled
+ * this rank's latest epoch. Every rank signals the same number of times. A wait past 1 s sets the
+ * context's error word. No counterpart in the reference (its engine runs on one GPU); it replaces the
+ * all-gather step of the column-sharded prefill. Asynchronous on `stream`. */
+S4_API int s4_peer_signal(s4_ctx* ctx, void* const* flags, int nranks, int rank, void* stream);
+S4_API int s4_matmul_gather_wait(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, int M, void* const* dst,
+                                 int ndst, int ldy, int col0, const void* own_flags, int nranks, void* stream);
+S4_API int s4_add_rmsnorm_wait(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps,
+                               void* h, const void* own_flags, int nranks, void* stream);
+
 /* Dispatcher. s4_plan reports the (family, tile, split) s4_matmul will use for M on an
  * (N, K) weight (for the tcgen05 family with N and K given: the tokens per tile and CTAs it launches;
  * otherwise the bucket's values, 0 = kernel default); replaces matmulKernel(M) (engine.js:17-33).

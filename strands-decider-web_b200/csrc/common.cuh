@@ -231,4 +231,28 @@ __device__ __forceinline__ void set_error(uint32_t* err, uint32_t bits) {
   if (err) atomicOr(err, bits);
 }
 
+// Cross-GPU flag arrays of the column-sharded prefill (peer.cu): slot q of a rank's own array holds
+// the latest epoch rank q has signalled to it; slot kPeerCounterSlot counts the rank's own signals.
+constexpr int kPeerCounterSlot = 8;
+
+// Called by one thread of a consumer kernel after its grid-dependency wait: waits until every one
+// of the nranks ranks has signalled at least this rank's latest epoch (the kernel before it in the
+// stream was this rank's signal, so its counter slot is visible). Acquire at system scope: the
+// peers' stores before their signals are then visible to this thread and, after a block barrier, to
+// its CTA. Bounded: false after kWaitTimeoutNs.
+__device__ __forceinline__ bool peer_wait_all(const uint32_t* own, int nranks) {
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(own + kPeerCounterSlot);
+  const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
+  for (int q = 0; q < nranks; ++q) {
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + q) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if (globaltimer_ns() > deadline) return false;
+      __nanosleep(32);
+    }
+  }
+  return true;
+}
+
 }  // namespace s4

@@ -111,6 +111,10 @@ struct TcParams {
   int64_t ldr;
   float* ssp;
   int64_t ldss;
+  // Column-sharded prefill: the activations were gathered from wait_n ranks; the activation producer
+  // waits for every rank's signal (peer_wait_all on this rank's flag array) before its first load.
+  const uint32_t* wait_flags;
+  int wait_n;
 };
 
 // Output stores. Each destination is the local buffer or, for the column-sharded prefill, a peer's
@@ -343,6 +347,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     // ------------- activation tiles: producer (TMA) -------------
     if (lane == 0) {
       pdl_wait();  // x is written by the previous kernel in the stream
+      if (p.wait_flags) {
+        // and by the peers: their generic stores, then this warp's TMA (async proxy) loads
+        if (!peer_wait_all(p.wait_flags, p.wait_n)) set_error(p.err, kErrWaitTimeout);
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
       int issued = 0;
       bool ok = true;
       const uint32_t xbytes = (uint32_t)p.tn * 128u;
@@ -841,7 +850,7 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
                               cudaStream_t stream, bool pdl, bool ticket_fixup, int glu, float* resid,
-                              int64_t ldr, float* ssp, int64_t ldss) {
+                              int64_t ldr, float* ssp, int64_t ldss, const uint32_t* wait_flags, int wait_n) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   int tn = tile_n > 0 ? tile_n : (M >= kTcMaxTn ? kTcMaxTn : ((M + 15) / 16) * 16);
@@ -859,6 +868,9 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
   p.vec = (ldy % 8 == 0 && ycol0 % 8 == 0) ? 1 : 0;
   for (int d = 0; d < ndst; ++d)
     if (reinterpret_cast<uintptr_t>(ydst[d]) & 15) p.vec = 0;
+  if (wait_flags && (wait_n < 1 || wait_n > 8)) return cudaErrorInvalidValue;
+  p.wait_flags = wait_flags;
+  p.wait_n = wait_n;
   p.resid = resid;
   p.ldr = ldr;
   p.ssp = ssp;
@@ -955,7 +967,8 @@ cudaError_t launch_tc_gemm(const uint8_t* wq, const uint8_t* ws, const uint8_t* 
                            bool ticket_fixup, int glu) {
   __half* dst[1] = {y};
   return launch_tc_gemm_ex(wq, ws, wb, x, K, dst, 1, glu ? N / 2 : N, 0, partials, tickets, max_tickets, err, M, N, K,
-                           nblk, ktiles, tile_n, grid, stream, pdl, ticket_fixup, glu, nullptr, 0, nullptr, 0);
+                           nblk, ktiles, tile_n, grid, stream, pdl, ticket_fixup, glu, nullptr, 0, nullptr, 0,
+                           nullptr, 0);
 }
 
 }  // namespace s4

@@ -23,14 +23,24 @@ __device__ __forceinline__ float block_sum_256(float v, float* red) {
 // loads and stores, 8-byte y loads and h stores), so x is read once.
 constexpr int kNormMaxNV = 8;
 
-template <int NV>
+// wait_flags: y was gathered from wait_n ranks (column-sharded prefill): thread 0 waits for every
+// rank's signal before the CTA reads y (a timeout sets err and the row is computed from what is there).
+__device__ __forceinline__ void norm_peer_wait(const uint32_t* wait_flags, int wait_n, uint32_t* err) {
+  if (!wait_flags) return;
+  if (threadIdx.x == 0 && !peer_wait_all(wait_flags, wait_n)) set_error(err, kErrWaitTimeout);
+  __syncthreads();
+}
+
 // y and h may be the same buffer (the projection's output normalised in place): every thread reads
 // its elements of y before the block reduction and writes the same elements of h after it.
+template <int NV>
 __global__ void __launch_bounds__(256) add_rmsnorm_reg_kernel(float* __restrict__ x, const __half* y,
                                                               const float* __restrict__ w, int D, float eps,
-                                                              __half* h) {
+                                                              __half* h, const uint32_t* wait_flags, int wait_n,
+                                                              uint32_t* err) {
   pdl_wait();
   pdl_launch_dependents();
+  norm_peer_wait(wait_flags, wait_n, err);
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   float4* xr = reinterpret_cast<float4*>(x + row * D);
@@ -67,9 +77,11 @@ __global__ void __launch_bounds__(256) add_rmsnorm_reg_kernel(float* __restrict_
 }
 
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x, const __half* y,
-                                                          const float* __restrict__ w, int D, float eps, __half* h) {
+                                                          const float* __restrict__ w, int D, float eps, __half* h,
+                                                          const uint32_t* wait_flags, int wait_n, uint32_t* err) {
   pdl_wait();
   pdl_launch_dependents();
+  norm_peer_wait(wait_flags, wait_n, err);
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   float* xr = x + row * D;
@@ -135,7 +147,8 @@ cudaError_t launch_rmsnorm_from_sums(const float* x, const float* ssp, int64_t l
 }
 
 cudaError_t launch_add_rmsnorm(float* x, const __half* y, const float* w, int M, int D, float eps, __half* h,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, const uint32_t* wait_flags, int wait_n, uint32_t* err) {
+  if (wait_flags && (wait_n < 1 || wait_n > 8)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M, 1, 1);
   cfg.blockDim = dim3(256, 1, 1);
@@ -149,17 +162,17 @@ cudaError_t launch_add_rmsnorm(float* x, const __half* y, const float* w, int M,
   const int nv = D / 1024;
   if (D % 1024 == 0 && nv <= kNormMaxNV && aligned(x, 16) && aligned(y, 8) && aligned(w, 16) && aligned(h, 8)) {
     switch (nv) {
-      case 1: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<1>, x, y, w, D, eps, h);
-      case 2: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<2>, x, y, w, D, eps, h);
-      case 3: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<3>, x, y, w, D, eps, h);
-      case 4: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<4>, x, y, w, D, eps, h);
-      case 5: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<5>, x, y, w, D, eps, h);
-      case 6: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<6>, x, y, w, D, eps, h);
-      case 7: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<7>, x, y, w, D, eps, h);
-      default: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<8>, x, y, w, D, eps, h);
+      case 1: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<1>, x, y, w, D, eps, h, wait_flags, wait_n, err);
+      case 2: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<2>, x, y, w, D, eps, h, wait_flags, wait_n, err);
+      case 3: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<3>, x, y, w, D, eps, h, wait_flags, wait_n, err);
+      case 4: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<4>, x, y, w, D, eps, h, wait_flags, wait_n, err);
+      case 5: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<5>, x, y, w, D, eps, h, wait_flags, wait_n, err);
+      case 6: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<6>, x, y, w, D, eps, h, wait_flags, wait_n, err);
+      case 7: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<7>, x, y, w, D, eps, h, wait_flags, wait_n, err);
+      default: return cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<8>, x, y, w, D, eps, h, wait_flags, wait_n, err);
     }
   }
-  return cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, x, y, w, D, eps, h);
+  return cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, x, y, w, D, eps, h, wait_flags, wait_n, err);
 }
 
 }  // namespace s4

@@ -38,7 +38,8 @@ cudaError_t launch_transcode(const uint32_t* q, const __half* scales, const __ha
                              cudaStream_t stream);
 cudaError_t launch_fwht(__half* a, int64_t blocks, int n, cudaStream_t stream);
 cudaError_t launch_add_rmsnorm(float* x, const __half* y, const float* w, int M, int D, float eps, __half* h,
-                               cudaStream_t stream);
+                               cudaStream_t stream, const uint32_t* wait_flags, int wait_n, uint32_t* err);
+cudaError_t launch_peer_signal(uint32_t* const* flags, int nranks, int rank, cudaStream_t stream, bool pdl);
 cudaError_t launch_peer_barrier(uint32_t* const* flags, int nranks, int rank, uint32_t epoch, uint32_t* err,
                                 cudaStream_t stream);
 cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, int64_t ldx,
@@ -46,7 +47,7 @@ cudaError_t launch_tc_gemm_ex(const uint8_t* wq, const uint8_t* ws, const uint8_
                               int ndst, int64_t ldy, int ycol0, float* partials, uint32_t* tickets, int max_tickets,
                               uint32_t* err, int M, int N, int K, int nblk, int ktiles, int tile_n, int grid,
                               cudaStream_t stream, bool pdl, bool ticket_fixup, int glu, float* resid,
-                              int64_t ldr, float* ssp, int64_t ldss);
+                              int64_t ldr, float* ssp, int64_t ldss, const uint32_t* wait_flags, int wait_n);
 cudaError_t launch_rmsnorm_from_sums(const float* x, const float* ssp, int64_t ldss, const float* w, int M, int D,
                                      float eps, __half* h, cudaStream_t stream, bool pdl);
 int chain_create(s4_ctx* ctx, int nops, const s4_weight* const* w, const void* const* x, void* const* y, const int* M,
@@ -1030,17 +1031,30 @@ int s4_chain_free(s4_chain* chain) {
   return S4_OK;
 }
 
-int s4_add_rmsnorm(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps, void* h,
-                   void* stream) {
+static int add_rmsnorm_impl(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps, void* h,
+                            const void* own_flags, int nranks, void* stream) {
   if (!ctx || !x || !h) return fail(S4_ERR_INVALID, "NULL argument");
   if (M < 0 || D < 1) return fail(S4_ERR_INVALID, "bad shape M=%d D=%d", M, D);
+  if (own_flags && (nranks < 1 || nranks > 8)) return fail(S4_ERR_INVALID, "nranks must be in [1, 8]");
   if (M == 0) return S4_OK;
   DeviceGuard guard(ctx->device);
   cudaError_t e = s4::launch_add_rmsnorm(x, static_cast<const __half*>(y), w, M, D, eps, static_cast<__half*>(h),
-                                         static_cast<cudaStream_t>(stream));
+                                         static_cast<cudaStream_t>(stream), static_cast<const uint32_t*>(own_flags),
+                                         nranks, ctx->err);
   if (e != cudaSuccess) return cuda_fail(e, "add_rmsnorm launch");
   ++ctx->launches;
   return S4_OK;
+}
+
+int s4_add_rmsnorm(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps, void* h,
+                   void* stream) {
+  return add_rmsnorm_impl(ctx, x, y, w, M, D, eps, h, nullptr, 0, stream);
+}
+
+int s4_add_rmsnorm_wait(s4_ctx* ctx, float* x, const void* y, const float* w, int M, int D, float eps, void* h,
+                        const void* own_flags, int nranks, void* stream) {
+  if (!own_flags) return fail(S4_ERR_INVALID, "NULL flag array");
+  return add_rmsnorm_impl(ctx, x, y, w, M, D, eps, h, own_flags, nranks, stream);
 }
 
 int s4_matmul_add_rmsnorm(s4_ctx* ctx, const s4_weight* w, const void* x, int M, float* resid, const float* norm_w,
@@ -1073,7 +1087,7 @@ int s4_matmul_add_rmsnorm(s4_ctx* ctx, const s4_weight* w, const void* x, int M,
       cudaError_t e = s4::launch_tc_gemm_ex(w->wq, w->ws, w->wb, static_cast<const __half*>(x) + r0 * w->K, w->K, &hr,
                                             1, N, 0, ctx->partials, ctx->tickets, kMaxTickets, ctx->err, rows, N, w->K,
                                             w->nblk, w->ktiles, tn, grid, st, ctx->pdl, false, 0, xr, N, ctx->norm_ss,
-                                            rows);
+                                            rows, nullptr, 0);
       if (e != cudaSuccess) return cuda_fail(e, "tc gemm launch (residual epilogue)");
       e = s4::launch_rmsnorm_from_sums(xr, ctx->norm_ss, rows, norm_w, rows, N, eps, hr, st, ctx->pdl);
       if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
@@ -1085,7 +1099,7 @@ int s4_matmul_add_rmsnorm(s4_ctx* ctx, const s4_weight* w, const void* x, int M,
   int rc = s4_matmul(ctx, w, x, M, h, stream);
   if (rc != S4_OK) return rc;
   cudaError_t e = s4::launch_add_rmsnorm(resid, static_cast<const __half*>(h), norm_w, M, N, eps,
-                                         static_cast<__half*>(h), st);
+                                         static_cast<__half*>(h), st, nullptr, 0, nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "add_rmsnorm launch");
   ++ctx->launches;
   return S4_OK;
@@ -1138,9 +1152,10 @@ int s4_ipc_close(s4_ctx* ctx, void* ptr) {
   return S4_OK;
 }
 
-int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, int M, void* const* dst, int ndst,
-                     int ldy, int col0, void* stream) {
+static int matmul_gather_impl(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, int M, void* const* dst,
+                              int ndst, int ldy, int col0, const void* own_flags, int nranks, void* stream) {
   if (!ctx || !w || !dst) return fail(S4_ERR_INVALID, "NULL argument");
+  if (own_flags && (nranks < 1 || nranks > 8)) return fail(S4_ERR_INVALID, "nranks must be in [1, 8]");
   if (w->ctx != ctx) return fail(S4_ERR_INVALID, "weight belongs to another context");
   if (M < 0 || ndst < 1 || ndst > 8) return fail(S4_ERR_INVALID, "bad M or ndst");
   if (M == 0) return S4_OK;
@@ -1162,10 +1177,21 @@ int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, in
                                         reinterpret_cast<__half* const*>(dst), ndst, ldy, col0, ctx->partials,
                                         ctx->tickets, kMaxTickets, ctx->err, M, w->N, w->K, w->nblk, w->ktiles, tn,
                                         grid, static_cast<cudaStream_t>(stream), ctx->pdl, cta, w->glu, nullptr, 0,
-                                        nullptr, 0);
+                                        nullptr, 0, static_cast<const uint32_t*>(own_flags), nranks);
   if (e != cudaSuccess) return cuda_fail(e, "gathered tc gemm launch");
   ++ctx->launches;
   return S4_OK;
+}
+
+int s4_matmul_gather(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, int M, void* const* dst, int ndst,
+                     int ldy, int col0, void* stream) {
+  return matmul_gather_impl(ctx, w, x, ldx, M, dst, ndst, ldy, col0, nullptr, 0, stream);
+}
+
+int s4_matmul_gather_wait(s4_ctx* ctx, const s4_weight* w, const void* x, int ldx, int M, void* const* dst,
+                          int ndst, int ldy, int col0, const void* own_flags, int nranks, void* stream) {
+  if (!own_flags) return fail(S4_ERR_INVALID, "NULL flag array");
+  return matmul_gather_impl(ctx, w, x, ldx, M, dst, ndst, ldy, col0, own_flags, nranks, stream);
 }
 
 int s4_silu_mul_gather(s4_ctx* ctx, const void* big, int M, int Is, void* const* dst, int ndst, int ldd, int col0,
@@ -1189,6 +1215,19 @@ int s4_peer_barrier(s4_ctx* ctx, void* const* flags, int nranks, int rank, uint3
   cudaError_t e = s4::launch_peer_barrier(reinterpret_cast<uint32_t* const*>(flags), nranks, rank, epoch, ctx->err,
                                           static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "peer barrier launch");
+  ++ctx->launches;
+  return S4_OK;
+}
+
+int s4_peer_signal(s4_ctx* ctx, void* const* flags, int nranks, int rank, void* stream) {
+  if (!ctx || !flags) return fail(S4_ERR_INVALID, "NULL argument");
+  if (nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks) return fail(S4_ERR_INVALID, "bad rank / nranks");
+  for (int q = 0; q < nranks; ++q)
+    if (!flags[q]) return fail(S4_ERR_INVALID, "NULL flag array of rank %d", q);
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = s4::launch_peer_signal(reinterpret_cast<uint32_t* const*>(flags), nranks, rank,
+                                         static_cast<cudaStream_t>(stream), ctx->pdl);
+  if (e != cudaSuccess) return cuda_fail(e, "peer signal launch");
   ++ctx->launches;
   return S4_OK;
 }

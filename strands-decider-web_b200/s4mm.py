@@ -80,6 +80,10 @@ _SIGS = {
     "s4_matmul_gather": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.POINTER(_P), C.c_int, C.c_int, C.c_int, _P]),
     "s4_silu_mul_gather": (C.c_int, [_P, _P, C.c_int, C.c_int, C.POINTER(_P), C.c_int, C.c_int, C.c_int, _P]),
     "s4_peer_barrier": (C.c_int, [_P, C.POINTER(_P), C.c_int, C.c_int, C.c_uint32, _P]),
+    "s4_peer_signal": (C.c_int, [_P, C.POINTER(_P), C.c_int, C.c_int, _P]),
+    "s4_matmul_gather_wait": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, C.POINTER(_P), C.c_int, C.c_int, C.c_int,
+                                        _P, C.c_int, _P]),
+    "s4_add_rmsnorm_wait": (C.c_int, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_float, _P, _P, C.c_int, _P]),
     "s4_plan": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int),
                           C.POINTER(C.c_int)]),
     "s4_force": (C.c_int, [_P, C.c_int, C.c_int, C.c_int]),
@@ -490,9 +494,12 @@ class Context:
         _check(_lib.s4_silu_mul(self.handle, big.data_ptr(), int(M), int(I), mid.data_ptr(), _stream_handle(stream)))
         return mid
 
-    def add_rmsnorm(self, x, y=None, w=None, eps: float = 1e-6, h=None, stream=None):
+    def add_rmsnorm(self, x, y=None, w=None, eps: float = 1e-6, h=None, stream=None, wait_flags=None,
+                    nranks: int = 0):
         """``x += y`` (fp32 residual, in place; skipped when y is None), then
-        ``h = f16(x * rsqrt(mean(x^2) + eps) * w)`` (w None = ones). Returns h."""
+        ``h = f16(x * rsqrt(mean(x^2) + eps) * w)`` (w None = ones). Returns h. With ``wait_flags``
+        (this rank's flag array) the kernel first waits for all ``nranks`` ranks' latest signal
+        (``s4_add_rmsnorm_wait``)."""
         import torch
         M, D = x.shape
         if x.dtype != torch.float32 or not x.is_contiguous():
@@ -501,6 +508,11 @@ class Context:
             raise S4Error(1, "add_rmsnorm: y must be a contiguous fp16 tensor shaped like x")
         if h is None:
             h = torch.empty((M, D), dtype=torch.float16, device=x.device)
+        if wait_flags is not None:
+            _check(_lib.s4_add_rmsnorm_wait(self.handle, x.data_ptr(), y.data_ptr() if y is not None else None,
+                                            w.data_ptr() if w is not None else None, int(M), int(D), float(eps),
+                                            h.data_ptr(), wait_flags, int(nranks), _stream_handle(stream)))
+            return h
         _check(_lib.s4_add_rmsnorm(self.handle, x.data_ptr(), y.data_ptr() if y is not None else None,
                                    w.data_ptr() if w is not None else None, int(M), int(D), float(eps), h.data_ptr(),
                                    _stream_handle(stream)))
@@ -554,8 +566,15 @@ class Context:
     def _ptr_array(ptrs):
         return (_P * len(ptrs))(*[_P(int(p)) for p in ptrs])
 
-    def matmul_gather(self, x_ptr: int, ldx: int, M: int, W: Weight, dst_ptrs, ldy: int, col0: int, stream=None):
+    def matmul_gather(self, x_ptr: int, ldx: int, M: int, W: Weight, dst_ptrs, ldy: int, col0: int, stream=None,
+                      wait_flags=None, nranks: int = 0):
+        """``s4_matmul_gather``; with ``wait_flags`` (this rank's flag array) the activation loads first
+        wait for all ``nranks`` ranks' latest signal (``s4_matmul_gather_wait``)."""
         arr = self._ptr_array(dst_ptrs)
+        if wait_flags is not None:
+            _check(_lib.s4_matmul_gather_wait(self.handle, W.handle, x_ptr, int(ldx), int(M), arr, len(dst_ptrs),
+                                              int(ldy), int(col0), wait_flags, int(nranks), _stream_handle(stream)))
+            return
         _check(_lib.s4_matmul_gather(self.handle, W.handle, x_ptr, int(ldx), int(M), arr, len(dst_ptrs), int(ldy),
                                      int(col0), _stream_handle(stream)))
 
@@ -563,6 +582,10 @@ class Context:
         arr = self._ptr_array(dst_ptrs)
         _check(_lib.s4_silu_mul_gather(self.handle, big.data_ptr(), int(big.shape[0]), int(Is), arr, len(dst_ptrs),
                                        int(ldd), int(col0), _stream_handle(stream)))
+
+    def peer_signal(self, flag_ptrs, rank: int, stream=None):
+        arr = self._ptr_array(flag_ptrs)
+        _check(_lib.s4_peer_signal(self.handle, arr, len(flag_ptrs), int(rank), _stream_handle(stream)))
 
     def peer_barrier(self, flag_ptrs, rank: int, epoch: int, stream=None):
         arr = self._ptr_array(flag_ptrs)

@@ -280,10 +280,11 @@ class FusedColshardStack:
     between projections orders the writes before the next projection reads them."""
 
     def __init__(self, ctx, group, rank: int, world: int, max_tokens: int = 2048, n_layers: int = N_LAYERS,
-                 fuse_silu: bool = True):
+                 fuse_silu: bool = True, split_barrier: bool = True):
         import torch
         import torch.distributed as dist
         self.ctx, self.group, self.rank, self.world = ctx, group, rank, world
+        self.split_barrier = split_barrier
         self.device = torch.device("cuda", ctx.device)
         # its forward runs the norms itself (replicated, after each gather)
         self.stack = CudaStack(ctx, n_layers, rank, world, self.device, fuse_silu=fuse_silu, fuse_norm=False)
@@ -319,6 +320,8 @@ class FusedColshardStack:
         """x: [M, 2048] fp16 embeddings, the same on every rank; returns the final-normed hidden
         states [M, 2048] fp16 (a view of this object's buffer, valid until the next call). The fp32
         residual stream and the norms are replicated; the projections are sharded."""
+        if self.world > 1 and self.split_barrier:
+            return self._forward_split(x)
         ctx, r, g = self.ctx, self.rank, self.world
         M = x.shape[0]
         assert M <= self.max_tokens
@@ -343,6 +346,46 @@ class FusedColshardStack:
             self.barrier()
             y = self._view("d", M, HIDDEN)
         ctx.add_rmsnorm(xs, y, h=h)                                     # final norm
+        return h
+
+    def _forward_split(self, x):
+        """The same forward with the barrier split: each gathered GEMM is followed by a signal to
+        every rank, and the next consumer of gathered data (GEMM or ADD_NORM) waits for all ranks'
+        signals itself, so the wait overlaps that kernel's start (its weight stream) instead of
+        taking a kernel of its own. Consumers of local data (the in_proj and gate|up GEMMs read h)
+        do not wait: the wait before them already covered every rank's reads of what they
+        overwrite."""
+        ctx, r, g = self.ctx, self.rank, self.world
+        M = x.shape[0]
+        assert M <= self.max_tokens
+        xs, h = self.x[:M], self.h[:M]
+        xs.copy_(x)
+        own, flags = self.local["flags"], self.ptrs["flags"]
+        wait = {"wait_flags": own, "nranks": g}
+        y = None
+        for w in self.stack.layers:
+            if y is None:
+                ctx.add_rmsnorm(xs, None, h=h)                          # in_norm of layer 0
+            else:
+                ctx.add_rmsnorm(xs, y, h=h, **wait)                     # in_norm (waits for down)
+            nin = w["in_proj"].N * g
+            ctx.matmul_gather(h.data_ptr(), HIDDEN, M, w["in_proj"], self.ptrs["a"], nin, r * w["in_proj"].N)
+            ctx.peer_signal(flags, r)
+            ctx.matmul_gather(self.local["a"], nin, M, w["out_proj"], self.ptrs["b"], HIDDEN, r * (HIDDEN // g),
+                              **wait)
+            ctx.peer_signal(flags, r)
+            ctx.add_rmsnorm(xs, self._view("b", M, HIDDEN), h=h, **wait)  # post_norm
+            if self.stack.fuse_silu:
+                ctx.matmul_gather(h.data_ptr(), HIDDEN, M, w["gate_up"], self.ptrs["mid"], INTER, r * (INTER // g))
+            else:
+                gu = ctx.matmul(h, w["gate_up"], M, self.gu[:M])
+                ctx.silu_mul_gather(gu, INTER // g, self.ptrs["mid"], INTER, r * (INTER // g))
+            ctx.peer_signal(flags, r)
+            ctx.matmul_gather(self.local["mid"], INTER, M, w["down"], self.ptrs["d"], HIDDEN, r * (HIDDEN // g),
+                              **wait)
+            ctx.peer_signal(flags, r)
+            y = self._view("d", M, HIDDEN)
+        ctx.add_rmsnorm(xs, y, h=h, **wait)                             # final norm
         return h
 
     def capture(self, x):

@@ -177,3 +177,36 @@ def test_fused_stack_one_gpu_eager_graph_and_plain_agree(ctx, serve):
         assert ctx.check_errors() == 0
     finally:
         fused.close()
+
+
+def test_split_barrier_consumers_on_one_rank(ctx):
+    """The split barrier's API on one GPU (nranks = 1): a signal, then the waiting GEMM and ADD_NORM
+    give exactly what their plain forms give, and no wait expires."""
+    rng = np.random.default_rng(21)
+    K, N, M = 2048, 2048, 200
+    packed, scales = s4ref.config_weights(rng, K, N)
+    W = ctx.upload(packed, scales, N, K)
+    flags = ctx.buffer_alloc(64)
+    try:
+        x = torch.from_numpy(s4ref.config_x(rng, M, K)).cuda()
+        y1 = torch.zeros((M, N), dtype=torch.float16, device="cuda")
+        y2 = torch.zeros_like(y1)
+        ctx.matmul_gather(x.data_ptr(), K, M, W, [y1.data_ptr()], N, 0)
+        for _ in range(3):  # several epochs in a row
+            ctx.peer_signal([flags], 0)
+            ctx.matmul_gather(x.data_ptr(), K, M, W, [y2.data_ptr()], N, 0, wait_flags=flags, nranks=1)
+        r = (torch.randn((M, N), device="cuda") * 0.5)
+        r1, r2 = r.clone(), r.clone()
+        h1 = ctx.add_rmsnorm(r1, y1)
+        ctx.peer_signal([flags], 0)
+        h2 = ctx.add_rmsnorm(r2, y2, wait_flags=flags, nranks=1)
+        torch.cuda.synchronize()
+        assert ctx.check_errors() == 0
+        assert torch.equal(y1, y2)
+        assert torch.equal(r1, r2) and torch.equal(h1, h2)
+        _, ref = s4ref.matmul(x.cpu().numpy(), packed, scales)
+        ok, mr, mc = s4ref.check(y2.cpu().numpy(), ref)
+        assert ok, (mr, mc)
+    finally:
+        W.free()
+        ctx.buffer_free(flags)

@@ -50,3 +50,36 @@ def test_peer_barrier_wait_expires_and_context_recovers(pkg):
         c.buffer_free(silent)
     finally:
         c.close()
+
+
+def test_norm_peer_wait_expires_and_context_recovers(pkg):
+    """The waiting half of the split barrier, run out: rank 0 of 2 signals (its own slot and the
+    absent rank's array get the epoch), then an ADD_NORM that waits for both ranks finds rank 1's slot
+    of its own array never written. Thread 0 gives up after one second, sets kErrWaitTimeout, and the
+    kernel finishes (it normalises what it has); the context then runs the same call correctly."""
+    c = pkg.Context(0)
+    try:
+        mine = c.buffer_alloc(64)
+        silent = c.buffer_alloc(64)
+        M, D = 64, 2048
+        x = (torch.randn((M, D), device="cuda") * 2).contiguous()
+        y = torch.randn((M, D), device="cuda").half()
+        c.peer_signal([mine, silent], 0)
+        t0 = time.time()
+        c.add_rmsnorm(x.clone(), y, wait_flags=mine, nranks=2)
+        err = c.check_errors()
+        dt = time.time() - t0
+        assert err & K_ERR_WAIT_TIMEOUT, f"expected the wait-timeout bit, got 0x{err:x}"
+        assert 0.5 < dt < 30.0, f"the bounded wait took {dt:.2f} s"
+        c.clear_errors()
+        x1 = x.clone()
+        h = c.add_rmsnorm(x1, y, wait_flags=mine, nranks=1)  # rank 0 alone: its own signal is there
+        torch.cuda.synchronize()
+        assert c.check_errors() == 0
+        xr, hr = s4ref.add_rmsnorm(x.cpu().numpy(), y.cpu().numpy())
+        np.testing.assert_array_equal(x1.cpu().numpy(), xr)
+        np.testing.assert_allclose(h.cpu().numpy().astype(np.float32), hr.astype(np.float32), rtol=1e-3, atol=1e-3)
+        c.buffer_free(mine)
+        c.buffer_free(silent)
+    finally:
+        c.close()
