@@ -36,13 +36,17 @@ constexpr int kTcMaxTn = 256;
 // Pipeline stages: stage s holds one k-tile's activations (TMA) and its dequantised weights (A). One
 // "full" barrier per stage completes when the activation bytes have landed AND all dequant warps have
 // arrived; one "empty" barrier per stage is signalled by a single tcgen05.commit once the stage's
-// MMAs are done. The MMA thread thus waits once and commits once per k-tile: its per-k-tile issue
-// time (measured ~750 cycles with separate activation / weight barriers and two commits, against 136
-// cycles of tensor work for a 64-token tile) bounds every shape of this kernel.
-constexpr int kTcStages = 3;
+// MMAs are done. The MMA thread thus waits once and commits once per k-tile (~370 cycles for four
+// MMAs and the commit). Single-thread roles share their sub-partition's issue slots with two busy
+// dequant warps and an epilogue warp, so their loops do their index math once per tile segment:
+// a runtime division or two per k-tile kept the weight producer at ~850 cycles per chunk, one chunk
+// ahead of the dequant warps, and paced the kernel (a per-role clock64 timeline showed it). With
+// that gone the activation loads' round trip through the stage ring is on the critical loop: four
+// stages, and six weight slots (the weight producer now runs a dozen chunks ahead).
+constexpr int kTcStages = 4;
 constexpr int kTcStagesX = kTcStages;  // activation tiles (TMA)
 constexpr int kTcStagesA = kTcStages;  // dequantised weight (MMA operand A)
-constexpr int kTcSlotsW = 12;
+constexpr int kTcSlotsW = 6;
 constexpr int kTcThreads = 512;
 constexpr int kTcDequantWarps = 8;  // warps 4..11
 // The dequant warps form kTcDqGroups groups that take alternate chunks (group g: chunks i with
@@ -319,23 +323,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
     if (lane == 0) {
       int issued = 0;
       bool ok = true;
-      for (int i = 0; i < n; ++i) {
-        const int slot = i % SW;
-        if (i >= SW && !mbar_wait(empty_w + slot, ((i / SW) - 1) & 1)) {
-          set_error(p.err, kErrWaitTimeout);
-          ok = false;
-          break;
+      // index math once per segment (a run of units of one tile): runtime divisions per unit cost
+      // this single thread issue slots it shares with the dequant warps
+      int slot = 0, round = 0;
+      for (int i = 0; i < n && ok;) {
+        const int u0 = wk.unit(i);
+        const int tile = u0 / KT;
+        const int seg_end = min(wk.range_end(i), (tile + 1) * KT);
+        const int64_t chunk0 = (int64_t)(tile % p.nblk) * KT + (u0 - tile * KT);
+        const uint8_t* srcq = p.wq + chunk0 * kChunkWBytes;
+        const uint8_t* srcs = p.ws + chunk0 * kChunkSBytes;
+        const uint8_t* srcb = kAsym ? p.wb + chunk0 * kChunkSBytes : nullptr;
+        for (int u = u0; u < seg_end; ++u, ++i) {
+          if (round > 0 && !mbar_wait(empty_w + slot, (round - 1) & 1)) {
+            set_error(p.err, kErrWaitTimeout);
+            ok = false;
+            break;
+          }
+          uint8_t* dst = wraw + slot * WB;
+          mbar_arrive_expect_tx(full_w + slot, WB);
+          bulk_g2s_plain(dst, srcq, kChunkWBytes, full_w + slot);
+          bulk_g2s_plain(dst + kChunkWBytes, srcs, kChunkSBytes, full_w + slot);
+          if (kAsym) {
+            bulk_g2s_plain(dst + kChunkWBytes + kChunkSBytes, srcb, kChunkSBytes, full_w + slot);
+            srcb += kChunkSBytes;
+          }
+          srcq += kChunkWBytes;
+          srcs += kChunkSBytes;
+          ++issued;
+          if (++slot == SW) {
+            slot = 0;
+            ++round;
+          }
         }
-        const int u = wk.unit(i);
-        const int tile = u / KT, kt = u - tile * KT;
-        const int nb = tile % p.nblk;
-        const int64_t chunk = (int64_t)nb * KT + kt;
-        uint8_t* dst = wraw + slot * WB;
-        mbar_arrive_expect_tx(full_w + slot, WB);
-        bulk_g2s_plain(dst, p.wq + chunk * kChunkWBytes, kChunkWBytes, full_w + slot);
-        bulk_g2s_plain(dst + kChunkWBytes, p.ws + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
-        if (kAsym) bulk_g2s_plain(dst + kChunkWBytes + kChunkSBytes, p.wb + chunk * kChunkSBytes, kChunkSBytes, full_w + slot);
-        ++issued;
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
@@ -355,19 +375,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcParams p
       int issued = 0;
       bool ok = true;
       const uint32_t xbytes = (uint32_t)p.tn * 128u;
-      for (int i = 0; i < n; ++i) {
-        const int s = i % kTcStagesX;
-        if (i >= kTcStagesX && !mbar_wait(empty + s, ((i / kTcStagesX) - 1) & 1)) {
-          set_error(p.err, kErrWaitTimeout);
-          ok = false;
-          break;
+      int s = 0, round = 0;
+      for (int i = 0; i < n && ok;) {
+        const int u0 = wk.unit(i);
+        const int tile = u0 / KT;
+        const int seg_end = min(wk.range_end(i), (tile + 1) * KT);
+        const int row0 = (tile / p.nblk) * p.tn;
+        int kcol = (u0 - tile * KT) * 64;
+        for (int u = u0; u < seg_end; ++u, ++i) {
+          if (round > 0 && !mbar_wait(empty + s, (round - 1) & 1)) {
+            set_error(p.err, kErrWaitTimeout);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + s, xbytes);
+          tma_load_2d(xs + s * kTcXStageBytes, &tmap_x, kcol, row0, full + s);
+          kcol += 64;
+          ++issued;
+          if (++s == kTcStagesX) {
+            s = 0;
+            ++round;
+          }
         }
-        const int u = wk.unit(i);
-        const int tile = u / KT, kt = u - tile * KT;
-        const int tb = tile / p.nblk;
-        mbar_arrive_expect_tx(full + s, xbytes);
-        tma_load_2d(xs + s * kTcXStageBytes, &tmap_x, kt * 64, tb * p.tn, full + s);
-        ++issued;
       }
       if (!ok) {
         const uint64_t deadline = globaltimer_ns() + kWaitTimeoutNs;
