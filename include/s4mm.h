@@ -102,6 +102,13 @@ S4_API int s4_weight_upload_wire(s4_ctx* ctx, const uint8_t* packed, const uint8
  * become plain int4 weights (exactly); asymmetric ones keep their biases and run through s4_matmul and
  * s4_matmul_noalloc (the chained launch rejects them with S4_ERR_UNSUPPORTED). */
 #define S4_UPLOAD_DEVICE 1u
+/* Symmetric 2-bit weights only: also keep the weight in a native 2-bit decode layout (2048 bytes per
+ * 128 x 64 chunk instead of 4096), which the decode GEMV (M <= 16, s4_matmul) streams instead of the
+ * int4 layout; the tcgen05 GEMM and chained runs keep reading the int4 layout, so the weight takes
+ * 1.44x the device memory. Results are identical (the same fp16 fragments enter the same MMAs). A
+ * single decode call is dominated by launch and first-byte latency, so it gains little time (measured
+ * within 3 % on B200); no counterpart in the reference, whose shaders read the 2-bit words in place. */
+#define S4_UPLOAD_DECODE_LAYOUT 2u
 S4_API int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, const void* bias, int N, int K,
                                    int bits, int group, uint32_t flags, s4_weight** out);
 

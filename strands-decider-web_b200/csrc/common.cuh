@@ -185,6 +185,30 @@ __device__ __forceinline__ void i4x8_to_h2x4_centered(uint32_t w, uint32_t (&h)[
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[3]) : "r"(t3), "r"(mul16), "r"(add72));
 }
 
+// Symmetric 2-bit: the four half2 (q - 2) pairs of 32-block blk of a word in the native 2-bit decode
+// layout (repack2_kernel in format.cu): h[j] = (value 2j, value 2j + 1) of the lane's 8 values, the
+// same fragment order i4x8_to_h2x4_centered gives for an int4 word. Each 2-bit field lands in the
+// mantissa of 1024 (times 1, 4, 16, 64) and one exact f16 subtract or fma removes the offset.
+__device__ __forceinline__ void i2x8_to_h2x4_centered(uint32_t u, int blk, uint32_t (&h)[4]) {
+  const uint32_t w = blk ? (u >> 8) : u;
+  const uint32_t kMagic = 0x64006400u;
+  const uint32_t sub1026 = 0x64026402u;  // half2(1026, 1026)
+  const uint32_t mul4 = 0x34003400u;     // half2(1/4, 1/4)
+  const uint32_t add258 = 0xdc08dc08u;   // half2(-258, -258)
+  const uint32_t mul16 = 0x2c002c00u;    // half2(1/16, 1/16)
+  const uint32_t add66 = 0xd420d420u;    // half2(-66, -66)
+  const uint32_t mul64 = 0x24002400u;    // half2(1/64, 1/64)
+  const uint32_t add18 = 0xcc80cc80u;    // half2(-18, -18)
+  const uint32_t t0 = lop3_and_or(w, 0x00030003u, kMagic);
+  const uint32_t t1 = lop3_and_or(w, 0x000c000cu, kMagic);
+  const uint32_t t2 = lop3_and_or(w, 0x00300030u, kMagic);
+  const uint32_t t3 = lop3_and_or(w, 0x00c000c0u, kMagic);
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(h[0]) : "r"(t0), "r"(sub1026));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[1]) : "r"(t1), "r"(mul4), "r"(add258));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[2]) : "r"(t2), "r"(mul16), "r"(add66));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[3]) : "r"(t3), "r"(mul64), "r"(add18));
+}
+
 // silu(g) * u in fp32 (wgsl.js:81-90); every kernel that produces SiLU*mul outputs uses this one.
 __device__ __forceinline__ float silu_mul_f32(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 

@@ -51,6 +51,51 @@ __global__ void transcode_kernel(const uint32_t* __restrict__ q, const __half* _
   }
 }
 
+// Native 2-bit decode layout (symmetric 2-bit weights): per (n-block, k-tile) chunk 2048 bytes =
+// [8 sub-tiles][32 lanes][2 u32]. Lane L = 4g + t of sub-tile s holds word h (row nb*128 + 16s + g + 8h)
+// for both 32-blocks of the k-tile: value i (K = kt*64 + 32*blk + 8t + i) of block blk sits at bits
+// 8*blk + 2*(i/2) for even i and 16 + 8*blk + 2*(i/2) for odd i, so one shift and a 0x00030003-style
+// mask put the pair (i, i + 1) in the two halves of a half2 (the GEMV's fragment order, as the int4
+// layout's nibble shuffle does). Rows >= N and blocks >= K/32 hold 2, the zero weight.
+__global__ void repack2_kernel(const uint32_t* __restrict__ q, int N, int blocks, int nblk, int ktiles,
+                               uint32_t* __restrict__ out) {
+  const int64_t words = (int64_t)nblk * ktiles * 512;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
+    const int h = (int)(i & 1);
+    const int lane = (int)((i >> 1) & 31);
+    const int sub = (int)((i >> 6) & 7);
+    const int64_t chunk = i >> 9;
+    const int kt = (int)(chunk % ktiles);
+    const int nb = (int)(chunk / ktiles);
+    const int g = lane >> 2, t = lane & 3;
+    const int r = nb * 128 + sub * 16 + g + 8 * h;
+    uint32_t o = 0;
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const int b = kt * 2 + blk;
+      const bool in = r < N && b < blocks;
+      const uint32_t w = in ? q[((int64_t)r * blocks + b) * 2 + (t >> 1)] : 0u;
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const int e = 8 * t + v;  // position in the 32-block
+        const uint32_t val = in ? (w >> (2 * (e & 15))) & 3u : 2u;
+        o |= val << ((v & 1) * 16 + 8 * blk + 2 * (v >> 1));
+      }
+    }
+    out[i] = o;
+  }
+}
+
+cudaError_t launch_repack2(const uint32_t* q, int N, int K, int nblk, int ktiles, uint8_t* out, int sm_count,
+                           cudaStream_t stream) {
+  const int64_t words = (int64_t)nblk * ktiles * 512;
+  int64_t want = (words + 255) / 256;
+  int grid = (int)(want < (int64_t)sm_count * 16 ? want : (int64_t)sm_count * 16);
+  if (grid < 1) grid = 1;
+  repack2_kernel<<<grid, 256, 0, stream>>>(q, N, K / 32, nblk, ktiles, reinterpret_cast<uint32_t*>(out));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_transcode(const uint32_t* q, const __half* scales, const __half* bias, int N, int K, int bits,
                              int group, uint8_t* packed4, __half* scales32, __half* bias32, int sm_count,
                              cudaStream_t stream) {

@@ -43,6 +43,8 @@ struct GemvParams {
   int xrow;           // padded activation row: 128 bytes per k-tile + 64
 };
 
+constexpr int kChunkW2Bytes = 2048;  // native 2-bit decode layout: bytes of one chunk (format.cu)
+
 constexpr int kGemvWarps = 8;                 // one per 16-row sub-tile of the n-block
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kGemvMaxGroups = 2;             // GEMV serves M <= 16
@@ -57,10 +59,10 @@ constexpr int kGemvMaxCopyGroups = kGemvMaxKtPerCta / kGemvGroup;
 struct GemvLayout {
   int s_off, b_off, x_off, red_off, bar_off, total, xrow;
 };
-static GemvLayout gemv_layout(int nkt, int MG, bool asym) {
+static GemvLayout gemv_layout(int nkt, int MG, bool asym, int wbytes = kChunkWBytes) {
   GemvLayout L;
   L.xrow = nkt * 128 + 64;
-  L.s_off = nkt * kChunkWBytes;
+  L.s_off = nkt * wbytes;
   L.b_off = L.s_off + nkt * kChunkSBytes;
   L.x_off = L.b_off + (asym ? nkt * kChunkSBytes : 0);
   L.red_off = L.x_off + 8 * MG * L.xrow;
@@ -85,8 +87,11 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-template <int MG, bool ASYM>
+// BITS: 4 (wq in the int4 layout) or 2 (wq in the native 2-bit decode layout; symmetric only)
+template <int MG, bool ASYM, int BITS>
 __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const GemvParams p) {
+  static_assert(BITS == 4 || (BITS == 2 && !ASYM), "2-bit decode layout: symmetric weights only");
+  constexpr int WBYTES = BITS == 2 ? kChunkW2Bytes : kChunkWBytes;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* wsm = smem;
   uint8_t* ssm = smem + p.s_off;
@@ -112,8 +117,8 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
     const int64_t chunk0 = (int64_t)nb * KT + kt0;
     for (int q = 0; q < ngroups; ++q) {
       const int t0 = q * kGemvGroup, nt = min(kGemvGroup, nkt - t0);
-      mbar_arrive_expect_tx(bars + q, (uint32_t)nt * (kChunkWBytes + (ASYM ? 2 : 1) * kChunkSBytes));
-      bulk_g2s(wsm + t0 * kChunkWBytes, p.wq + (chunk0 + t0) * kChunkWBytes, (uint32_t)nt * kChunkWBytes, bars + q, pol);
+      mbar_arrive_expect_tx(bars + q, (uint32_t)nt * (WBYTES + (ASYM ? 2 : 1) * kChunkSBytes));
+      bulk_g2s(wsm + t0 * WBYTES, p.wq + (chunk0 + t0) * WBYTES, (uint32_t)nt * WBYTES, bars + q, pol);
       bulk_g2s(ssm + t0 * kChunkSBytes, p.ws + (chunk0 + t0) * kChunkSBytes, (uint32_t)nt * kChunkSBytes, bars + q, pol);
       if (ASYM)
         bulk_g2s(bsm + t0 * kChunkSBytes, p.wb + (chunk0 + t0) * kChunkSBytes, (uint32_t)nt * kChunkSBytes, bars + q, pol);
@@ -147,7 +152,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
   const uint8_t* xr[MG];
 #pragma unroll
   for (int mg = 0; mg < MG; ++mg) xr[mg] = xs + min(mg * 8 + g, rows - 1) * p.xrow + 16 * t;
-  const uint8_t* wl = wsm + sub * 512 + lane * 16;
+  const uint8_t* wl = wsm + (BITS == 2 ? sub * 256 + lane * 8 : sub * 512 + lane * 16);
   const uint8_t* sl = ssm + sub * 64 + g * 8;
   float acc[MG][4];
 #pragma unroll
@@ -161,12 +166,19 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_cluster_kernel(const Gem
     for (int i = 0; i < kGemvGroup; ++i) {
       const int kk = q * kGemvGroup + i;
       if (kk < nkt) {
-        const uint4 w = *reinterpret_cast<const uint4*>(wl + kk * kChunkWBytes);
         const uint2 sc = *reinterpret_cast<const uint2*>(sl + kk * kChunkSBytes);
-        if constexpr (ASYM) {
+        if constexpr (BITS == 2) {
+          const uint2 w2 = *reinterpret_cast<const uint2*>(wl + kk * WBYTES);
+          const uint8_t* xj[MG];
+#pragma unroll
+          for (int mg = 0; mg < MG; ++mg) xj[mg] = xr[mg] + kk * 128;
+          gemv_tile_rows2<MG>(w2, sc, xj, acc);
+        } else if constexpr (ASYM) {
+          const uint4 w = *reinterpret_cast<const uint4*>(wl + kk * WBYTES);
           const uint2 bi = *reinterpret_cast<const uint2*>(sl + (p.b_off - p.s_off) + kk * kChunkSBytes);
           gemv_tile_asym<MG>(w, sc, bi, xl + kk * 128, xgroup, (kt0 + kk) * 64 + 32 < p.K, xok, acc);
         } else {
+          const uint4 w = *reinterpret_cast<const uint4*>(wl + kk * WBYTES);
           const uint8_t* xj[MG];
 #pragma unroll
           for (int mg = 0; mg < MG; ++mg) xj[mg] = xr[mg] + kk * 128;
@@ -255,14 +267,15 @@ static int gemv_pick_split(int nblk, int KT, int sm_count) {
   return s;
 }
 
-template <int MG, bool ASYM>
+template <int MG, bool ASYM, int BITS>
 static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t stream, bool pdl) {
+  constexpr int WBYTES = BITS == 2 ? kChunkW2Bytes : kChunkWBytes;
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  const GemvLayout L = gemv_layout((p.ktiles + p.split - 1) / p.split, MG, ASYM);
+  const GemvLayout L = gemv_layout((p.ktiles + p.split - 1) / p.split, MG, ASYM, WBYTES);
   p.s_off = L.s_off;
   p.b_off = L.b_off;
   p.x_off = L.x_off;
@@ -270,17 +283,21 @@ static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t strea
   p.bar_off = L.bar_off;
   p.xrow = L.xrow;
   if (!configured[dev]) {
-    const int max_smem = gemv_layout(kGemvMaxKtPerCta, kGemvMaxGroups, ASYM).total;
-    e = cudaFuncSetAttribute(gemv_cluster_kernel<MG, ASYM>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    // the 2-bit layout keeps the int4 layout's shared-memory footprint: with a smaller one the block
+    // scheduler packs three CTAs onto an SM where the int4 launch spreads them over more SMs, and the
+    // call ran 20-40 % slower for all its halved bytes
+    const int max_smem = gemv_layout(kGemvMaxKtPerCta, kGemvMaxGroups, ASYM, kChunkWBytes).total;
+    e = cudaFuncSetAttribute(gemv_cluster_kernel<MG, ASYM, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             max_smem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_cluster_kernel<MG, ASYM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      e = cudaFuncSetAttribute(gemv_cluster_kernel<MG, ASYM, BITS>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nblk * p.split, 1, 1);
   cfg.blockDim = dim3(kGemvThreads, 1, 1);
-  cfg.dynamicSmemBytes = L.total;
+  cfg.dynamicSmemBytes = gemv_layout((p.ktiles + p.split - 1) / p.split, MG, ASYM, kChunkWBytes).total;
   cfg.stream = stream;
   cudaLaunchAttribute attr[3];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -293,17 +310,17 @@ static cudaError_t launch_gemv_mg(GemvParams p, int sm_count, cudaStream_t strea
   attr[2].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicySpread;
   cfg.attrs = attr;
   cfg.numAttrs = 3;
-  return cudaLaunchKernelEx(&cfg, gemv_cluster_kernel<MG, ASYM>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_cluster_kernel<MG, ASYM, BITS>, p);
 }
 
 // k-splits per n-block for a single call: the fewest CTAs (each streaming the most weight bytes)
 // that still give at least half the SMs a CTA and fit in one wave with 10 % to spare (a cluster must
 // fit in one GPC). A sweep of the four decode shapes at M = 1, 8, 16 found these 14-36 % faster than
 // about two CTAs per SM (gemv_pick_split), e.g. attn qkv M = 1 at S = 4: 4.1 us instead of 6.5 us.
-static int gemv_pick_split_fit(int nblk, int KT, int sm_count, int MG, bool asym) {
+static int gemv_pick_split_fit(int nblk, int KT, int sm_count, int MG, bool asym, int wbytes) {
   const int min_s = (KT + kGemvMaxKtPerCta - 1) / kGemvMaxKtPerCta;
   for (int S = min_s < 1 ? 1 : min_s; S <= kGemvMaxSplit && S <= KT; ++S) {
-    const GemvLayout L = gemv_layout((KT + S - 1) / S, MG, asym);
+    const GemvLayout L = gemv_layout((KT + S - 1) / S, MG, asym, wbytes);
     int per_sm = (228 * 1024) / (L.total + 1024);  // 228 KB per SM, 1 KB reserved per CTA
     if (per_sm > 3) per_sm = 3;                     // __launch_bounds__ of the kernel
     const long long grid = (long long)nblk * S, cap = (long long)sm_count * per_sm;
@@ -312,11 +329,13 @@ static int gemv_pick_split_fit(int nblk, int KT, int sm_count, int MG, bool asym
   return gemv_pick_split(nblk, KT, sm_count);
 }
 
+// wq2: the weight's native 2-bit decode layout (symmetric 2-bit formats), streamed instead of wq
 cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
                         uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0, int groups, int split,
-                        int sm_count, cudaStream_t stream, bool pdl, int glu) {
+                        int sm_count, cudaStream_t stream, bool pdl, int glu, const uint8_t* wq2) {
+  const bool two = wq2 != nullptr && wb == nullptr && !glu;
   GemvParams p;
-  p.wq = wq;
+  p.wq = two ? wq2 : wq;
   p.ws = ws;
   p.wb = wb;
   p.glu = glu;
@@ -335,14 +354,18 @@ cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb,
     if (split > ktiles) split = ktiles;
     if (split > kGemvMaxSplit) split = kGemvMaxSplit;
   } else {
-    split = gemv_pick_split_fit(nblk, ktiles, sm_count, groups, wb != nullptr);
+    split = gemv_pick_split_fit(nblk, ktiles, sm_count, groups, wb != nullptr, kChunkWBytes);
   }
   p.split = split;
   if ((ktiles + p.split - 1) / p.split > kGemvMaxKtPerCta) return cudaErrorInvalidValue;  // K > 16384
   p.token0 = token0;
   switch (groups) {
-    case 1: return wb ? launch_gemv_mg<1, true>(p, sm_count, stream, pdl) : launch_gemv_mg<1, false>(p, sm_count, stream, pdl);
-    case 2: return wb ? launch_gemv_mg<2, true>(p, sm_count, stream, pdl) : launch_gemv_mg<2, false>(p, sm_count, stream, pdl);
+    case 1:
+      if (two) return launch_gemv_mg<1, false, 2>(p, sm_count, stream, pdl);
+      return wb ? launch_gemv_mg<1, true, 4>(p, sm_count, stream, pdl) : launch_gemv_mg<1, false, 4>(p, sm_count, stream, pdl);
+    case 2:
+      if (two) return launch_gemv_mg<2, false, 2>(p, sm_count, stream, pdl);
+      return wb ? launch_gemv_mg<2, true, 4>(p, sm_count, stream, pdl) : launch_gemv_mg<2, false, 4>(p, sm_count, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

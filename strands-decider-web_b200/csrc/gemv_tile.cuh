@@ -68,6 +68,37 @@ __device__ __forceinline__ void gemv_tile_rows(const uint4 w, const uint2 sc, co
   }
 }
 
+// The same tile from the native 2-bit decode layout: w = the lane's two words (rows g and g + 8, both
+// 32-blocks of the k-tile), converted to the same fragments as the int4 form, then the same math.
+template <int MG>
+__device__ __forceinline__ void gemv_tile_rows2(const uint2 w, const uint2 sc, const uint8_t* const (&xr)[MG],
+                                                float (&acc)[MG][4]) {
+  const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&sc.x));
+  const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&sc.y));
+  uint4 xv[MG][2];
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg)
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) xv[mg][blk] = *reinterpret_cast<const uint4*>(xr[mg] + blk * 64);
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    uint32_t ha[4], hb[4];
+    i2x8_to_h2x4_centered(w.x, blk, ha);
+    i2x8_to_h2x4_centered(w.y, blk, hb);
+    const float sg = blk ? s1.x : s0.x, sg8 = blk ? s1.y : s0.y;
+#pragma unroll
+    for (int mg = 0; mg < MG; ++mg) {
+      float d[4];
+      mma_16816_zero(d, ha[0], hb[0], ha[1], hb[1], xv[mg][blk].x, xv[mg][blk].y);
+      mma_16816(d, ha[2], hb[2], ha[3], hb[3], xv[mg][blk].z, xv[mg][blk].w);
+      acc[mg][0] = fmaf(sg, d[0], acc[mg][0]);
+      acc[mg][1] = fmaf(sg, d[1], acc[mg][1]);
+      acc[mg][2] = fmaf(sg8, d[2], acc[mg][2]);
+      acc[mg][3] = fmaf(sg8, d[3], acc[mg][3]);
+    }
+  }
+}
+
 // Asymmetric formats: the lane's weights dequantised to fp16 first, w = fma(q, scale, bias) per
 // element (the f16 form of kernels.js:36), then one mma per 16 K; no per-block scaling after it.
 // bi = biases in the order of sc.

@@ -72,5 +72,9 @@ struct s4_weight {
   uint8_t* wb = nullptr;  // asymmetric formats: per-32-block fp16 biases in the layout of ws
   int glu = 0;            // fused gate|up weight (rows permuted, see repack.cu): matmuls write SiLU*mul, N / 2 wide
   size_t wq_bytes = 0, ws_bytes = 0;
+  // symmetric 2-bit formats: the same weight in a 2-bit decode layout (2048 bytes per chunk, scales
+  // shared with ws) that the decode GEMV streams instead of wq; nullptr for every other weight
+  uint8_t* wq2 = nullptr;
+  size_t wq2_bytes = 0;
 };
 

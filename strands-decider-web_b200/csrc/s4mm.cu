@@ -25,7 +25,9 @@ cudaError_t launch_repack(const uint8_t* packed, const __half* scales, uint32_t*
                           int nblk, int ktiles, int sm_count, cudaStream_t stream, int glu_I);
 cudaError_t launch_gemv(const uint8_t* wq, const uint8_t* ws, const uint8_t* wb, const __half* x, __half* y,
                         uint32_t* err, int M, int N, int K, int nblk, int ktiles, int token0, int groups, int split,
-                        int sm_count, cudaStream_t stream, bool pdl, int glu);
+                        int sm_count, cudaStream_t stream, bool pdl, int glu, const uint8_t* wq2);
+cudaError_t launch_repack2(const uint32_t* q, int N, int K, int nblk, int ktiles, uint8_t* out, int sm_count,
+                           cudaStream_t stream);
 int gemv_max_split();
 int gemv_max_tokens();
 cudaError_t launch_silu_mul(const __half* big, __half* mid, int M, int I, int sm_count, cudaStream_t stream);
@@ -511,8 +513,10 @@ int s4_weight_upload_wire(s4_ctx* ctx, const uint8_t* packed, const uint8_t* wir
 int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, const void* bias, int N, int K, int bits,
                             int group, uint32_t flags, s4_weight** out) {
   if (!ctx || !q || !scales || !out) return fail(S4_ERR_INVALID, "NULL argument");
-  if (flags & ~S4_UPLOAD_DEVICE) return fail(S4_ERR_INVALID, "unknown flags 0x%x", flags);
+  if (flags & ~(S4_UPLOAD_DEVICE | S4_UPLOAD_DECODE_LAYOUT)) return fail(S4_ERR_INVALID, "unknown flags 0x%x", flags);
   if (bits < 2 || bits > 4) return fail(S4_ERR_INVALID, "bits must be 2, 3 or 4 (got %d)", bits);
+  if ((flags & S4_UPLOAD_DECODE_LAYOUT) && (bits != 2 || bias))
+    return fail(S4_ERR_UNSUPPORTED, "the native decode layout exists for symmetric 2-bit weights only");
   if (group != 32 && group != 64) return fail(S4_ERR_INVALID, "group must be 32 or 64 (got %d)", group);
   int rc = check_shape(N, K);
   if (rc) return rc;
@@ -560,6 +564,26 @@ int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, cons
     return cuda_fail(e, "format upload");
   }
   rc = upload_common(ctx, d, ds32, N, K, out, db32);
+  if (rc == S4_OK && (flags & S4_UPLOAD_DECODE_LAYOUT)) {
+    // symmetric 2-bit: also the native 2-bit decode layout, which the decode GEMV streams (2048 weight
+    // bytes per chunk instead of 4096); the int4 layout stays for the tcgen05 GEMM and chained runs
+    s4_weight* w = *out;
+    w->wq2_bytes = (size_t)w->nblk * w->ktiles * 2048;
+    e = cudaMalloc(&w->wq2, w->wq2_bytes);
+    if (e == cudaSuccess) {
+      e = s4::launch_repack2(static_cast<const uint32_t*>(dq), N, K, w->nblk, w->ktiles, w->wq2, ctx->sm_count,
+                             ctx->stream);
+      if (e == cudaSuccess) ++ctx->launches;
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(d);
+      s4_weight_free(w);
+      *out = nullptr;
+      return cuda_fail(e, "2-bit decode layout");
+    }
+  }
   cudaFree(d);
   return rc;
 }
@@ -613,6 +637,7 @@ int s4_weight_free(s4_weight* w) {
   cudaFree(w->wq);
   cudaFree(w->ws);
   cudaFree(w->wb);
+  cudaFree(w->wq2);
   delete w;
   return S4_OK;
 }
@@ -621,7 +646,7 @@ int s4_weight_info(const s4_weight* w, int* N, int* K, size_t* device_bytes) {
   if (!w) return fail(S4_ERR_INVALID, "NULL weight");
   if (N) *N = w->N;
   if (K) *K = w->K;
-  if (device_bytes) *device_bytes = w->wq_bytes + w->ws_bytes + (w->wb ? w->ws_bytes : 0);
+  if (device_bytes) *device_bytes = w->wq_bytes + w->ws_bytes + (w->wb ? w->ws_bytes : 0) + w->wq2_bytes;
   if (N && w->glu) *N = w->N / 2;  // a fused gate|up weight's matmul writes N / 2 columns
   return S4_OK;
 }
@@ -905,7 +930,8 @@ int s4_matmul(s4_ctx* ctx, const s4_weight* w, const void* x, int M, void* y, vo
     const int rem = M - tok0;
     const int groups = rem >= kGemvMaxM ? kGemvMaxM / 8 : (rem + 7) / 8;
     e = s4::launch_gemv(w->wq, w->ws, w->wb, static_cast<const __half*>(x), static_cast<__half*>(y), ctx->err, M, w->N,
-                        w->K, w->nblk, w->ktiles, tok0, groups, b.split, ctx->sm_count, st, ctx->pdl, w->glu);
+                        w->K, w->nblk, w->ktiles, tok0, groups, b.split, ctx->sm_count, st, ctx->pdl, w->glu,
+                        w->wq2);
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     ++ctx->launches;
   }

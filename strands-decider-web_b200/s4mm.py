@@ -29,6 +29,7 @@ FAMILY_AUTO, FAMILY_GEMV, FAMILY_TC = 0, 1, 2
 FAMILY_NAMES = {FAMILY_AUTO: "auto", FAMILY_GEMV: "gemv", FAMILY_TC: "tc"}
 ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_DEVICE, ERR_UNSUPPORTED, ERR_IO = 1, 2, 3, 4, 5, 6
 UPLOAD_DEVICE = 1  # s4_weight_upload_format: pointers are device memory
+UPLOAD_DECODE_LAYOUT = 2  # s4_weight_upload_format: symmetric 2-bit, also the native 2-bit decode layout
 
 # Every symbol include/s4mm.h declares, with its ctypes signature.
 _P = C.c_void_p
@@ -390,11 +391,14 @@ class Context:
         _check(_lib.s4_weight_upload_wire(self.handle, p.ctypes.data, w.ctypes.data, N, K, 0, C.byref(h)))
         return Weight(self, h.value, N, K)
 
-    def upload_format(self, q, scales, N: int, K: int, bits: int, group: int = 32, bias=None) -> Weight:
+    def upload_format(self, q, scales, N: int, K: int, bits: int, group: int = 32, bias=None,
+                      decode_layout: bool = False) -> Weight:
         """Upload a weight in one of the engine's formats (``{bits, group, asym}``): ``q`` u32
         [N][K/32][bits], ``scales`` fp16 [N][K/group], ``bias`` fp16 [N][K/group] or None. Host numpy
-        arrays, or CUDA tensors (all on the device). Synchronous."""
+        arrays, or CUDA tensors (all on the device). Synchronous. ``decode_layout`` (symmetric 2-bit
+        only): also keep the native 2-bit layout the decode GEMV streams (``S4_UPLOAD_DECODE_LAYOUT``)."""
         h = _P()
+        extra = UPLOAD_DECODE_LAYOUT if decode_layout else 0
         if hasattr(q, "is_cuda") and q.is_cuda:
             import torch
             ng = N * (K // group) if group else 0
@@ -404,7 +408,7 @@ class Context:
                 _dev_buf("bias", bias, self.device, ng * 2, torch.float16)
             _check(_lib.s4_weight_upload_format(self.handle, q.data_ptr(), scales.data_ptr(),
                                                 None if bias is None else bias.data_ptr(), N, K, bits, group,
-                                                UPLOAD_DEVICE, C.byref(h)))
+                                                UPLOAD_DEVICE | extra, C.byref(h)))
         else:
             qa = np.ascontiguousarray(np.asarray(q, dtype=np.uint32))
             sa = np.ascontiguousarray(np.asarray(scales, dtype=np.float16))
@@ -413,7 +417,7 @@ class Context:
                     (ba is not None and ba.size != sa.size):
                 raise S4Error(ERR_INVALID, f"q/scales/bias sizes do not match N={N} K={K} bits={bits} group={group}")
             _check(_lib.s4_weight_upload_format(self.handle, qa.ctypes.data, sa.ctypes.data,
-                                                None if ba is None else ba.ctypes.data, N, K, bits, group, 0,
+                                                None if ba is None else ba.ctypes.data, N, K, bits, group, extra,
                                                 C.byref(h)))
         return Weight(self, h.value, N, K)
 

@@ -173,3 +173,43 @@ def test_fwht_errors(ctx, pkg):
         with pytest.raises(pkg.S4Error):
             ctx.fwht(d, n)
     assert ctx.check_errors() == 0
+
+
+@pytest.mark.parametrize("group", [32, 64])
+@pytest.mark.parametrize("K,N", [(2048, 1536), (1024, 2200), (6144, 2048)])
+def test_two_bit_decode_layout_streams_half_the_bytes(ctx, K, N, group):
+    """A symmetric 2-bit weight uploaded with S4_UPLOAD_DECODE_LAYOUT also gets the native 2-bit decode
+    layout (2048 bytes per 128 x 64 chunk instead of 4096), which the decode GEMV streams: its outputs
+    match the oracle, and with the split forced equal they are bit-identical to the int4 layout's (the
+    same fp16 fragments enter the same MMAs). Ragged N (not a multiple of 128) included; the device
+    footprint counts both layouts; the flag is refused for other formats."""
+    rng = np.random.default_rng(K + N + group)
+    words, sc = _format_weight(rng, K, N, 2, group)
+    W = ctx.upload_format(words, sc, N, K, 2, group, decode_layout=True)
+    packed, s32 = s4ref.transcode_sym(words, sc, 2, group)
+    Wr = ctx.upload(packed, s32, N, K)
+    nblk, kt = -(-N // 128), -(-K // 64)
+    assert W.device_bytes == Wr.device_bytes + nblk * kt * 2048
+    deq = s4ref.dequant_format(words, sc, 2, group)
+    try:
+        for M in (1, 5, 8, 16):
+            x = torch.from_numpy(s4ref.config_x(rng, M, K)).cuda()
+            y = ctx.matmul(x, W)
+            torch.cuda.synchronize()
+            ok, mr, mc = s4ref.check(y.cpu().numpy(), x.cpu().numpy().astype(np.float32) @ deq.T)
+            assert ok, f"M={M}: max_rel={mr:.2e} min_cos={mc:.7f}"
+            for split in (2, 4):
+                ctx.force("gemv", 0, split)
+                try:
+                    a, b = ctx.matmul(x, W), ctx.matmul(x, Wr)
+                    torch.cuda.synchronize()
+                finally:
+                    ctx.force()
+                assert torch.equal(a, b), (M, split)
+        assert ctx.check_errors() == 0
+        w3, s3 = _format_weight(rng, K, 256, 3, group)
+        with pytest.raises(Exception):
+            ctx.upload_format(w3, s3, 256, K, 3, group, decode_layout=True)
+    finally:
+        W.free()
+        Wr.free()
