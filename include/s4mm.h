@@ -107,7 +107,8 @@ S4_API int s4_weight_upload_wire(s4_ctx* ctx, const uint8_t* packed, const uint8
  * int4 layout; the tcgen05 GEMM and chained runs keep reading the int4 layout, so the weight takes
  * 1.44x the device memory. Results are identical (the same fp16 fragments enter the same MMAs). A
  * single decode call is dominated by launch and first-byte latency, so it gains little time (measured
- * within 3 % on B200); no counterpart in the reference, whose shaders read the 2-bit words in place. */
+ * within 3 % on B200); no counterpart in the reference, whose shaders read the 2-bit words in place.
+ * s4_weight_save stores the int4 layout only: a weight loaded back decodes from it. */
 #define S4_UPLOAD_DECODE_LAYOUT 2u
 S4_API int s4_weight_upload_format(s4_ctx* ctx, const void* q, const void* scales, const void* bias, int N, int K,
                                    int bits, int group, uint32_t flags, s4_weight** out);
