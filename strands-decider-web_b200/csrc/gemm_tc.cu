@@ -15,8 +15,8 @@
 // number of MMAs and only those last tiles can be split. A run of units of one tile is a segment; a
 // segment that covers the whole K range is written as fp16 directly, otherwise its fp32 partial goes
 // to scratch and either a fix-up kernel launched right after sums the partials of each split tile in
-// CTA order, or the last CTA to arrive at the tile does it in this kernel (atomic ticket; the
-// dispatcher's choice, and always for the allocation-free entry point).
+// CTA order (the automatic choice, and the allocation-free entry point's), or the last CTA to arrive
+// at the tile does it in this kernel (atomic ticket; a dispatch-table choice).
 //
 // Warp roles (512 threads): warp 0 lane 0 streams raw int4 chunks (1-D bulk copies) into a
 // kTcSlotsW-slot ring; warp 2 lane 0 loads activation tiles by TMA into a kTcStagesX-stage ring; warp 1 owns TMEM
@@ -42,7 +42,7 @@ constexpr int kTcMaxTn = 256;
 // a runtime division or two per k-tile kept the weight producer at ~850 cycles per chunk, one chunk
 // ahead of the dequant warps, and paced the kernel (a per-role clock64 timeline showed it). With
 // that gone the activation loads' round trip through the stage ring is on the critical loop: four
-// stages, and six weight slots (the weight producer now runs a dozen chunks ahead).
+// stages, and six weight slots (the weight producer now keeps all six filled ahead of the dequant).
 constexpr int kTcStages = 4;
 constexpr int kTcStagesX = kTcStages;  // activation tiles (TMA)
 constexpr int kTcStagesA = kTcStages;  // dequantised weight (MMA operand A)
