@@ -176,13 +176,14 @@ def test_fwht_errors(ctx, pkg):
 
 
 @pytest.mark.parametrize("group", [32, 64])
-@pytest.mark.parametrize("K,N", [(2048, 1536), (1024, 2200), (6144, 2048)])
+@pytest.mark.parametrize("K,N", [(2048, 1536), (1024, 2200), (6144, 2048), (1088, 384)])
 def test_two_bit_decode_layout_streams_half_the_bytes(ctx, K, N, group):
     """A symmetric 2-bit weight uploaded with S4_UPLOAD_DECODE_LAYOUT also gets the native 2-bit decode
     layout (2048 bytes per 128 x 64 chunk instead of 4096), which the decode GEMV streams: its outputs
     match the oracle, and with the split forced equal they are bit-identical to the int4 layout's (the
-    same fp16 fragments enter the same MMAs). Ragged N (not a multiple of 128) included; the device
-    footprint counts both layouts; the flag is refused for other formats."""
+    same fp16 fragments enter the same MMAs). Ragged N (not a multiple of 128) and a K whose last
+    k-tile holds one 32-block (1088) included; the device footprint counts both layouts; the flag is
+    refused for other formats."""
     rng = np.random.default_rng(K + N + group)
     words, sc = _format_weight(rng, K, N, 2, group)
     W = ctx.upload_format(words, sc, N, K, 2, group, decode_layout=True)
