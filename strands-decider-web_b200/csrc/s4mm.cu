@@ -876,6 +876,16 @@ static void auto_shape(int M, const s4_weight* w, int sms, int* tn_out, int* gri
   // 7-22 % faster whole; at 65 tiles for 148 SMs splitting still won)
   const long long tiles = (long long)((M + tn - 1) / tn) * nb;
   if (tiles < grid && tiles * 5 >= (long long)grid * 3) grid = (int)tiles;
+  // more tiles than CTAs: whole waves of whole tiles when a CTA count of at least 85 % of the SMs
+  // divides the tile count (no split tile, no fix-up launch); measured against stream-K over every
+  // SM: gate|up M = 1024 / 2048 on 128 CTAs 16 / 7.5 % faster, the fused qkvz|ab projection on 130
+  // CTAs 26 / 12 % faster
+  if (tiles > grid && grid == sms)
+    for (long long g = sms; g * 100 >= (long long)sms * 85; --g)
+      if (tiles % g == 0) {
+        grid = (int)g;
+        break;
+      }
   *tn_out = tn;
   *grid_out = grid;
 }

@@ -52,7 +52,8 @@ def candidates(M: int, K: int, N: int, sms: int):
     """Buckets to try for one (shape, M): the GEMV family with its automatic split and a few fixed
     ones (M <= 16); the tcgen05 family with its automatic shape, all SMs in stream-K, whole tiles on
     fewer CTAs, and 128- / 256-token tiles above M = 256; split tiles summed by the fix-up kernel
-    or by their last CTA."""
+    or by their last CTA. With more tiles than SMs, also the largest CTA count of at least 85 % of the
+    SMs that divides the tile count (whole waves of whole tiles, no split at all)."""
     out = []
     if M <= 16:
         for s in (0, 2, 4, 8):
@@ -65,6 +66,11 @@ def candidates(M: int, K: int, N: int, sms: int):
         grids = {0, sms}
         if ntiles < sms:
             grids.add(ntiles)
+        else:
+            for g in range(sms, (sms * 85 + 99) // 100 - 1, -1):
+                if ntiles % g == 0:
+                    grids.add(g)
+                    break
         for g in sorted(grids):
             for fx in ("kernel", "cta"):
                 out.append({"family": "tc", "tile": t, "split": g, "fixup": fx})
