@@ -877,13 +877,14 @@ static void auto_shape(int M, const s4_weight* w, int sms, int* tn_out, int* gri
   const long long tiles = (long long)((M + tn - 1) / tn) * nb;
   if (tiles < grid && tiles * 5 >= (long long)grid * 3) grid = (int)tiles;
   // more tiles than CTAs: whole waves of whole tiles when a CTA count of at least 85 % of the SMs
-  // divides the tile count (no split tile, no fix-up launch); measured against stream-K over every
-  // SM: gate|up M = 1024 / 2048 on 128 CTAs 16 / 7.5 % faster, the fused qkvz|ab projection on 130
-  // CTAs 26 / 12 % faster
+  // divides the tile count (no split tile, no fix-up launch) and costs each CTA at most one tile more
+  // than stream-K over every SM would; measured against stream-K: gate|up M = 1024 / 2048 on 128
+  // CTAs 16 / 7.5 % faster, the fused qkvz|ab projection on 130 CTAs 26 / 12 % faster; at many waves
+  // (8192-token serving chunks) the idle SMs cost more than the split tiles
   if (tiles > grid && grid == sms)
     for (long long g = sms; g * 100 >= (long long)sms * 85; --g)
       if (tiles % g == 0) {
-        grid = (int)g;
+        if (tiles * (sms - g) <= g * (long long)sms) grid = (int)g;
         break;
       }
   *tn_out = tn;

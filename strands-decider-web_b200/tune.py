@@ -53,7 +53,8 @@ def candidates(M: int, K: int, N: int, sms: int):
     ones (M <= 16); the tcgen05 family with its automatic shape, all SMs in stream-K, whole tiles on
     fewer CTAs, and 128- / 256-token tiles above M = 256; split tiles summed by the fix-up kernel
     or by their last CTA. With more tiles than SMs, also the largest CTA count of at least 85 % of the
-    SMs that divides the tile count (whole waves of whole tiles, no split at all)."""
+    SMs that divides the tile count (whole waves of whole tiles, no split at all; the automatic shape
+    takes it when it costs each CTA at most one tile more than stream-K)."""
     out = []
     if M <= 16:
         for s in (0, 2, 4, 8):
