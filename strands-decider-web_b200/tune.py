@@ -52,7 +52,8 @@ def candidates(M: int, K: int, N: int, sms: int):
     """Buckets to try for one (shape, M): the GEMV family with its automatic split and a few fixed
     ones (M <= 16); the tcgen05 family with its automatic shape, all SMs in stream-K, whole tiles on
     fewer CTAs, and 128- / 256-token tiles above M = 256; split tiles summed by the fix-up kernel
-    or by their last CTA. With more tiles than SMs, also the largest CTA count of at least 85 % of the
+    or by their last CTA. With fewer tiles than SMs, every multiple of the tile count up to the SM
+    count (each tile cut into that many equal K ranges). With more tiles than SMs, the largest CTA count of at least 85 % of the
     SMs that divides the tile count (whole waves of whole tiles, no split at all; the automatic shape
     takes it when it costs each CTA at most one tile more than stream-K)."""
     out = []
@@ -66,7 +67,9 @@ def candidates(M: int, K: int, N: int, sms: int):
         ntiles = ((M + tn - 1) // tn) * nblk
         grids = {0, sms}
         if ntiles < sms:
-            grids.add(ntiles)
+            # one whole tile per CTA, or every tile cut into exactly k equal K ranges
+            for k in range(1, sms // ntiles + 1):
+                grids.add(k * ntiles)
         else:
             for g in range(sms, (sms * 85 + 99) // 100 - 1, -1):
                 if ntiles % g == 0:
